@@ -1,0 +1,105 @@
+/* ppdl_ops.h — operator-level C ABI of the B200 PP-DocLayoutV3 hot path.
+ *
+ * This is the drop-in replacement for the reference's tagged ggml custom-op
+ * hooks (caojiachen1/ppdoclayout-ggml, patches/ggml-ppdl.patch:612-930):
+ *
+ *   reference                                      here
+ *   bool ggml_cuda_compute_forward_ppdl(ctx, dst)  ppdl_op_launch(desc, stream)
+ *        (patch:612-817, ppdl-ops.cuh:925)
+ *   bool ggml_cuda_supports_ppdl_op(op)            ppdl_op_supported(desc)
+ *        (patch:908-917, ppdl-ops.cuh:926)
+ *
+ * A ggml tensor is described by ppdl_tensor (device pointer + ggml ne[4],
+ * contiguous) and a GGML_OP_CUSTOM node by ppdl_op_desc: the destination,
+ * up to four sources (ggml dst->src[0..3]) and the node's int32
+ * op_params[16], with op_params[12] = PPDL_MAGIC and op_params[13] = the op
+ * id, exactly as the reference's graph builder tags them
+ * (src/ppdoclayout.cpp:50-53).  op_params[14]/[15] carry the per-op
+ * parameters with the reference's encodings (listed per id below).  The
+ * ggml-side adapter that fills a ppdl_op_desc from a ggml_tensor is shown in
+ * INTEGRATION.md.
+ *
+ * Batching: the reference runs every op at batch 1.  Here the outermost ne
+ * dimension that the reference leaves at 1 may hold several independent
+ * pages (noted per op); all pages are processed in one launch.
+ *
+ * No function in this header allocates device memory; all run asynchronously
+ * on the given stream (a cudaStream_t, NULL = legacy default stream).
+ */
+#ifndef PPDL_OPS_H
+#define PPDL_OPS_H
+
+#include <stdint.h>
+
+#if defined(_WIN32)
+#  define PPDL_OPS_API __declspec(dllexport)
+#else
+#  define PPDL_OPS_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PPDL_MAGIC 0x5050444C /* "PPDL", op_params[12] (src/ppdoclayout.cpp:51) */
+
+/* Op ids, op_params[13] (patch:121-134). */
+#define PPDL_OP_MASKBOX    1  /* src0 mask logits ne(40000,nq[,B]) -> dst ne(4,nq[,B]) inverse-sigmoid cxcywh */
+#define PPDL_OP_MSDEF      2  /* src0 value ne(256,13125[,B]), src1 offsets ne(192,nq[,B]), src2 attn logits
+                                 ne(96,nq[,B]), src3 ref ne(4,nq[,B]) -> dst ne(256,nq[,B]).
+                                 op_params[14] = 1 selects the canonical form: src1 = sampling locations
+                                 in [0,1] (same index order), src2 = softmax-normalised weights, no src3. */
+#define PPDL_OP_CONV       3  /* K==1: src0 x ne(IW,IH,IC[,B]) CHW, src1 ".wr" ne(OC,IC,1), dst ne(IW,IH,OC[,B]);
+                                 op_params[14] = K | pad<<8, [15] = 0 (CHW store).  The legacy K==3
+                                 channel-last form ([15] = 1) is not provided (PPDL_ERR_UNSUPPORTED). */
+#define PPDL_OP_CONVDIRECT 4  /* src0 x ne(IW,IH,IC[,B]), src1 ".wr" ne(OC,IC,K*K), src2 bias ne(OC) -> dst
+                                 ne(OW,OH,OC[,B]); op_params[14] = K | S<<8 | PAD<<16 | ACT<<24,
+                                 (K,S,PAD) in {(3,1,1),(3,2,1),(2,1,0),(1,1,0)}, ACT 0/1/2 = none/ReLU/SiLU */
+#define PPDL_OP_BIASACT    5  /* dst = act(src0 + bias[plane]); src0/dst ne(W,H,C[,B]), src1 bias ne(C);
+                                 op_params[14] = ACT */
+#define PPDL_OP_COPY       6  /* contiguous f32 copy, n = nelements(dst) */
+#define PPDL_OP_WG_INPUT   7  /* Winograd F(2,3) stages: not provided (PPDL_ERR_UNSUPPORTED); */
+#define PPDL_OP_WG_OUTPUT  8  /*   F(4,3) below is the k3-s1-p1 path                            */
+#define PPDL_OP_WG_MADD    9
+#define PPDL_OP_WG4_INPUT  10 /* src0 padded x ne(IW_p,IH_p,IC[,B]) -> dst dt ne(T,IC,36[,B]);
+                                 op_params[14] = T, [15] = TH (tile rows), TW = T/TH */
+#define PPDL_OP_WG4_OUTPUT 11 /* src0 yt ne(T,OC,36[,B]), src1 bias ne(OC) -> dst ne(OW,OH,OC[,B]);
+                                 op_params[14] = ACT, [15] = TW */
+#define PPDL_OP_WG4_MADD   12 /* src0 dt ne(T,IC,36[,B]), src1 ".wg4" ne(OC,IC,36) -> dst yt ne(T,OC,36[,B]) */
+#define PPDL_OP_TOPK       13 /* src0 class logits ne(nc,ntok[,B]) -> dst i32 ne(nq[,B]): tokens with the
+                                 largest max-class logit, descending, ties to the lower index */
+
+/* Status codes of ppdl_op_launch. */
+#define PPDL_OK               0
+#define PPDL_ERR_UNSUPPORTED  1  /* not a PPDL op or a form this build does not provide
+                                    (the reference hook returns false) */
+#define PPDL_ERR_SHAPE        2  /* shape / parameter violation (the reference aborts via GGML_ASSERT) */
+#define PPDL_ERR_CUDA         3  /* the launch failed; cudaGetLastError() was consumed */
+
+typedef struct {
+    void *  data;   /* device pointer, f32 unless stated, contiguous */
+    int64_t ne[4];  /* ggml element counts, ne[0] fastest */
+} ppdl_tensor;
+
+typedef struct {
+    ppdl_tensor dst;
+    ppdl_tensor src[4];
+    int32_t     op_params[16];
+} ppdl_op_desc;
+
+/* Non-zero when desc is a tagged PPDL op that this build provides
+   (ggml_cuda_supports_ppdl_op, patch:908-917). */
+PPDL_OPS_API int ppdl_op_supported(const ppdl_op_desc * desc);
+
+/* Enqueue the op on stream (ggml_cuda_compute_forward_ppdl, patch:612-817).
+   Returns a PPDL_OK / PPDL_ERR_* status. */
+PPDL_OPS_API int ppdl_op_launch(const ppdl_op_desc * desc, void * stream);
+
+/* Human-readable text of the last error of ppdl_op_launch on this thread. */
+PPDL_OPS_API const char * ppdl_op_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PPDL_OPS_H */

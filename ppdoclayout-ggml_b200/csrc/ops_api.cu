@@ -1,0 +1,138 @@
+// ops_api.cu — the operator-level C ABI (include/ppdl_ops.h).
+//
+// Replaces the reference's ggml hook pair ggml_cuda_compute_forward_ppdl /
+// ggml_cuda_supports_ppdl_op (patches/ggml-ppdl.patch:612-817, 908-917): the
+// same op ids, the same op_params[14]/[15] encodings, the same tensor
+// layouts.  Where the reference aborts on a shape violation (GGML_ASSERT)
+// this layer returns PPDL_ERR_SHAPE with a message instead; where the
+// reference hook returns false (unknown id) this returns
+// PPDL_ERR_UNSUPPORTED.
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/ppdl_ops.h"
+#include "kernels.h"
+#include "ops_internal.h"
+
+namespace {
+
+thread_local char g_err[256] = "";
+
+int fail(int code, const char *fmt, long long a = 0, long long b = 0) {
+    snprintf(g_err, sizeof g_err, fmt, a, b);
+    return code;
+}
+
+long long nel(const ppdl_tensor &t) { return t.ne[0] * t.ne[1] * t.ne[2] * t.ne[3]; }
+
+int to_status(ppdl::Status s) {
+    switch (s) {
+        case ppdl::OK: return PPDL_OK;
+        case ppdl::ERR_UNSUPPORTED: return fail(PPDL_ERR_UNSUPPORTED, "unsupported op form");
+        case ppdl::ERR_SHAPE: return fail(PPDL_ERR_SHAPE, "shape, size or alignment violation");
+        default: {
+            snprintf(g_err, sizeof g_err, "CUDA launch failed");
+            return PPDL_ERR_CUDA;
+        }
+    }
+}
+
+bool provided(int id) {
+    switch (id) {
+        case PPDL_OP_MASKBOX: case PPDL_OP_MSDEF: case PPDL_OP_BIASACT: case PPDL_OP_COPY:
+        case PPDL_OP_TOPK:
+            return true;
+        default:
+            return ppdl::ops_ext_provided(id);
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+PPDL_OPS_API int ppdl_op_supported(const ppdl_op_desc *d) {
+    if (!d || (uint32_t)d->op_params[12] != PPDL_MAGIC) return 0;
+    const int id = d->op_params[13];
+    if (id == PPDL_OP_CONV && d->op_params[15] != 0) return 0;
+    return provided(id) ? 1 : 0;
+}
+
+PPDL_OPS_API const char *ppdl_op_last_error(void) { return g_err; }
+
+PPDL_OPS_API int ppdl_op_launch(const ppdl_op_desc *d, void *stream_ptr) {
+    g_err[0] = 0;
+    if (!d) return fail(PPDL_ERR_SHAPE, "null descriptor");
+    if ((uint32_t)d->op_params[12] != PPDL_MAGIC)
+        return fail(PPDL_ERR_UNSUPPORTED, "op_params[12] is not the PPDL magic");
+    cudaStream_t st = (cudaStream_t)stream_ptr;
+    const int32_t *p = d->op_params;
+    const ppdl_tensor &dst = d->dst;
+    const ppdl_tensor &s0 = d->src[0];
+    switch (p[13]) {
+        case PPDL_OP_MASKBOX: {
+            // patch:618-622: dst ne(4, nq), src0 ne(40000, nq)
+            if (dst.ne[0] != 4 || s0.ne[0] != ppdl::kMaskPix)
+                return fail(PPDL_ERR_SHAPE, "mask_box: dst ne0 %lld (want 4), src ne0 %lld (want 40000)",
+                            dst.ne[0], s0.ne[0]);
+            const long long rows = dst.ne[1] * dst.ne[2] * dst.ne[3];
+            if (s0.ne[1] * s0.ne[2] * s0.ne[3] != rows)
+                return fail(PPDL_ERR_SHAPE, "mask_box: %lld src rows vs %lld dst rows",
+                            s0.ne[1] * s0.ne[2] * s0.ne[3], rows);
+            return to_status(ppdl::launch_mask_box((const float *)s0.data, (float *)dst.data,
+                                                   (int)rows, st));
+        }
+        case PPDL_OP_MSDEF: {
+            // patch:623-631: dst ne(256, nq), value ne(256, 13125); pages in ne[2]
+            const bool canon = p[14] == 1;
+            const long long nq = dst.ne[1], B = dst.ne[2] * dst.ne[3];
+            if (dst.ne[0] != ppdl::kDM || s0.ne[0] != ppdl::kDM || s0.ne[1] != ppdl::kNTok)
+                return fail(PPDL_ERR_SHAPE, "msdeform: dst ne0 %lld / value ne(%lld, .) mismatch",
+                            dst.ne[0], s0.ne[0]);
+            if (s0.ne[2] * s0.ne[3] != B || nel(d->src[1]) != 192 * nq * B ||
+                nel(d->src[2]) != 96 * nq * B || (!canon && nel(d->src[3]) != 4 * nq * B))
+                return fail(PPDL_ERR_SHAPE, "msdeform: operand sizes disagree with nq=%lld B=%lld",
+                            nq, B);
+            return to_status(ppdl::launch_msda((const float *)s0.data, (const float *)d->src[1].data,
+                                               (const float *)d->src[2].data,
+                                               canon ? nullptr : (const float *)d->src[3].data,
+                                               (float *)dst.data, (int)nq, (int)B, canon, st));
+        }
+        case PPDL_OP_BIASACT: {
+            // patch:719-728: dst = act(src0 + bias[plane]), plane = ne0*ne1
+            const long long n = nel(dst);
+            if (nel(s0) != n) return fail(PPDL_ERR_SHAPE, "bias_act: %lld vs %lld elements", nel(s0), n);
+            if (nel(d->src[1]) != dst.ne[2])
+                return fail(PPDL_ERR_SHAPE, "bias_act: bias has %lld entries for %lld planes",
+                            nel(d->src[1]), dst.ne[2]);
+            if (p[14] < 0 || p[14] > 2) return fail(PPDL_ERR_SHAPE, "bias_act: act %lld", p[14]);
+            return to_status(ppdl::launch_bias_act((const float *)s0.data,
+                                                   (const float *)d->src[1].data, (float *)dst.data, n,
+                                                   dst.ne[0] * dst.ne[1], (int)dst.ne[2], p[14], st));
+        }
+        case PPDL_OP_COPY: {
+            const long long n = nel(dst);
+            if (nel(s0) < n) return fail(PPDL_ERR_SHAPE, "copy: src %lld < dst %lld", nel(s0), n);
+            return to_status(ppdl::launch_copy((const float *)s0.data, (float *)dst.data, n, st));
+        }
+        case PPDL_OP_TOPK: {
+            // patch:771-777: src0 ne(nc, ntok), dst i32 ne(nq); pages in ne[2] / ne[1]
+            const long long nc = s0.ne[0], ntok = s0.ne[1], B = s0.ne[2] * s0.ne[3];
+            const long long nq = dst.ne[0];
+            if (dst.ne[1] * dst.ne[2] * dst.ne[3] != B)
+                return fail(PPDL_ERR_SHAPE, "topk: %lld dst pages vs %lld src pages",
+                            dst.ne[1] * dst.ne[2] * dst.ne[3], B);
+            if (ntok > 16384 || nq > ntok)
+                return fail(PPDL_ERR_SHAPE, "topk: ntok %lld (max 16384), nq %lld", ntok, nq);
+            return to_status(ppdl::launch_topk((const float *)s0.data, (int32_t *)dst.data, (int)ntok,
+                                               (int)nc, (int)nq, (int)B, st));
+        }
+        default: {
+            int status = PPDL_ERR_UNSUPPORTED;
+            if (ppdl::ops_ext_launch(d, st, &status, g_err, sizeof g_err)) return status;
+            return fail(PPDL_ERR_UNSUPPORTED, "op id %lld is not provided by this build", p[13]);
+        }
+    }
+}
+
+}  // extern "C"

@@ -1,0 +1,88 @@
+// topk.cu — top-300 query selection (op 13).
+//
+// Reference: op_topk300 (src/ppdoclayout.cpp:73-96) and ppdl_topk_kernel
+// (patches/ggml-ppdl.patch:440-486): the nq tokens with the largest
+// max-over-classes logit, descending, ties to the lower token index.
+//
+// B200 design: one block per page.  Each token becomes a 64-bit key
+// (order-preserving bits of its max logit << 32 | ~index), so "descending
+// key" is exactly the reference order including the tie rule; -0.0 is
+// folded to +0.0 first because the reference compares values, under which
+// the two zeros tie.  The up-to-16384 keys are bitonic-sorted in 128 KB of
+// shared memory (one pass of 105 compare-exchange stages, no global
+// scratch) and the first nq indices are written out.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ppdl {
+
+namespace {
+
+constexpr int kThreads = 1024;
+constexpr int kMaxKeys = 16384;
+
+__global__ void __launch_bounds__(kThreads)
+topk_kernel(const float *__restrict__ lg, int32_t *__restrict__ out, int ntok, int nc, int nq,
+            int n2) {
+    extern __shared__ unsigned long long s_key[];
+    const float *lb = lg + (size_t)blockIdx.x * ntok * nc;
+    for (int q = threadIdx.x; q < n2; q += kThreads) {
+        unsigned long long key = 0ull;
+        if (q < ntok) {
+            const float *p = lb + (size_t)q * nc;
+            float m = p[0];
+            for (int c = 1; c < nc; c++) m = (m < p[c]) ? p[c] : m;  // std::max
+            if (m == 0.0f) m = 0.0f;                                 // -0 ties +0
+            unsigned u = __float_as_uint(m);
+            u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            key = ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)q);
+        }
+        s_key[q] = key;
+    }
+    __syncthreads();
+    // bitonic sort, descending
+    for (int k = 2; k <= n2; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n2; i += kThreads) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long a = s_key[i], b = s_key[ixj];
+                    const bool desc = (i & k) == 0;
+                    if (desc ? (a < b) : (a > b)) {
+                        s_key[i] = b;
+                        s_key[ixj] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int r = threadIdx.x; r < nq; r += kThreads)
+        out[(size_t)blockIdx.x * nq + r] =
+            (int32_t)(0xFFFFFFFFu - (unsigned)(s_key[r] & 0xFFFFFFFFull));
+}
+
+}  // namespace
+
+Status launch_topk(const float *lg, int32_t *out, int ntok, int nc, int nq, int batch,
+                   cudaStream_t stream) {
+    if (ntok <= 0 || nc <= 0 || nq <= 0 || batch <= 0) return ERR_SHAPE;
+    if (ntok > kMaxKeys || nq > ntok) return ERR_SHAPE;
+    int n2 = 1;
+    while (n2 < ntok) n2 <<= 1;
+    if (n2 < 2) n2 = 2;
+    const size_t smem = (size_t)n2 * sizeof(unsigned long long);
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kMaxKeys * (int)sizeof(unsigned long long)) != cudaSuccess)
+            return ERR_CUDA;
+        attr_set[dev] = true;
+    }
+    topk_kernel<<<batch, kThreads, smem, stream>>>(lg, out, ntok, nc, nq, n2);
+    return cuda_status();
+}
+
+}  // namespace ppdl
