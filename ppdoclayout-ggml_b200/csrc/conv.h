@@ -1,0 +1,46 @@
+// conv.h — launchers of conv.cu (Winograd transforms, depthwise, glue).
+//
+// Tensors are CHW per page; "xbs"/"ybs" are the page strides in floats, so a
+// view may be a channel slice of a wider (concatenated) buffer.
+#pragma once
+
+#include "common.cuh"
+
+namespace ppdl {
+
+// x [B][IC][H][W] -> dt [B*36][IC][T], tiles TW x TH of 4x4 outputs; `pad`
+// is the left/top zero padding (1 for a k3-s1-p1 conv on the unpadded
+// tensor, 0 for the reference's op 10 on an already padded tensor).
+Status launch_wg4_input(const float *x, long long xbs, float *dt, int IC, int H, int W, int TW,
+                        int TH, int pad, int B, cudaStream_t st);
+
+// yt [B*36][OC][T] -> y = act(A^T m A + bias (+res if res_mode==1)) (+res if
+// res_mode==2), y/res [B][OC][OH][OW] views.
+Status launch_wg4_output(const float *yt, const float *bias, float *y, long long ybs,
+                         const float *res, long long rbs, int res_mode, int OC, int OH, int OW,
+                         int TW, int TH, int act, int B, cudaStream_t st);
+
+// w [OC][IC][3][3] -> wg4 [36][IC][OC] (G g G^T with the reference's G)
+Status launch_wg4_filter(const float *w, float *wg4, int IC, int OC, cudaStream_t st);
+
+// depthwise KxK (K in {3,5}) conv + bias + act, symmetric padding P
+Status launch_dwconv(const float *x, long long xbs, const float *w, const float *bias, float *y,
+                     long long ybs, int C, int H, int W, int K, int S, int P, int act, int B,
+                     cudaStream_t st);
+
+// 2x2 stride-1 max pool of the input zero-padded by one row/column at the
+// end: out is H x W like the input
+Status launch_maxpool2_pad(const float *x, long long xbs, float *y, long long ybs, int C, int H,
+                           int W, int B, cudaStream_t st);
+
+// ggml_interpolate nearest / bilinear (no align-corners); y = base + interp
+// when base is non-null
+Status launch_interp(const float *x, long long xbs, float *y, long long ybs, const float *base,
+                     long long bbs, int C, int H, int W, int OH, int OW, bool bilinear, int B,
+                     cudaStream_t st);
+
+// y[c][r] = x[r][c] for an R x Cc matrix per page (row strides ldx, ldy)
+Status launch_transpose(const float *x, long long xbs, float *y, long long ybs, int R, int Cc,
+                        long long ldx, long long ldy, int B, cudaStream_t st);
+
+}  // namespace ppdl

@@ -1,0 +1,303 @@
+// dec.cu — row-wise and small kernels of the encoder/decoder and the GPU
+// postprocess.
+//
+// LayerNorm (ggml_norm eps 1e-5 * w + b, src/ppdoclayout.cpp:550-554),
+// softmax rows (ggml_soft_max, :580), the box-refinement update
+// sigmoid(delta + inverse_sigmoid(ref)) (:589-594, :849-850), the masked
+// memory (:798) and the top-k row gather (:808), plus the reference's host
+// postprocess (:927-993) moved to the device so only the final dets and
+// masks cross PCIe.
+#include "common.cuh"
+#include "dec.h"
+
+namespace ppdl {
+
+namespace {
+
+inline int blocks(long long n, int t = 256) { return (int)((n + t - 1) / t); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// one warp per 256-wide row; y = LN(x (+ r)) * g + b
+__global__ void layernorm256_kernel(const float *__restrict__ x, const float *__restrict__ r,
+                                    const float *__restrict__ g, const float *__restrict__ bta,
+                                    float *__restrict__ y, long long rows) {
+    const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int lane = threadIdx.x & 31;
+    const float4 *xp = reinterpret_cast<const float4 *>(x + row * 256);
+    float4 v[2];
+    v[0] = xp[lane];
+    v[1] = xp[lane + 32];
+    if (r) {
+        const float4 *rp = reinterpret_cast<const float4 *>(r + row * 256);
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const float4 q = rp[lane + 32 * k];
+            v[k].x = __fadd_rn(v[k].x, q.x); v[k].y = __fadd_rn(v[k].y, q.y);
+            v[k].z = __fadd_rn(v[k].z, q.z); v[k].w = __fadd_rn(v[k].w, q.w);
+        }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 2; k++) s += v[k].x + v[k].y + v[k].z + v[k].w;
+    const float mean = warp_sum(s) * (1.0f / 256.0f);
+    float s2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        v[k].x -= mean; v[k].y -= mean; v[k].z -= mean; v[k].w -= mean;
+        s2 += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+    }
+    const float var = warp_sum(s2) * (1.0f / 256.0f);
+    const float sc = 1.0f / sqrtf(var + 1e-5f);
+    const float4 *gp = reinterpret_cast<const float4 *>(g);
+    const float4 *bp = reinterpret_cast<const float4 *>(bta);
+    float4 *yp = reinterpret_cast<float4 *>(y + row * 256);
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        const float4 gg = gp[lane + 32 * k], bb = bp[lane + 32 * k];
+        float4 o;
+        o.x = v[k].x * sc * gg.x + bb.x; o.y = v[k].y * sc * gg.y + bb.y;
+        o.z = v[k].z * sc * gg.z + bb.z; o.w = v[k].w * sc * gg.w + bb.w;
+        yp[lane + 32 * k] = o;
+    }
+}
+
+// one warp per row of length L, in place
+__global__ void softmax_rows_kernel(float *__restrict__ x, long long rows, int L) {
+    const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int lane = threadIdx.x & 31;
+    float *p = x + row * L;
+    float m = -INFINITY;
+    for (int i = lane; i < L; i += 32) m = fmaxf(m, p[i]);
+    m = warp_max(m);
+    float s = 0.f;
+    for (int i = lane; i < L; i += 32) {
+        const float e = expf(p[i] - m);
+        p[i] = e;
+        s += e;
+    }
+    s = warp_sum(s);
+    const float inv = 1.0f / s;
+    for (int i = lane; i < L; i += 32) p[i] *= inv;
+}
+
+__global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b,
+                           float *__restrict__ y, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __fadd_rn(a[i], b[i]);
+}
+
+__global__ void sigmoid_kernel(const float *__restrict__ x, float *__restrict__ y, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x[i])));
+}
+
+// ref = sigmoid(delta + inverse_sigmoid(ref)), inverse_sigmoid per :589-594
+__global__ void refine_kernel(const float *__restrict__ delta, float *__restrict__ ref, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float x = fminf(fmaxf(ref[i], 0.0f), 1.0f);
+    const float x1 = fminf(fmaxf(x, 1e-5f), 1.0f);
+    const float x2 = fminf(fmaxf(__fsub_rn(1.0f, x), 1e-5f), 1.0f);
+    const float inv = __fsub_rn(logf(x1), logf(x2));
+    const float z = __fadd_rn(delta[i], inv);
+    ref[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+}
+
+// y[b][t][:] = x[b][t][:] * v[t]
+__global__ void row_scale_kernel(const float *__restrict__ x, const float *__restrict__ v,
+                                 float *__restrict__ y, long long rows_per_page, int D, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const long long t = (i / D) % rows_per_page;
+    y[i] = __fmul_rn(x[i], v[t]);
+}
+
+// y[b][i][:] = x[b][idx[b][i]][:]
+__global__ void gather_rows_kernel(const float *__restrict__ x, const int32_t *__restrict__ idx,
+                                   float *__restrict__ y, int rows_in, int rows_out, int D, int B) {
+    const long long n = (long long)B * rows_out * D;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int d = (int)(i % D);
+    const long long r = i / D;
+    const int b = (int)(r / rows_out);
+    const int src = idx[r];
+    y[i] = x[((long long)b * rows_in + src) * D + d];
+}
+
+// ---- postprocess ---------------------------------------------------------------
+// votes[j] = sum_{i != j} sigmoid(order[j + 300 i] - order[i + 300 j]) in i
+// order; rank = position in the stable ascending sort of the votes
+__global__ void pp_votes_rank_kernel(const float *__restrict__ order, int32_t *__restrict__ rank) {
+    __shared__ float s_votes[kNQ];
+    const int b = blockIdx.x;
+    const float *o = order + (long long)b * kNQ * kNQ;
+    for (int j = threadIdx.x; j < kNQ; j += blockDim.x) {
+        float acc = 0.0f;
+        for (int i = 0; i < kNQ; i++) {
+            if (i == j) continue;
+            const float diff = __fsub_rn(o[j + kNQ * i], o[i + kNQ * j]);
+            acc = __fadd_rn(acc, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-diff))));
+        }
+        s_votes[j] = acc;
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < kNQ; j += blockDim.x) {
+        const float vj = s_votes[j];
+        int r = 0;
+        for (int k = 0; k < kNQ; k++) {
+            const float vk = s_votes[k];
+            r += (vk < vj) || (vk == vj && k < j);
+        }
+        rank[b * kNQ + j] = r;
+    }
+}
+
+// top-300 of the 7500 sigmoid scores (ties to the lower flat index) and the
+// detections rows; one block per page, bitonic sort of 8192 keys
+__global__ void __launch_bounds__(1024)
+pp_select_kernel(const float *__restrict__ logits, const float *__restrict__ boxes,
+                 const int32_t *__restrict__ rank, const int32_t *__restrict__ ori_hw,
+                 float *__restrict__ dets, int32_t *__restrict__ sel) {
+    constexpr int N = kNQ * kNC, N2 = 8192;
+    extern __shared__ unsigned long long s_key[];  // N2 keys (64 KB, dynamic)
+    const int b = blockIdx.x;
+    const float *lg = logits + (long long)b * N;
+    for (int i = threadIdx.x; i < N2; i += blockDim.x) {
+        unsigned long long key = 0ull;
+        if (i < N) {
+            float sc = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-lg[i])));
+            if (sc == 0.0f) sc = 0.0f;
+            unsigned u = __float_as_uint(sc);
+            u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            key = ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)i);
+        }
+        s_key[i] = key;
+    }
+    __syncthreads();
+    for (int k = 2; k <= N2; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < N2; i += blockDim.x) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long a = s_key[i], c = s_key[ixj];
+                    if (((i & k) == 0) ? (a < c) : (a > c)) {
+                        s_key[i] = c;
+                        s_key[ixj] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    const float sf_h = __fdiv_rn((float)kImg, (float)ori_hw[2 * b]);
+    const float sf_w = __fdiv_rn((float)kImg, (float)ori_hw[2 * b + 1]);
+    const float oh = floorf(__fadd_rn(__fdiv_rn((float)kImg, sf_h), 0.5f));
+    const float ow = floorf(__fadd_rn(__fdiv_rn((float)kImg, sf_w), 0.5f));
+    for (int r = threadIdx.x; r < kNQ; r += blockDim.x) {
+        const int flat = (int)(0xFFFFFFFFu - (unsigned)(s_key[r] & 0xFFFFFFFFull));
+        const int q = flat / kNC, c = flat - q * kNC;
+        const float *bx = boxes + ((long long)b * kNQ + q) * 4;
+        float *o = dets + ((long long)b * kNQ + r) * 7;
+        o[0] = (float)c;
+        o[1] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-lg[flat])));
+        o[2] = __fmul_rn(__fsub_rn(bx[0], __fmul_rn(bx[2], 0.5f)), ow);
+        o[3] = __fmul_rn(__fsub_rn(bx[1], __fmul_rn(bx[3], 0.5f)), oh);
+        o[4] = __fmul_rn(__fadd_rn(bx[0], __fmul_rn(bx[2], 0.5f)), ow);
+        o[5] = __fmul_rn(__fadd_rn(bx[1], __fmul_rn(bx[3], 0.5f)), oh);
+        o[6] = (float)rank[b * kNQ + q];
+        sel[b * kNQ + r] = flat;
+    }
+}
+
+// masks[b][r][p] = mask_logits[b][sel/25][p] > 0
+__global__ void pp_masks_kernel(const float *__restrict__ ml, const int32_t *__restrict__ sel,
+                                int32_t *__restrict__ out) {
+    const int r = blockIdx.y, b = blockIdx.z;
+    const int q = sel[b * kNQ + r] / kNC;
+    const float4 *src = reinterpret_cast<const float4 *>(ml + ((long long)b * kNQ + q) * kMaskPix);
+    int4 *dst = reinterpret_cast<int4 *>(out + ((long long)b * kNQ + r) * kMaskPix);
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= kMaskPix / 4) return;
+    const float4 v = __ldg(src + i);
+    dst[i] = make_int4(v.x > 0.0f, v.y > 0.0f, v.z > 0.0f, v.w > 0.0f);
+}
+
+}  // namespace
+
+Status launch_layernorm256(const float *x, const float *r, const float *g, const float *b,
+                           float *y, long long rows, cudaStream_t st) {
+    if (rows <= 0) return rows == 0 ? OK : ERR_SHAPE;
+    layernorm256_kernel<<<blocks(rows * 32), 256, 0, st>>>(x, r, g, b, y, rows);
+    return cuda_status();
+}
+
+Status launch_softmax_rows(float *x, long long rows, int L, cudaStream_t st) {
+    softmax_rows_kernel<<<blocks(rows * 32), 256, 0, st>>>(x, rows, L);
+    return cuda_status();
+}
+
+Status launch_add(const float *a, const float *b, float *y, long long n, cudaStream_t st) {
+    add_kernel<<<blocks(n), 256, 0, st>>>(a, b, y, n);
+    return cuda_status();
+}
+
+Status launch_sigmoid(const float *x, float *y, long long n, cudaStream_t st) {
+    sigmoid_kernel<<<blocks(n), 256, 0, st>>>(x, y, n);
+    return cuda_status();
+}
+
+Status launch_refine(const float *delta, float *ref, long long n, cudaStream_t st) {
+    refine_kernel<<<blocks(n), 256, 0, st>>>(delta, ref, n);
+    return cuda_status();
+}
+
+Status launch_row_scale(const float *x, const float *v, float *y, long long rows_per_page, int D,
+                        int B, cudaStream_t st) {
+    const long long n = (long long)B * rows_per_page * D;
+    row_scale_kernel<<<blocks(n), 256, 0, st>>>(x, v, y, rows_per_page, D, n);
+    return cuda_status();
+}
+
+Status launch_gather_rows(const float *x, const int32_t *idx, float *y, int rows_in, int rows_out,
+                          int D, int B, cudaStream_t st) {
+    const long long n = (long long)B * rows_out * D;
+    gather_rows_kernel<<<blocks(n), 256, 0, st>>>(x, idx, y, rows_in, rows_out, D, B);
+    return cuda_status();
+}
+
+Status launch_postprocess(const float *logits, const float *boxes, const float *order,
+                          const float *mask_logits, const int32_t *ori_hw, int32_t *rank,
+                          float *dets, int32_t *sel, int32_t *masks, int B, cudaStream_t st) {
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int smem = 8192 * (int)sizeof(unsigned long long);
+    if (dev < 64 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(pp_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem) != cudaSuccess)
+            return ERR_CUDA;
+        attr_set[dev] = true;
+    }
+    pp_votes_rank_kernel<<<B, 320, 0, st>>>(order, rank);
+    pp_select_kernel<<<B, 1024, smem, st>>>(logits, boxes, rank, ori_hw, dets, sel);
+    if (masks) {
+        dim3 grid((unsigned)cdiv(kMaskPix / 4, 256), kNQ, (unsigned)B);
+        pp_masks_kernel<<<grid, 256, 0, st>>>(mask_logits, sel, masks);
+    }
+    return cuda_status();
+}
+
+}  // namespace ppdl

@@ -1,0 +1,31 @@
+// dec.h — launchers of dec.cu (row-wise decoder kernels, GPU postprocess).
+#pragma once
+
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace ppdl {
+
+// y = LayerNorm(x (+ r)) * g + b over rows of 256 (eps 1e-5)
+Status launch_layernorm256(const float *x, const float *r, const float *g, const float *b,
+                           float *y, long long rows, cudaStream_t st);
+// softmax over rows of length L, in place
+Status launch_softmax_rows(float *x, long long rows, int L, cudaStream_t st);
+Status launch_add(const float *a, const float *b, float *y, long long n, cudaStream_t st);
+Status launch_sigmoid(const float *x, float *y, long long n, cudaStream_t st);
+// ref = sigmoid(delta + inverse_sigmoid(ref))
+Status launch_refine(const float *delta, float *ref, long long n, cudaStream_t st);
+// y[b][t][:] = x[b][t][:] * v[t]
+Status launch_row_scale(const float *x, const float *v, float *y, long long rows_per_page, int D,
+                        int B, cudaStream_t st);
+// y[b][i][:] = x[b][idx[b][i]][:]
+Status launch_gather_rows(const float *x, const int32_t *idx, float *y, int rows_in, int rows_out,
+                          int D, int B, cudaStream_t st);
+// reading-order ranks, top-300 selection, dets rows and (if masks is
+// non-null) the thresholded, reordered int32 masks of B pages
+Status launch_postprocess(const float *logits, const float *boxes, const float *order,
+                          const float *mask_logits, const int32_t *ori_hw, int32_t *rank,
+                          float *dets, int32_t *sel, int32_t *masks, int B, cudaStream_t st);
+
+}  // namespace ppdl

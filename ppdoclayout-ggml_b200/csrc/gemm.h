@@ -19,8 +19,19 @@ struct Operand {
     long long div = 1, bs_hi = 0, bs_lo = 0;
 };
 
+// Implicit-GEMM convolution: when K > 0 the B operand is not a matrix but
+// the CHW input of page z (B.p + off(z)) read through the conv geometry,
+// B(k, n) = x[ic][oy*S + kh - P][ox*S + kw - P] (zero outside H x W) with
+// k = (ic*K + kh)*K + kw and n = oy*OW + ox — no im2col is materialised.
+// tap_major = 1 orders k as (kh*K + kw)*IC + ic instead, the row order of
+// the reference's repacked ".wr" weights (src/ppdoclayout.cpp:273-280).
+struct ConvGeom {
+    int K = 0, S = 1, P = 0, H = 0, W = 0, OW = 0, IC = 0, tap_major = 0;
+};
+
 struct GemmArgs {
     int M = 0, N = 0, K = 0, batch = 1;
+    ConvGeom conv;
     Operand A;        // (m, k): s0 = stride of m, s1 = stride of k
     Operand B;        // (k, n): s0 = stride of k, s1 = stride of n
     float *C = nullptr;

@@ -20,7 +20,7 @@ namespace {
 
 constexpr int kThreads = 256;
 
-template <int BM, int BN, int BK, bool kAK, bool kBN>
+template <int BM, int BN, int BK, bool kAK, bool kBN, bool kConv>
 __global__ void __launch_bounds__(kThreads)
 gemm_simt_kernel(const GemmArgs g) {
     constexpr int TM = BM / 16, TN = BN / 16;
@@ -52,7 +52,25 @@ gemm_simt_kernel(const GemmArgs g) {
             int kk, nn;
             if (kBN) { kk = e / BN; nn = e % BN; } else { nn = e / BK; kk = e % BK; }
             const int n = n0 + nn, k = k0 + kk;
-            rb[i] = (n < N && k < K) ? __ldg(B + (long long)k * g.B.s0 + (long long)n * g.B.s1) : 0.0f;
+            if (kConv) {
+                float v = 0.0f;
+                if (n < N && k < K) {
+                    const int KK = g.conv.K * g.conv.K;
+                    int ic, r;
+                    if (g.conv.tap_major) { r = k / g.conv.IC; ic = k - r * g.conv.IC; }
+                    else { ic = k / KK; r = k - ic * KK; }
+                    const int kh = r / g.conv.K, kw = r - kh * g.conv.K;
+                    const int oy = n / g.conv.OW, ox = n - oy * g.conv.OW;
+                    const int iy = oy * g.conv.S + kh - g.conv.P;
+                    const int ix = ox * g.conv.S + kw - g.conv.P;
+                    if (iy >= 0 && iy < g.conv.H && ix >= 0 && ix < g.conv.W)
+                        v = __ldg(B + ((long long)ic * g.conv.H + iy) * g.conv.W + ix);
+                }
+                rb[i] = v;
+            } else {
+                rb[i] = (n < N && k < K) ? __ldg(B + (long long)k * g.B.s0 + (long long)n * g.B.s1)
+                                         : 0.0f;
+            }
         }
     };
     auto store = [&](int buf) {
@@ -153,10 +171,18 @@ Status dispatch(const GemmArgs &g, cudaStream_t stream) {
     const bool ak = g.A.s1 == 1;  // k contiguous
     const bool bn = g.B.s1 == 1;  // n contiguous
     dim3 grid((unsigned)cdiv(g.N, BN), (unsigned)cdiv(g.M, BM), (unsigned)g.batch);
-    if (ak && bn) gemm_simt_kernel<BM, BN, BK, true, true><<<grid, kThreads, 0, stream>>>(g);
-    else if (ak) gemm_simt_kernel<BM, BN, BK, true, false><<<grid, kThreads, 0, stream>>>(g);
-    else if (bn) gemm_simt_kernel<BM, BN, BK, false, true><<<grid, kThreads, 0, stream>>>(g);
-    else gemm_simt_kernel<BM, BN, BK, false, false><<<grid, kThreads, 0, stream>>>(g);
+    if (g.conv.K > 0) {
+        if (ak) gemm_simt_kernel<BM, BN, BK, true, true, true><<<grid, kThreads, 0, stream>>>(g);
+        else gemm_simt_kernel<BM, BN, BK, false, true, true><<<grid, kThreads, 0, stream>>>(g);
+    } else if (ak && bn) {
+        gemm_simt_kernel<BM, BN, BK, true, true, false><<<grid, kThreads, 0, stream>>>(g);
+    } else if (ak) {
+        gemm_simt_kernel<BM, BN, BK, true, false, false><<<grid, kThreads, 0, stream>>>(g);
+    } else if (bn) {
+        gemm_simt_kernel<BM, BN, BK, false, true, false><<<grid, kThreads, 0, stream>>>(g);
+    } else {
+        gemm_simt_kernel<BM, BN, BK, false, false, false><<<grid, kThreads, 0, stream>>>(g);
+    }
     return cuda_status();
 }
 
@@ -167,7 +193,8 @@ Status launch_gemm_simt(const GemmArgs &g, cudaStream_t stream) {
     if (g.M == 0 || g.N == 0 || g.batch == 0) return OK;
     if (g.batch > 65535) return ERR_SHAPE;
     if (g.A.s0 != 1 && g.A.s1 != 1) return ERR_SHAPE;
-    if (g.B.s0 != 1 && g.B.s1 != 1) return ERR_SHAPE;
+    if (g.conv.K == 0 && g.B.s0 != 1 && g.B.s1 != 1) return ERR_SHAPE;
+    if (g.conv.K > 0 && (g.conv.OW <= 0 || (long long)g.N % g.conv.OW != 0)) return ERR_SHAPE;
     if (g.bias_mode && !g.bias) return ERR_SHAPE;
     if (g.res_mode && !g.res.p) return ERR_SHAPE;
     if (g.M <= 32) return dispatch<32, 128, 8>(g, stream);

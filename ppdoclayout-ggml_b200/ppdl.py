@@ -123,6 +123,120 @@ def op_supported(op_id, params=()) -> bool:
     return bool(lib().ppdl_op_supported(C.byref(d)))
 
 
+STEP_KINDS = {0: "other", 1: "gemm_1x1", 2: "wg_madd", 3: "gemm_implicit", 4: "gemm_linear",
+              5: "wg_input", 6: "wg_output", 7: "dwconv", 8: "msda", 9: "mask_box", 10: "topk",
+              11: "postprocess", 12: "glue"}
+
+
+class StepStat(C.Structure):
+    _fields_ = [("name", C.c_char * 48), ("kind", C.c_int32), ("ms", C.c_float),
+                ("flops", C.c_double), ("bytes", C.c_double)]
+
+
+class Context:
+    """One loaded model on one GPU (ppdl_ctx).  Mirrors the reference usage
+    ppdl_init -> ppdl_infer (-> ppdl_dump_raw) -> ppdl_free."""
+
+    def __init__(self, model_path: str, device: int = -1, max_batch: int = 1,
+                 dumps: bool = False, backend: int = BACKEND_CUDA):
+        L = lib()
+        L.ppdl_init_dev.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.ppdl_init_dev.restype = C.c_void_p
+        L.ppdl_infer_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                       C.POINTER(Result)]
+        L.ppdl_infer_batch.restype = C.c_int
+        L.ppdl_infer_device.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+        L.ppdl_infer_device.restype = C.c_int
+        L.ppdl_device_outputs.argtypes = [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]
+        L.ppdl_device_outputs.restype = C.c_int
+        L.ppdl_sync.argtypes = [C.c_void_p]
+        L.ppdl_sync.restype = C.c_int
+        self.lib = L
+        self.max_batch = max_batch
+        self.ctx = L.ppdl_init_dev(model_path.encode(), backend, device, max_batch, int(dumps))
+        if not self.ctx:
+            raise RuntimeError(f"ppdl_init failed for {model_path}")
+
+    def infer(self, image, ori_h: int = IMG_SIZE, ori_w: int = IMG_SIZE):
+        """One page (float32 [3,800,800]) -> (dets [300,7], masks [300,200,200])."""
+        import numpy as np
+        img = np.ascontiguousarray(image, dtype=np.float32)
+        res = Result()
+        rc = self.lib.ppdl_infer(self.ctx, img.ctypes.data, int(ori_h), int(ori_w), C.byref(res))
+        if rc != 0:
+            raise RuntimeError(f"ppdl_infer returned {rc}")
+        dets = np.ctypeslib.as_array(res.dets, (NUM_DETS, DET_FIELDS)).copy()
+        masks = np.ctypeslib.as_array(res.masks, (NUM_DETS, MASK_HW, MASK_HW)).copy()
+        return dets, masks, res.infer_ms
+
+    def infer_batch(self, images, ori_hw):
+        """n pages [n,3,800,800] -> list of (dets, masks) (copies)."""
+        import numpy as np
+        imgs = np.ascontiguousarray(images, dtype=np.float32)
+        hw = np.ascontiguousarray(ori_hw, dtype=np.int32).reshape(-1, 2)
+        n = imgs.shape[0]
+        res = (Result * n)()
+        rc = self.lib.ppdl_infer_batch(self.ctx, imgs.ctypes.data, n, hw.ctypes.data, res)
+        if rc != 0:
+            raise RuntimeError(f"ppdl_infer_batch returned {rc}")
+        out = []
+        for r in res:
+            out.append((np.ctypeslib.as_array(r.dets, (NUM_DETS, DET_FIELDS)).copy(),
+                        np.ctypeslib.as_array(r.masks, (NUM_DETS, MASK_HW, MASK_HW)).copy()))
+        return out
+
+    def infer_device(self, d_images_ptr: int, n: int, ori_hw) -> int:
+        import numpy as np
+        hw = np.ascontiguousarray(ori_hw, dtype=np.int32).reshape(-1, 2)
+        self._hw = hw
+        return self.lib.ppdl_infer_device(self.ctx, C.c_void_p(d_images_ptr), n, hw.ctypes.data)
+
+    def device_outputs(self):
+        d = C.c_void_p()
+        m = C.c_void_p()
+        rc = self.lib.ppdl_device_outputs(self.ctx, C.byref(d), C.byref(m))
+        if rc != 0:
+            raise RuntimeError("no device outputs")
+        return d.value, m.value
+
+    def sync(self) -> int:
+        return self.lib.ppdl_sync(self.ctx)
+
+    def stream_ptr(self) -> int:
+        self.lib.ppdl_stream.argtypes = [C.c_void_p]
+        self.lib.ppdl_stream.restype = C.c_void_p
+        return self.lib.ppdl_stream(self.ctx) or 0
+
+    def profile_steps(self, n: int):
+        """[(name, kind, ms, flops_per_page, bytes_per_page)] of one eager
+        forward of the last n pages, with a CUDA event after every step."""
+        self.lib.ppdl_profile_steps.argtypes = [C.c_void_p, C.c_int, C.POINTER(StepStat), C.c_int]
+        self.lib.ppdl_profile_steps.restype = C.c_int
+        buf = (StepStat * 4096)()
+        k = self.lib.ppdl_profile_steps(self.ctx, n, buf, 4096)
+        if k < 0:
+            raise RuntimeError("ppdl_profile_steps failed")
+        return [(buf[i].name.decode(), STEP_KINDS.get(buf[i].kind, "other"), buf[i].ms,
+                 buf[i].flops, buf[i].bytes) for i in range(k)]
+
+    def dump_raw(self, pfx: str) -> int:
+        return self.lib.ppdl_dump_raw(self.ctx, pfx.encode())
+
+    def dump(self, d: str) -> int:
+        return self.lib.ppdl_dump(self.ctx, d.encode())
+
+    def close(self):
+        if self.ctx:
+            self.lib.ppdl_free(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def last_error() -> str:
     return lib().ppdl_op_last_error().decode()
 

@@ -19,8 +19,9 @@ The FFN widths are not pinned by the reference sources (its GEMM
 micro-bench uses 2048 for the decoder FFN, bench/gemm_bench.cu:99); the
 product, the oracle and the tests all read them from the same GGUF.
 
-Init: Kaiming-normal convs (fan-in), Xavier-normal linears, small normal
-biases, LayerNorm gains near 1; BN is already folded (weight + bias only).
+Init: Kaiming-normal convs (fan-in, gain by the following activation),
+Xavier-normal linears, small normal biases, LayerNorm gains near 1; BN is
+already folded (weight + bias only).
 """
 from __future__ import annotations
 
@@ -41,15 +42,19 @@ DEC_FFN = 2048
 
 
 def manifest() -> "OrderedDict[str, tuple]":
-    """name -> (kind, torch-order shape); kind in conv/dwconv/linear/ln/bias."""
+    """name -> (kind, torch-order shape[, activation]); kind in
+    conv/dwconv/linear/ln/bias.  The activation after a conv picks its init
+    gain (relu/silu 2, none 1, "half" 0.5 for the two summed RepVGG branches)
+    so activations stay O(1) through the network, which is what the folded
+    BatchNorm of a trained checkpoint achieves."""
     m: "OrderedDict[str, tuple]" = OrderedDict()
 
-    def conv(name, ic, oc, k):
-        m[name + ".weight"] = ("conv", (oc, ic, k, k))
+    def conv(name, ic, oc, k, act="relu"):
+        m[name + ".weight"] = ("conv", (oc, ic, k, k), act)
         m[name + ".bias"] = ("bias", (oc,))
 
-    def dw(name, c, k):
-        m[name + ".weight"] = ("dwconv", (c, 1, k, k))
+    def dw(name, c, k, act="none"):
+        m[name + ".weight"] = ("dwconv", (c, 1, k, k), act)
         m[name + ".bias"] = ("bias", (c,))
 
     def lin(name, i, o):
@@ -74,43 +79,43 @@ def manifest() -> "OrderedDict[str, tuple]":
             for l in range(6):
                 p = f"{st}.b{b}.l{l}"
                 if light:
-                    conv(p + ".c1", cur, mid, 1)
-                    dw(p + ".c2", mid, 5)
+                    conv(p + ".c1", cur, mid, 1, "none")
+                    dw(p + ".c2", mid, 5, "relu")
                 else:
                     conv(p, cur, mid, 3)
                 cur = mid
             cat = bin_ + 6 * mid
             conv(f"{st}.b{b}.agg0", cat, cout // 2, 1)
             conv(f"{st}.b{b}.agg1", cout // 2, cout, 1)
-    conv("enc_in0", 512, 256, 1)
-    conv("enc_in1", 1024, 256, 1)
-    conv("enc_in2", 2048, 256, 1)
+    conv("enc_in0", 512, 256, 1, "none")
+    conv("enc_in1", 1024, 256, 1, "none")
+    conv("enc_in2", 2048, 256, 1, "none")
     for n in ("q", "k", "v", "o"):
         lin(f"aifi.{n}", 256, 256)
     ln("aifi.ln1")
     ln("aifi.ln2")
     lin("aifi.fc1", 256, AIFI_FFN)
     lin("aifi.fc2", AIFI_FFN, 256)
-    conv("lat0", 256, 256, 1)
-    conv("lat1", 256, 256, 1)
+    conv("lat0", 256, 256, 1, "silu")
+    conv("lat1", 256, 256, 1, "silu")
     for blk in ("fpn0", "fpn1", "pan0", "pan1"):
-        conv(f"{blk}.c1", 512, 256, 1)
-        conv(f"{blk}.c2", 512, 256, 1)
+        conv(f"{blk}.c1", 512, 256, 1, "silu")
+        conv(f"{blk}.c2", 512, 256, 1, "silu")
         for i in range(3):
-            conv(f"{blk}.bn{i}.c1", 256, 256, 3)
-            conv(f"{blk}.bn{i}.c2", 256, 256, 1)
-    conv("pand0", 256, 256, 3)
-    conv("pand1", 256, 256, 3)
-    conv("mh0.0", 256, 64, 3)
-    conv("mh1.0", 256, 64, 3)
-    conv("mh2.0", 256, 64, 3)
-    conv("mh2.2", 64, 64, 3)
-    conv("mh.out", 64, 64, 3)
-    conv("mlat", 128, 64, 3)
-    conv("mout.base", 64, 64, 3)
-    conv("mout.conv", 64, 32, 1)
+            conv(f"{blk}.bn{i}.c1", 256, 256, 3, "half")
+            conv(f"{blk}.bn{i}.c2", 256, 256, 1, "half")
+    conv("pand0", 256, 256, 3, "silu")
+    conv("pand1", 256, 256, 3, "silu")
+    conv("mh0.0", 256, 64, 3, "silu")
+    conv("mh1.0", 256, 64, 3, "silu")
+    conv("mh2.0", 256, 64, 3, "silu")
+    conv("mh2.2", 64, 64, 3, "silu")
+    conv("mh.out", 64, 64, 3, "silu")
+    conv("mlat", 128, 64, 3, "silu")
+    conv("mout.base", 64, 64, 3, "silu")
+    conv("mout.conv", 64, 32, 1, "none")
     for i in range(3):
-        conv(f"dec_in{i}", 256, 256, 1)
+        conv(f"dec_in{i}", 256, 256, 1, "none")
     lin("enc_out.l", 256, 256)
     ln("enc_out.ln")
     lin("score_head", 256, 25)
@@ -144,16 +149,24 @@ def manifest() -> "OrderedDict[str, tuple]":
 def make_weights(seed: int = 0) -> "OrderedDict[str, np.ndarray]":
     rng = np.random.default_rng(seed)
     out: "OrderedDict[str, np.ndarray]" = OrderedDict()
-    for name, (kind, shape) in manifest().items():
-        if kind == "conv":
+    gain = {"relu": 2.0, "silu": 2.0, "none": 1.0, "half": 0.5}
+    for name, spec in manifest().items():
+        kind, shape = spec[0], spec[1]
+        if kind in ("conv", "dwconv"):
             fan_in = shape[1] * shape[2] * shape[3]
-            a = rng.standard_normal(shape) * np.sqrt(2.0 / fan_in)
-        elif kind == "dwconv":
-            a = rng.standard_normal(shape) * np.sqrt(2.0 / (shape[2] * shape[3]))
+            g = gain[spec[2]]
+            if name.endswith(".agg1.weight") and (".b1." in name or ".b2." in name):
+                g *= 0.5  # the block output is added to a residual of equal variance
+            a = rng.standard_normal(shape) * np.sqrt(g / fan_in)
         elif kind == "linear":
             a = rng.standard_normal(shape) * np.sqrt(2.0 / (shape[0] + shape[1]))
         elif kind == "ln":
             a = 1.0 + 0.05 * rng.standard_normal(shape)
+        elif name == "enc_out.l.bias":
+            # masked (border) memory tokens are exactly zero; a zero bias maps
+            # them to the LayerNorm offset, i.e. low class logits, as a trained
+            # model's two-stage selection does
+            a = np.zeros(shape)
         else:
             a = 0.05 * rng.standard_normal(shape)
         out[name] = a.astype(np.float32)

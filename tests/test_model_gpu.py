@@ -1,0 +1,128 @@
+"""End-to-end parity: the B200 forward through the public C ABI
+(ppdl_infer_batch / ppdl_infer / ppdl_dump_raw) against the CPU restatement
+of the reference graph (oracle/model_ref.py), on seeded synthetic pages and
+seeded random weights.
+
+Gates (the hot path's end-to-end contract):
+  * identical labels and top-300 selection for detections whose score
+    margin to their neighbours exceeds 1e-4;
+  * score diff < 1e-4, box diff <= 0.01 px;
+  * mask IoU >= 0.99;
+  * identical reading order for detections with score >= 0.3.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import ppdl
+import synth
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def gguf_path(tmp_path_factory):
+    d = os.environ.get("PPDL_SYNTH_DIR") or str(tmp_path_factory.mktemp("synth"))
+    return synth.cached_gguf(0, d)
+
+
+@pytest.fixture(scope="module")
+def ref_model(gguf_path):
+    from oracle import model_ref
+    return model_ref.RefModel(model_ref.load_gguf(gguf_path))
+
+
+@pytest.fixture(scope="module")
+def pages():
+    return [(synth.synth_page(100 + i), hw) for i, hw in enumerate([(1000, 700), (800, 800)])]
+
+
+@pytest.fixture(scope="module")
+def ref_out(ref_model, pages):
+    return [ref_model.forward(img, h, w) for img, (h, w) in pages]
+
+
+@pytest.fixture(scope="module")
+def gpu_out(cuda, gguf_path, pages, tmp_path_factory):
+    ctx = ppdl.Context(gguf_path, max_batch=2)
+    imgs = np.stack([p[0] for p in pages])
+    hw = np.array([p[1] for p in pages], np.int32)
+    outs = ctx.infer_batch(imgs, hw)
+    d = tmp_path_factory.mktemp("raw")
+    assert ctx.dump_raw(str(d) + "/p0_") == 0
+    raw = {k: np.fromfile(str(d) + f"/p0_{k}.bin", dtype=np.int32 if k == "sel" else np.float32)
+           for k in ("logits", "boxes", "order", "sel")}
+    ctx.close()
+    return outs, raw
+
+
+def _margin_ok(scores, i, tol=1e-4):
+    lo = scores[i + 1] if i + 1 < len(scores) else -1.0
+    hi = scores[i - 1] if i > 0 else 2.0
+    return hi - scores[i] > tol and scores[i] - lo > tol
+
+
+def test_raw_outputs_page0(gpu_out, ref_out):
+    _, raw = gpu_out
+    r = ref_out[0]
+    lg = raw["logits"].reshape(300, 25)
+    s_gpu, s_ref = 1 / (1 + np.exp(-lg.astype(np.float64))), 1 / (1 + np.exp(-r["logits"].astype(np.float64)))
+    assert np.abs(s_gpu - s_ref).max() < 1e-4, np.abs(s_gpu - s_ref).max()
+    assert np.abs(raw["boxes"].reshape(300, 4) - r["boxes"]).max() * 1000 <= 0.01
+    od = raw["order"]
+    assert np.abs(od - r["order"]).max() / max(np.abs(r["order"]).max(), 1) < 1e-4
+
+
+@pytest.mark.parametrize("page", [0, 1])
+def test_dets_and_masks(gpu_out, ref_out, pages, page):
+    outs, _ = gpu_out
+    dets, masks = outs[page]
+    r = ref_out[page]
+    rd, rm = r["dets"], r["masks"].reshape(300, 200, 200)
+    scores = rd[:, 1]
+    n_checked = 0
+    for i in range(300):
+        if not _margin_ok(scores, i):
+            continue
+        n_checked += 1
+        assert dets[i, 0] == rd[i, 0], f"label row {i}"
+        assert abs(dets[i, 1] - rd[i, 1]) < 1e-4, f"score row {i}"
+        h, w = pages[page][1]
+        # box diff in pixels of the original image
+        assert np.abs(dets[i, 2:6] - rd[i, 2:6]).max() <= 0.01, f"box row {i}"
+        a, b = masks[i] != 0, rm[i] != 0
+        union = np.logical_or(a, b).sum()
+        iou = np.logical_and(a, b).sum() / union if union else 1.0
+        assert iou >= 0.99, f"mask IoU row {i}: {iou}"
+        if rd[i, 1] >= 0.3:
+            assert dets[i, 6] == rd[i, 6], f"reading order row {i}"
+    assert n_checked >= 30, n_checked
+    # the whole score column regardless of margins
+    assert np.abs(dets[:, 1] - rd[:, 1]).max() < 1e-4
+
+
+def test_single_page_api_matches_batch(cuda, gguf_path, pages, gpu_out):
+    ctx = ppdl.Context(gguf_path, max_batch=1)
+    img, (h, w) = pages[0]
+    dets, masks, ms = ctx.infer(img, h, w)
+    dets2, _, _ = ctx.infer(img, h, w)  # graph replay path
+    ctx.close()
+    np.testing.assert_array_equal(dets, dets2)
+    bd, bm = gpu_out[0][0]
+    np.testing.assert_allclose(dets, bd, rtol=0, atol=1e-5)
+    assert ms > 0
+
+
+def test_bad_arguments(cuda, gguf_path):
+    import ctypes as C
+    L = ppdl.lib()
+    res = ppdl.Result()
+    assert L.ppdl_infer(None, None, 800, 800, C.byref(res)) == 1
+    ctx = ppdl.Context(gguf_path)
+    img = np.zeros((3, 800, 800), np.float32)
+    assert L.ppdl_infer(ctx.ctx, img.ctypes.data, 0, 800, C.byref(res)) == 1
+    assert L.ppdl_infer(ctx.ctx, img.ctypes.data, 800, -5, C.byref(res)) == 1
+    ctx.close()
+    assert L.ppdl_init(b"/nonexistent/model.gguf", 1) is None
+    assert L.ppdl_init(gguf_path.encode(), 0) is None  # no CPU backend in this build
