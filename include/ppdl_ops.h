@@ -95,6 +95,22 @@ PPDL_OPS_API int ppdl_op_supported(const ppdl_op_desc * desc);
    Returns a PPDL_OK / PPDL_ERR_* status. */
 PPDL_OPS_API int ppdl_op_launch(const ppdl_op_desc * desc, void * stream);
 
+/* Extension (no counterpart in the reference, which calls cuBLAS SGEMM with
+   TF32 off at patch:650-665 and 787-802): the FP32-faithful tensor-core GEMM
+   that the 1x1 convs, the Winograd madd and the linears run on.
+     C[z](m, n) = sum_k A[z](m, k) * B(n, k)
+   A: a_m_major != 0 -> A(m, k) = A[z*a_bs + k*lda + m] (CHW activations);
+      otherwise     A(m, k) = A[z*a_bs + m*lda + k] (row-major).
+   B: [N][K] row-major, shared by all z.  C(m, n) at C[z*c_bs + m*ldc_m + n*ldc_n].
+   b_split: caller-provided device workspace of 2*N*K floats for the TF32
+   halves of B.  Requirements (TMA): A, b_split 16-byte aligned; lda, a_bs and
+   K multiples of 4.  Returns PPDL_OK / PPDL_ERR_SHAPE / PPDL_ERR_CUDA. */
+PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float * A,
+                                  int a_m_major, long long lda, long long a_bs,
+                                  const float * B, float * b_split, float * C,
+                                  long long ldc_m, long long ldc_n, long long c_bs,
+                                  void * stream);
+
 /* Human-readable text of the last error of ppdl_op_launch on this thread. */
 PPDL_OPS_API const char * ppdl_op_last_error(void);
 

@@ -63,7 +63,7 @@ int sm_count() {
 // (T, IC, 36) plane layout per page)
 __global__ void __launch_bounds__(256)
 wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ dt, int IC,
-                 int H, int W, int TW, int TH, int pad, int B) {
+                 int H, int W, int TW, int TH, int pad, int B, int ldt) {
     const int T = TW * TH;
     const long long n = (long long)B * IC * T;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -95,7 +95,7 @@ wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__
             for (int a = 0; a < 6; a++) s = fmaf(c_wgB[u * 6 + a], d[a][v], s);
             t1[u][v] = s;
         }
-    float *o = dt + ((long long)b * 36 * IC + ic) * T + tile;
+    float *o = dt + ((long long)b * 36 * IC + ic) * ldt + tile;
 #pragma unroll
     for (int u = 0; u < 6; u++)
 #pragma unroll
@@ -103,7 +103,7 @@ wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__
             float s = 0.0f;
 #pragma unroll
             for (int c = 0; c < 6; c++) s = fmaf(t1[u][c], c_wgB[w * 6 + c], s);
-            o[(long long)(u * 6 + w) * IC * T] = s;
+            o[(long long)(u * 6 + w) * IC * ldt] = s;
         }
 }
 
@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(256)
 wg4_output_kernel(const float *__restrict__ yt, const float *__restrict__ bias,
                   float *__restrict__ y, long long ybs, const float *__restrict__ res,
                   long long rbs, int res_mode, int OC, int OH, int OW, int TW, int TH, int act,
-                  int B) {
+                  int B, int ldt) {
     const int T = TW * TH;
     const long long n = (long long)B * OC * T;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -122,10 +122,10 @@ wg4_output_kernel(const float *__restrict__ yt, const float *__restrict__ bias,
     const int oc = (int)(r % OC);
     const int b = (int)(r / OC);
     const int ty = tile / TW, tx = tile - ty * TW;
-    const float *m = yt + ((long long)b * 36 * OC + oc) * T + tile;
+    const float *m = yt + ((long long)b * 36 * OC + oc) * ldt + tile;
     float mm[36];
 #pragma unroll
-    for (int p = 0; p < 36; p++) mm[p] = __ldg(m + (long long)p * OC * T);
+    for (int p = 0; p < 36; p++) mm[p] = __ldg(m + (long long)p * OC * ldt);
     float t1[4][6];
 #pragma unroll
     for (int a = 0; a < 4; a++)
@@ -180,6 +180,25 @@ __global__ void wg4_filter_kernel(const float *__restrict__ w, float *__restrict
             s = __fadd_rn(s, __fmul_rn(g, w[(((long long)oc * IC + ic) * 3 + a) * 3 + b]));
         }
     wg4[i] = s;
+}
+
+// wg4 [36][IC][OC] -> hi/lo [36][OC][IC] (K-major B operand of the
+// tensor-core madd, split into TF32 halves)
+__global__ void wg4_kmajor_split_kernel(const float *__restrict__ wg4, float *__restrict__ hi,
+                                        float *__restrict__ lo, int IC, int OC) {
+    const long long n = 36LL * IC * OC;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int ic = (int)(i % IC);
+    const long long r = i / IC;
+    const int oc = (int)(r % OC);
+    const int p = (int)(r / OC);
+    const float v = wg4[((long long)p * IC + ic) * OC + oc];
+    uint32_t hr;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hr) : "f"(v));  // nearest TF32
+    const float h = __uint_as_float(hr);
+    hi[i] = h;
+    lo[i] = v - h;
 }
 
 // ---- depthwise conv -----------------------------------------------------------
@@ -306,27 +325,38 @@ inline int blocks(long long n, int t = 256) { return (int)((n + t - 1) / t); }
 }  // namespace
 
 Status launch_wg4_input(const float *x, long long xbs, float *dt, int IC, int H, int W, int TW,
-                        int TH, int pad, int B, cudaStream_t st) {
+                        int TH, int pad, int B, cudaStream_t st, int ldt) {
     const long long n = (long long)B * IC * TW * TH;
     if (n <= 0) return n == 0 ? OK : ERR_SHAPE;
-    wg4_input_kernel<<<blocks(n), 256, 0, st>>>(x, xbs, dt, IC, H, W, TW, TH, pad, B);
+    if (ldt <= 0) ldt = TW * TH;
+    if (ldt < TW * TH) return ERR_SHAPE;
+    wg4_input_kernel<<<blocks(n), 256, 0, st>>>(x, xbs, dt, IC, H, W, TW, TH, pad, B, ldt);
     return cuda_status();
 }
 
 Status launch_wg4_output(const float *yt, const float *bias, float *y, long long ybs,
                          const float *res, long long rbs, int res_mode, int OC, int OH, int OW,
-                         int TW, int TH, int act, int B, cudaStream_t st) {
+                         int TW, int TH, int act, int B, cudaStream_t st, int ldt) {
     const long long n = (long long)B * OC * TW * TH;
     if (n <= 0) return n == 0 ? OK : ERR_SHAPE;
     if (TW < (OW + 3) / 4 || TH < (OH + 3) / 4) return ERR_SHAPE;
+    if (ldt <= 0) ldt = TW * TH;
+    if (ldt < TW * TH) return ERR_SHAPE;
     wg4_output_kernel<<<blocks(n), 256, 0, st>>>(yt, bias, y, ybs, res, rbs, res_mode, OC, OH, OW,
-                                                 TW, TH, act, B);
+                                                 TW, TH, act, B, ldt);
     return cuda_status();
 }
 
 Status launch_wg4_filter(const float *w, float *wg4, int IC, int OC, cudaStream_t st) {
     const long long n = 36LL * IC * OC;
     wg4_filter_kernel<<<blocks(n), 256, 0, st>>>(w, wg4, IC, OC);
+    return cuda_status();
+}
+
+Status launch_wg4_kmajor_split(const float *wg4, float *hi, float *lo, int IC, int OC,
+                               cudaStream_t st) {
+    const long long n = 36LL * IC * OC;
+    wg4_kmajor_split_kernel<<<blocks(n), 256, 0, st>>>(wg4, hi, lo, IC, OC);
     return cuda_status();
 }
 

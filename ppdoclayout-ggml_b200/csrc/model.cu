@@ -40,6 +40,7 @@
 #include "conv.h"
 #include "dec.h"
 #include "gemm.h"
+#include "gemm_tc.h"
 #include "gguf.h"
 #include "kernels.h"
 
@@ -127,6 +128,41 @@ public:
         for (auto &g : graphs) cudaGraphExecDestroy(g.second);
         for (void *p : allocs) cudaFree(p);
         if (st) cudaStreamDestroy(st);
+    }
+
+    // Tensor-core (3xTF32) GEMMs for every contraction whose operands satisfy
+    // the TMA rules; the SIMT FFMA GEMM takes the rest.  PPDL_TC=0 forces the
+    // SIMT path everywhere (a bisection knob like the reference's
+    // PPDL_CONV_MODE, src/ppdoclayout.cpp:392-398).
+    bool use_tc = true;
+    std::vector<std::function<void()>> finalizers;  // plans that need the scratch buffers
+
+    struct Split {
+        float *hi = nullptr, *lo = nullptr;
+    };
+    Split split(const float *w, long long n) {
+        Split s;
+        s.hi = dalloc(n);
+        s.lo = dalloc(n);
+        if (ok && launch_tf32_split(w, s.hi, s.lo, n, st) != OK) fail("weight split failed");
+        return s;
+    }
+    static bool tc_shape_ok(const float *p, long long plane, long long bs, int K) {
+        return ((uintptr_t)p & 15) == 0 && plane % 4 == 0 && bs % 4 == 0 && K % 4 == 0;
+    }
+    // launch a planned tensor-core GEMM for the current batch: rows_per_page > 0
+    // folds the pages into M, otherwise every page (x zmul planes) is a z slice
+    Status run_tc(const std::shared_ptr<TcGemm> &g, int rows_per_page, int zmul = 1) {
+        TcGemm r = *g;
+        if (rows_per_page > 0) {
+            r.M = nb * rows_per_page;
+            r.m_tiles = (r.M + 127) / 128;
+            r.batch = 1;
+        } else {
+            r.batch = nb * zmul;
+        }
+        r.tiles = r.m_tiles * r.n_tiles * r.batch;
+        return launch_tc_gemm(r, st);
     }
 
     template <typename F>
@@ -260,6 +296,25 @@ public:
             return;
         }
         if (K == 1 && s == 1 && p == 0 && p_hi < 0) {
+            // tensor cores: A = x (pixels x channels, M-major), B = W [OC][IC]
+            if (use_tc && tc_shape_ok(x.p, x.plane(), x.bs, IC)) {
+                const Split wsp = split(wp, (long long)OC * IC);
+                TcEpilogue e;
+                e.C = y.p; e.ldc_m = 1; e.ldc_n = y.plane(); e.c_bs = y.bs;
+                e.bias = bp; e.act = act;
+                if (res_mode) {
+                    e.res = res.p; e.res_ldm = 1; e.res_ldn = res.plane(); e.res_bs = res.bs;
+                    e.res_mode = res_mode;
+                }
+                auto g = std::make_shared<TcGemm>();
+                if (ok && tc_gemm_plan(g.get(), (int)x.plane(), OC, IC, Bmax, x.p, 1, x.plane(),
+                                       x.bs, wsp.hi, wsp.lo, 1, e)) {
+                    push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * OH * OW * IC,
+                         4.0 * ((double)IC * x.plane() + (double)OC * OH * OW),
+                         [=]() { return run_tc(g, 0); });
+                    return;
+                }
+            }
             push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * OH * OW * IC,
                  4.0 * ((double)IC * x.plane() + (double)OC * OH * OW), [=]() {
                 GemmArgs g;
@@ -278,32 +333,51 @@ public:
         }
         if (K == 3 && s == 1 && p == 1 && p_hi < 0) {
             // Winograd F(4,3) (src/ppdoclayout.cpp:430-464)
+            // plane rows padded to 4 floats so TMA row strides are 16-byte multiples
             const int TW = (x.W + 3) / 4, TH = (x.H + 3) / 4, T = TW * TH;
+            const int Tp = (T + 3) / 4 * 4;
             float *wg4 = dalloc(36LL * IC * OC);
             if (!ok) return;
             if (launch_wg4_filter(wp, wg4, IC, OC, st) != OK) {
                 fail("filter transform launch failed");
                 return;
             }
-            wg_dt_n = std::max(wg_dt_n, 36LL * IC * T * Bmax);
-            wg_yt_n = std::max(wg_yt_n, 36LL * OC * T * Bmax);
+            wg_dt_n = std::max(wg_dt_n, 36LL * IC * Tp * Bmax);
+            wg_yt_n = std::max(wg_yt_n, 36LL * OC * Tp * Bmax);
             push(name + ".wg_in", PPDL_STEP_WG_INPUT, 0.0,
                  4.0 * ((double)IC * x.plane() + 36.0 * IC * T), [=]() {
-                return launch_wg4_input(x.p, x.bs, wg_dt, IC, x.H, x.W, TW, TH, 1, nb, st);
+                return launch_wg4_input(x.p, x.bs, wg_dt, IC, x.H, x.W, TW, TH, 1, nb, st, Tp);
             });
+            std::shared_ptr<TcGemm> g;
+            if (use_tc && IC % 4 == 0) {
+                // B = wg4 as K-major TF32 halves [36][OC][IC]; A (the dt planes)
+                // exists only once the scratch is allocated -> plan in finalize
+                float *bhi = dalloc(36LL * IC * OC), *blo = dalloc(36LL * IC * OC);
+                if (!ok) return;
+                if (launch_wg4_kmajor_split(wg4, bhi, blo, IC, OC, st) != OK) fail("wg4 split");
+                g = std::make_shared<TcGemm>();
+                finalizers.push_back([=]() {
+                    TcEpilogue e;
+                    e.C = wg_yt; e.ldc_m = 1; e.ldc_n = Tp; e.c_bs = (long long)OC * Tp;
+                    if (!tc_gemm_plan(g.get(), T, OC, IC, Bmax * 36, wg_dt, 1, Tp,
+                                      (long long)IC * Tp, bhi, blo, 36, e))
+                        g->ok = false;
+                });
+            }
             push(name + ".wg_madd", PPDL_STEP_WG_MADD, 2.0 * 36 * T * IC * OC,
                  4.0 * (36.0 * T * (IC + OC) + 36.0 * IC * OC), [=]() {
-                GemmArgs g;
-                g.M = OC; g.N = T; g.K = IC; g.batch = nb * 36;
-                g.A = {wg4, 1, OC, 36, 0, (long long)IC * OC};
-                g.B = {wg_dt, T, 1, 1, (long long)IC * T, 0};
-                g.C = wg_yt; g.ldc_m = T; g.ldc_n = 1; g.c_bs_hi = (long long)OC * T;
-                return launch_gemm_simt(g, st);
+                if (g && g->ok) return run_tc(g, 0, 36);
+                GemmArgs q;
+                q.M = OC; q.N = T; q.K = IC; q.batch = nb * 36;
+                q.A = {wg4, 1, OC, 36, 0, (long long)IC * OC};
+                q.B = {wg_dt, Tp, 1, 1, (long long)IC * Tp, 0};
+                q.C = wg_yt; q.ldc_m = Tp; q.ldc_n = 1; q.c_bs_hi = (long long)OC * Tp;
+                return launch_gemm_simt(q, st);
             });
             push(name + ".wg_out", PPDL_STEP_WG_OUTPUT, 0.0,
                  4.0 * (36.0 * OC * T + (double)OC * OH * OW * (res_mode ? 2 : 1)), [=]() {
                 return launch_wg4_output(wg_yt, bp, y.p, y.bs, res.p, res.bs, res_mode, OC, OH, OW,
-                                         TW, TH, act, nb, st);
+                                         TW, TH, act, nb, st, Tp);
             });
             return;
         }
@@ -337,6 +411,19 @@ public:
             return;
         }
         const float *wp = wt.p, *bp = bt.p;
+        if (use_tc && tc_shape_ok(x.p, x.plane(), x.bs, IC)) {
+            const Split wsp = split(wp, (long long)OC * IC);
+            TcEpilogue e;
+            e.C = y.p + (long long)row0 * y.D; e.ldc_m = y.D; e.ldc_n = 1; e.c_bs = y.bs();
+            e.bias = bp;
+            auto g = std::make_shared<TcGemm>();
+            if (ok && tc_gemm_plan(g.get(), (int)x.plane(), OC, IC, Bmax, x.p, 1, x.plane(), x.bs,
+                                   wsp.hi, wsp.lo, 1, e)) {
+                push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * x.plane() * IC,
+                     4.0 * ((double)IC + OC) * x.plane(), [=]() { return run_tc(g, 0); });
+                return;
+            }
+        }
         push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * x.plane() * IC,
              4.0 * ((double)IC + OC) * x.plane(), [=]() {
             GemmArgs g;
@@ -361,6 +448,24 @@ public:
             return;
         }
         const float *wp = wt.p, *bp = bt.p;
+        if (use_tc && in % 4 == 0 && ((uintptr_t)x.p & 15) == 0) {
+            const Split wsp = split(wp, (long long)out * in);
+            TcEpilogue e;
+            e.C = y.p; e.ldc_m = out; e.ldc_n = 1;
+            e.bias = bp; e.act = act;
+            if (res.p) {
+                e.res = res.p; e.res_ldm = out; e.res_ldn = 1; e.res_mode = 2;
+            }
+            auto g = std::make_shared<TcGemm>();
+            if (ok && tc_gemm_plan(g.get(), Bmax * x.T, out, in, 1, x.p, 0, in, 0, wsp.hi, wsp.lo, 1,
+                                   e)) {
+                const int T = x.T;
+                push(name, PPDL_STEP_GEMM_LINEAR, 2.0 * x.T * out * in,
+                     4.0 * ((double)x.T * (in + out) + (double)in * out),
+                     [=]() { return run_tc(g, T); });
+                return;
+            }
+        }
         push(name, PPDL_STEP_GEMM_LINEAR, 2.0 * x.T * out * in,
              4.0 * ((double)x.T * (in + out) + (double)in * out), [=]() {
             GemmArgs g;
@@ -638,7 +743,25 @@ public:
         mlp3(tq, mq0, "mq");
         float *encm = dalloc((long long)kNQ * kMaskPix * Bmax);
         const V mf = mfeat;
+        // mask logits [b][q][p] = sum_c mq[b][q][c] mf[b][c][p]: on the tensor
+        // cores A = mf (pixels x 32 channels, M-major) and B = mq, split into
+        // TF32 halves per forward (it is an activation)
+        float *mq_hi = dalloc((long long)kNQ * 32 * Bmax), *mq_lo = dalloc((long long)kNQ * 32 * Bmax);
         auto mask_gemm = [=](const S &mq, float *dst) {
+            if (use_tc && tc_shape_ok(mf.p, mf.plane(), mf.bs, 32)) {
+                TcEpilogue e;
+                e.C = dst; e.ldc_m = 1; e.ldc_n = kMaskPix; e.c_bs = (long long)kNQ * kMaskPix;
+                auto g = std::make_shared<TcGemm>();
+                if (ok && tc_gemm_plan(g.get(), kMaskPix, kNQ, 32, Bmax, mf.p, 1, mf.plane(), mf.bs,
+                                       mq_hi, mq_lo, Bmax, e)) {
+                    push("mask_gemm", PPDL_STEP_GEMM_LINEAR, 2.0 * kNQ * kMaskPix * 32,
+                         4.0 * ((double)kNQ * kMaskPix + 32.0 * kMaskPix), [=]() {
+                        TRY(launch_tf32_split(mq.p, mq_hi, mq_lo, (long long)nb * mq.bs(), st));
+                        return run_tc(g, 0);
+                    });
+                    return;
+                }
+            }
             push("mask_gemm", PPDL_STEP_GEMM_LINEAR, 2.0 * kNQ * kMaskPix * 32,
                  4.0 * ((double)kNQ * kMaskPix + 32.0 * kMaskPix), [=]() {
                 GemmArgs g;
@@ -746,6 +869,8 @@ public:
         if (!ok) return;
         wg_dt = dalloc(wg_dt_n);
         wg_yt = dalloc(wg_yt_n);
+        if (!ok) return;
+        for (auto &f : finalizers) f();
     }
 
     float *pos = nullptr, *valid = nullptr;
@@ -759,6 +884,8 @@ public:
         Bmax = max_batch;
         nb = max_batch;
         dumps = want_dumps;
+        const char *tc_env = getenv("PPDL_TC");
+        use_tc = !(tc_env && tc_env[0] == '0');
         if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
             fail("no CUDA device / stream");
             return false;
@@ -962,6 +1089,10 @@ PPDL_API int ppdl_infer_batch(ppdl_ctx *c, const float *images, int n, const int
         fprintf(stderr, "ppdl: graph compute failed: %s\n", cudaGetErrorString(cudaGetLastError()));
         return 2;
     }
+    if (ppdl::tc_error_fetch_and_clear()) {
+        fprintf(stderr, "ppdl: tensor-core GEMM gave up waiting (device error flag set)\n");
+        return 2;
+    }
     float ms = 0.f;
     cudaEventElapsedTime(&ms, c->e0, c->e1);
     c->computed = true;
@@ -1001,7 +1132,8 @@ PPDL_API int ppdl_device_outputs(ppdl_ctx *c, const float **d_dets, const int32_
 PPDL_API int ppdl_sync(ppdl_ctx *c) {
     if (!c) return 1;
     cudaSetDevice(c->m->dev);
-    return cudaStreamSynchronize(c->m->st) == cudaSuccess ? 0 : 2;
+    if (cudaStreamSynchronize(c->m->st) != cudaSuccess) return 2;
+    return ppdl::tc_error_fetch_and_clear() ? 2 : 0;
 }
 
 PPDL_API int ppdl_dump(ppdl_ctx *c, const char *dir) {

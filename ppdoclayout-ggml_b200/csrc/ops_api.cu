@@ -12,6 +12,7 @@
 
 #include "../../include/ppdl_ops.h"
 #include "kernels.h"
+#include "gemm_tc.h"
 #include "ops_internal.h"
 
 namespace {
@@ -59,6 +60,26 @@ PPDL_OPS_API int ppdl_op_supported(const ppdl_op_desc *d) {
 }
 
 PPDL_OPS_API const char *ppdl_op_last_error(void) { return g_err; }
+
+PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float *A, int a_m_major,
+                                  long long lda, long long a_bs, const float *B, float *b_split,
+                                  float *C, long long ldc_m, long long ldc_n, long long c_bs,
+                                  void *stream) {
+    g_err[0] = 0;
+    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || !A || !B || !b_split || !C)
+        return fail(PPDL_ERR_SHAPE, "gemm: bad sizes or null pointer");
+    cudaStream_t st = (cudaStream_t)stream;
+    float *hi = b_split, *lo = b_split + (long long)N * K;
+    ppdl::Status s = ppdl::launch_tf32_split(B, hi, lo, (long long)N * K, st);
+    if (s != ppdl::OK) return to_status(s);
+    ppdl::TcEpilogue e;
+    e.C = C; e.ldc_m = ldc_m; e.ldc_n = ldc_n; e.c_bs = c_bs;
+    ppdl::TcGemm g;
+    if (!ppdl::tc_gemm_plan(&g, M, N, K, batch, A, a_m_major ? 1 : 0, lda, a_bs, hi, lo, 1, e))
+        return fail(PPDL_ERR_SHAPE, "gemm: operands violate the TMA rules (16-byte alignment, "
+                                    "strides and K multiples of 4)");
+    return to_status(ppdl::launch_tc_gemm(g, st));
+}
 
 PPDL_OPS_API int ppdl_op_launch(const ppdl_op_desc *d, void *stream_ptr) {
     g_err[0] = 0;
