@@ -38,17 +38,87 @@ def load_gguf(path: str) -> dict:
     return out
 
 
-class RefModel:
-    """Forward of one page: image [3,800,800] -> raw outputs + dets."""
+LVL = ((100, 100, 0), (50, 50, 10000), (25, 25, 12500))
 
-    def __init__(self, weights: dict, threads: int | None = None):
-        self.w = weights
+
+def msdeform_t(value, off, awr, ref):
+    """Torch restatement of op_msdeform (src/ppdoclayout.cpp:142-198) in the
+    dtype of its inputs (used for the float64 oracle): value [13125,256],
+    off [nq,192], awr [nq,96], ref [nq,4] -> [nq,256]."""
+    nq = off.shape[0]
+    w = torch.softmax(awr.reshape(nq, NH, 12), dim=-1)
+    off = off.reshape(nq, NH, 3, 4, 2)
+    v = value.reshape(-1, NH, HD)
+    out = torch.zeros((nq, NH, HD), dtype=value.dtype)
+    hidx = torch.arange(NH).view(1, NH, 1)
+    for l, (W, H, st) in enumerate(LVL):
+        lx = ref[:, 0].view(nq, 1, 1) + off[:, :, l, :, 0] / 4 * ref[:, 2].view(nq, 1, 1) * 0.5
+        ly = ref[:, 1].view(nq, 1, 1) + off[:, :, l, :, 1] / 4 * ref[:, 3].view(nq, 1, 1) * 0.5
+        fx, fy = lx * W - 0.5, ly * H - 0.5
+        x0, y0 = torch.floor(fx), torch.floor(fy)
+        tx, ty = fx - x0, fy - y0
+        x0, y0 = x0.long(), y0.long()
+        wl = w[:, :, l * 4:(l + 1) * 4]
+        for k in range(4):
+            dx, dy = k & 1, k >> 1
+            cw = (tx if dx else 1 - tx) * (ty if dy else 1 - ty)
+            xx, yy = x0 + dx, y0 + dy
+            ok = (xx >= 0) & (xx < W) & (yy >= 0) & (yy < H) & (cw != 0)
+            tok = (st + yy.clamp(0, H - 1) * W + xx.clamp(0, W - 1))       # [nq, NH, 4]
+            rows = v[tok, hidx.expand_as(tok)]                               # [nq, NH, 4, HD]
+            coef = (wl * cw * ok).unsqueeze(-1)
+            out += (coef * rows).sum(2)
+    return out.reshape(nq, DM)
+
+
+def mask_box_t(ml):
+    """op_mask_box (src/ppdoclayout.cpp:98-140) in torch: [nq,40000] -> [nq,4]."""
+    pos = (ml > 0).reshape(-1, 200, 200)
+    out = torch.zeros((pos.shape[0], 4), dtype=ml.dtype)
+    ar = torch.arange(200, dtype=ml.dtype)
+    for q in range(pos.shape[0]):
+        ys, xs = pos[q].any(1), pos[q].any(0)
+        if not bool(xs.any()):
+            b = torch.zeros(4, dtype=ml.dtype)
+        else:
+            b = torch.stack([ar[xs].min(), ar[ys].min(), ar[xs].max() + 1, ar[ys].max() + 1]) / 200
+        c = torch.stack([(b[0] + b[2]) * 0.5, (b[1] + b[3]) * 0.5, b[2] - b[0], b[3] - b[1]])
+        c = c.clamp(0, 1)
+        out[q] = torch.log(c.clamp(min=1e-5) / (1 - c).clamp(min=1e-5))
+    return out
+
+
+def topk_t(lg, nq=NQ):
+    """op_topk300 (src/ppdoclayout.cpp:73-96): stable descending sort of the
+    per-token max logit, ties to the lower index."""
+    mx = lg.max(dim=1).values
+    return torch.sort(-mx, stable=True).indices[:nq].numpy().astype(np.int32)
+
+
+class RefModel:
+    """Forward of one page: image [3,800,800] -> raw outputs + dets.
+
+    dtype=torch.float32 is the FP32 restatement (dense ops in torch FP32,
+    hot-path ops through the pinned C restatement); dtype=torch.float64
+    evaluates the same graph in double precision (hot-path ops through the
+    torch restatements above) as an exact-arithmetic reference; the discrete
+    postprocess runs on its outputs rounded to FP32."""
+
+    def __init__(self, weights: dict, threads: int | None = None, dtype=torch.float32):
+        self.dtype = dtype
+        self.w = {k: v.to(dtype) for k, v in weights.items()}
         if threads:
             torch.set_num_threads(threads)
         o = _oracle()
         self.o = o
-        self.pos = torch.from_numpy(o.pos_embed())
-        self.valid = torch.from_numpy(o.valid_mask())
+        self.pos = torch.from_numpy(o.pos_embed()).to(dtype)
+        self.valid = torch.from_numpy(o.valid_mask()).to(dtype)
+        if dtype == torch.float64:   # the constants in float64 math (:887-923)
+            om = 1.0 / np.power(10000.0, np.arange(64) / 64.0)
+            hh, ww = np.meshgrid(np.arange(25), np.arange(25), indexing="ij")
+            h, w_ = hh.reshape(-1, 1) * om, ww.reshape(-1, 1) * om
+            self.pos = torch.from_numpy(np.concatenate(
+                [np.sin(h), np.cos(h), np.sin(w_), np.cos(w_)], 1)).to(dtype)
 
     # ---- building blocks (src/ppdoclayout.cpp:379-594) ----------------------
     @staticmethod
@@ -93,7 +163,10 @@ class RefModel:
         q = self.lin(qk_in, pfx + ".q").reshape(T, NH, HD).permute(1, 0, 2)
         k = self.lin(qk_in, pfx + ".k").reshape(T, NH, HD).permute(1, 0, 2)
         v = self.lin(v_in, pfx + ".v").reshape(T, NH, HD).permute(1, 0, 2)
-        kq = torch.softmax((q @ k.transpose(1, 2)) * (1.0 / np.sqrt(HD)).astype(np.float32), dim=-1)
+        scale = 1.0 / np.sqrt(HD)
+        if self.dtype == torch.float32:
+            scale = float(np.float32(scale))  # ggml_scale's float factor
+        kq = torch.softmax((q @ k.transpose(1, 2)) * scale, dim=-1)
         o = (kq @ v).permute(1, 0, 2).reshape(T, DM)
         return self.lin(o, pfx + ".o")
 
@@ -184,7 +257,8 @@ class RefModel:
     # ---- full graph (:733-882) + postprocess (:927-993) -----------------------
     @torch.no_grad()
     def forward(self, image: np.ndarray, ori_h: int = 800, ori_w: int = 800, want_masks=True):
-        img = torch.from_numpy(np.ascontiguousarray(image, dtype=np.float32))
+        img = torch.from_numpy(np.ascontiguousarray(image, dtype=np.float32)).to(self.dtype)
+        f64 = self.dtype == torch.float64
         x4, p8, p16, p32 = self.backbone(img)
         f8, n16, n32, mfeat = self.encoder(x4, p8, p16, p32)
         mflat = mfeat.reshape(32, -1)                                   # [c][p]
@@ -194,11 +268,11 @@ class RefModel:
         memory = source * self.valid[:, None]
         om = self.ln(self.lin(memory, "enc_out.l"), "enc_out.ln")
         ecls = self.lin(om, "score_head")                               # [13125][25]
-        topk = self.o.topk(np.ascontiguousarray(ecls.numpy())[None])[0]
+        topk = topk_t(ecls) if f64 else self.o.topk(np.ascontiguousarray(ecls.numpy())[None])[0]
         target = om[torch.from_numpy(topk.astype(np.int64))]
         mq0 = self.mlp3(self.ln(target, "dec_norm"), "mq")              # [300][32]
         encm = (mq0 @ mflat).contiguous()                                # [300][40000]
-        refu = torch.from_numpy(self.o.mask_box(encm.numpy()[None])[0])
+        refu = mask_box_t(encm) if f64 else torch.from_numpy(self.o.mask_box(encm.numpy()[None])[0])
         ref = torch.sigmoid(refu)
         x = target
         for i in range(6):
@@ -209,9 +283,14 @@ class RefModel:
             value = self.lin(source, d + ".ca.vp")
             offs = self.lin(z, d + ".ca.so")
             aw = self.lin(z, d + ".ca.aw")
-            ca = torch.from_numpy(self.o.msdeform(
-                np.ascontiguousarray(value.numpy())[None], np.ascontiguousarray(offs.numpy())[None],
-                np.ascontiguousarray(aw.numpy())[None], np.ascontiguousarray(ref.numpy())[None])[0])
+            if f64:
+                ca = msdeform_t(value, offs, aw, ref)
+            else:
+                ca = torch.from_numpy(self.o.msdeform(
+                    np.ascontiguousarray(value.numpy())[None],
+                    np.ascontiguousarray(offs.numpy())[None],
+                    np.ascontiguousarray(aw.numpy())[None],
+                    np.ascontiguousarray(ref.numpy())[None])[0])
             x = self.ln(x + self.lin(ca, d + ".ca.op"), d + ".ln2")
             ff = self.lin(torch.relu(self.lin(x, d + ".fc1")), d + ".fc2")
             x = self.ln(x + ff, d + ".ln3")

@@ -47,9 +47,12 @@ __device__ int g_tc_error = 0;
 namespace {
 
 constexpr int kBM = 128, kBK = 32;
-constexpr int kThreads = 320;
-constexpr int kWarpProducer = 8, kWarpMma = 9;
-constexpr int kConvThreads = 128;
+// warps 0-3 and 8-11 epilogue, 4-5 converter, 6 TMA producer, 7 MMA issuer
+constexpr int kThreads = 384;
+constexpr int kWarpProducer = 6, kWarpMma = 7, kWarpEpi2 = 8;
+constexpr int kConvThreads = 64;
+constexpr int kEpiThreads = 256;
+constexpr int kHalfCols = 64;  // columns of the N tile per epilogue warp
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kTimeoutCycles = 4000000000LL;
 constexpr int kMaxStages = 4;
@@ -58,7 +61,7 @@ constexpr int kABytes = kBM * kBK * 4;  // 16 KB
 // 16 MMA adds each) and cross-term accumulators X0 | X1 (hi*lo + lo*hi of a
 // whole tile; they are ~2^-11 of the result, so their own accumulation error
 // is negligible).  The running total lives in epilogue registers.
-constexpr int kChunkKB = 4;
+constexpr int kChunkKB = 1;
 constexpr int kSlots = 2;
 constexpr int kSlotCols = 128;
 constexpr int kXCol = 256;
@@ -163,6 +166,33 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+        "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -206,11 +236,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         for (int i = 0; i < kSlots; i++) {
             mbar_init(bar_pfull + 8 * i, 1);
-            mbar_init(bar_pempty + 8 * i, 128);
+            mbar_init(bar_pempty + 8 * i, kEpiThreads);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(bar_xfull + 8 * i, 1);
-            mbar_init(bar_xempty + 8 * i, 128);
+            mbar_init(bar_xempty + 8 * i, kEpiThreads);
         }
         mbar_init(bar_done, 1);
         *abort_flag = 0;
@@ -268,7 +298,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 mbar_wait(bar_full + 8 * s, (uint32_t)((j / S) & 1), (volatile int *)&dummy);
             }
         }
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= 4 && warp < kWarpProducer) {
         // converter: in-place 3xTF32 split of the A tile
         const int ct = threadIdx.x - 128;
         long long it = 0;
@@ -363,13 +393,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             int dummy = 0;
             mbar_wait(bar_done, 0, (volatile int *)&dummy);
         }
-    } else if (warp < 4) {
-        // epilogue: fold every partial into a running FP32 total held in
-        // registers (one row of bn <= 128 columns per thread), finish the tile
+    } else if (warp < 4 || warp >= kWarpEpi2) {
+        // epilogue, 8 warps: two per TMEM lane quadrant (warp % 4), each
+        // owning 64 of the bn <= 128 columns.  Every partial is folded into a
+        // running FP32 total held in registers; the tile's cross terms are
+        // added last and the total goes back into the X slot, from where a
+        // compact 16-column loop applies bias / residual / activation and
+        // stores (a small loop body keeps the instruction cache warm for the
+        // other roles).
         const TcEpilogue &e = a.epi;
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        const int quad = warp & 3;
+        const int c_lo = warp >= kWarpEpi2 ? kHalfCols : 0;
+        const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const int nchunks = (kblocks + kChunkKB - 1) / kChunkKB;
-        float tot[kMaxBN];
+        float tot[kHalfCols];
         long long ctr = 0;
         int tcnt = 0;
         bool ok = true;
@@ -377,7 +414,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int z = t / (a.m_tiles * a.n_tiles);
             const int r = t - z * a.m_tiles * a.n_tiles;
             const int m0 = (r / a.n_tiles) * kBM, n0 = (r % a.n_tiles) * a.bn;
-            const int m = m0 + warp * 32 + lane;
+            const int m = m0 + quad * 32 + lane;
             float *C = e.C + (long long)z * e.c_bs;
             const float *R = e.res_mode ? e.res + (long long)z * e.res_bs : nullptr;
             for (int c = 0; c < nchunks; c++, ctr++) {
@@ -388,46 +425,46 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     break;
                 }
                 tc_fence_after();
-                const uint32_t part = tmem_base + lane_base + (uint32_t)(p * kSlotCols);
+                const uint32_t part = tmem_base + lane_base + (uint32_t)(p * kSlotCols + c_lo);
 #pragma unroll
-                for (int q = 0; q < kMaxBN / 16; q++) {
-                    if (q * 16 < a.bn) {
-                        uint32_t v[16];
-                        tmem_ld16(part + (uint32_t)(q * 16), v);
+                for (int q = 0; q < kHalfCols / 32; q++) {
+                    if (c_lo + q * 32 < a.bn) {
+                        uint32_t v[32];
+                        tmem_ld32(part + (uint32_t)(q * 32), v);
 #pragma unroll
-                        for (int j = 0; j < 16; j++)
-                            tot[q * 16 + j] = c == 0 ? __uint_as_float(v[j])
-                                                     : tot[q * 16 + j] + __uint_as_float(v[j]);
+                        for (int j = 0; j < 32; j++)
+                            tot[q * 32 + j] = c == 0 ? __uint_as_float(v[j])
+                                                     : tot[q * 32 + j] + __uint_as_float(v[j]);
                     }
                 }
                 tc_fence_before();
                 mbar_arrive(bar_pempty + 8 * p);
             }
             if (!ok) break;
-            // the cross terms of the whole tile, then the total goes back into
-            // the tile's X slot so the store loop can walk it 16 columns at a
-            // time (a compact loop instead of a 128-column unrolled body)
             const int xs = tcnt & 1;
             if (!mbar_wait(bar_xfull + 8 * xs, (uint32_t)((tcnt >> 1) & 1), abort_flag)) break;
             tc_fence_after();
-            const uint32_t xa = tmem_base + lane_base + (uint32_t)(kXCol + xs * kSlotCols);
+            const uint32_t xa = tmem_base + lane_base + (uint32_t)(kXCol + xs * kSlotCols + c_lo);
 #pragma unroll
-            for (int q = 0; q < kMaxBN / 16; q++) {
-                if (q * 16 < a.bn) {
-                    uint32_t v[16];
-                    tmem_ld16(xa + (uint32_t)(q * 16), v);
+            for (int q = 0; q < kHalfCols / 32; q++) {
+                if (c_lo + q * 32 < a.bn) {
+                    uint32_t v[32];
+                    tmem_ld32(xa + (uint32_t)(q * 32), v);
 #pragma unroll
-                    for (int j = 0; j < 16; j++)
-                        v[j] = __float_as_uint(tot[q * 16 + j] + __uint_as_float(v[j]));
-                    tmem_st16(xa + (uint32_t)(q * 16), v);
+                    for (int j = 0; j < 32; j++)
+                        v[j] = __float_as_uint(tot[q * 32 + j] + __uint_as_float(v[j]));
+                    tmem_st32(xa + (uint32_t)(q * 32), v);
                 }
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             const bool row_ok = m < a.M;
             float *Crow = C + (long long)m * e.ldc_m;
             const float *Rrow = R ? R + (long long)m * e.res_ldm : nullptr;
+            const int c_hi = a.bn < c_lo + kHalfCols ? a.bn : c_lo + kHalfCols;
+            const uint32_t xt = tmem_base + lane_base + (uint32_t)(kXCol + xs * kSlotCols);
 #pragma unroll 1
-            for (int c0 = 0; c0 < a.bn; c0 += 16) {
+            for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+                const uint32_t xa = xt;
                 uint32_t v[16];
                 tmem_ld16(xa + (uint32_t)c0, v);
                 if (!row_ok) continue;
