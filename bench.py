@@ -388,7 +388,7 @@ def run_forward(args, world, rank, local, pg):
     import synth
     dev = torch.device(f"cuda:{local}")
     torch.cuda.set_device(dev)
-    B = FWD_B
+    B = args.pages or FWD_B
     gguf = synth.cached_gguf(0)
     ctx = ppdl.Context(gguf, device=local, max_batch=B)
     pages = _fwd_pages(rank, B)
@@ -426,6 +426,14 @@ def run_forward(args, world, rank, local, pg):
 
     # per-step device profile of one eager forward (kernel classes, roofline)
     steps = ctx.profile_steps(B)
+    top = []
+    for name, kind, ms, fl, by in sorted(steps, key=lambda s: -s[2])[:12]:
+        e = {"step": name, "kind": kind, "ms": round(ms, 4)}
+        if kind in GEMM_KINDS and ms > 0:
+            e["tflops"] = round(fl * B / (ms / 1e3) / 1e12, 1)
+        elif ms > 0:
+            e["gbs"] = round(by * B / (ms / 1e3) / 1e9, 1)
+        top.append(e)
     hbm, bf16, peak_kind = _peaks()
     tc = bf16 / 6.0  # 3xTF32: three TF32 products at half the BF16 rate
     stages = stage_summary(steps, B, hbm, tc)
@@ -489,6 +497,7 @@ def run_forward(args, world, rank, local, pg):
         if conv_ms else None,
         "msda_gbs": stages.get("msda", {}).get("gbs"),
         "stages": stages,
+        "top_steps": top,
         "profile_ms_per_step": round(prof_ms, 3),
         "roofline": roof,
         "e2e": {"value": round(e2e_val, 2), "unit": "pages/s", "h2d_bytes_per_step": h2d,
@@ -588,6 +597,9 @@ def main():
     ap.add_argument("--workload", default="forward", choices=["forward", "msda"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pages", type=int, default=0,
+                    help="pages per GPU per step of the forward workload (default 8, config 3); "
+                         "smaller values are for profiler captures")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -468,6 +468,29 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 uint32_t v[16];
                 tmem_ld16(xa + (uint32_t)c0, v);
                 if (!row_ok) continue;
+                // row-major output (token-major linears): each thread owns a
+                // row, so 16 consecutive columns go out as four 16-byte stores
+                float *cp = Crow + (n0 + c0);
+                if (e.ldc_n == 1 && n0 + c0 + 16 <= a.N && ((uintptr_t)cp & 15) == 0 &&
+                    (e.res_mode == 0 || e.res_ldn == 1)) {
+                    float y[16];
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int n = n0 + c0 + j;
+                        float x = __uint_as_float(v[j]);
+                        if (e.alpha != 1.0f) x = x * e.alpha;
+                        if (e.bias) x = x + __ldg(e.bias + n);
+                        if (e.res_mode == 1) x = x + Rrow[n];
+                        x = act_apply(x, ACT);
+                        if (e.res_mode == 2) x = x + Rrow[n];
+                        y[j] = x;
+                    }
+                    float4 *c4 = reinterpret_cast<float4 *>(cp);
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        c4[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
                     const int n = n0 + c0 + j;
