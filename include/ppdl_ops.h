@@ -111,6 +111,23 @@ PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float * 
                                   long long ldc_m, long long ldc_n, long long c_bs,
                                   void * stream);
 
+/* No counterpart in the reference.  ppdl_gemm_tf32x3 for callers that
+   cannot allocate device memory — e.g. a ggml custom-op hook, which runs
+   inside ggml's graph compute where ggml's allocator owns every buffer and
+   the node sees only its own tensors.  Same arguments and result as
+   ppdl_gemm_tf32x3 minus b_split: the TF32 halves of B go to a workspace
+   that is a file-scope device array of this library (16 MiB on every device
+   that loads it, kept until the process exits), so N*K may be at most
+   2097152 (larger -> PPDL_ERR_SHAPE).  Nothing is allocated.  The first call
+   on a device resolves the array's address for that device; make it before
+   any stream capture on the device.  All calls share the array: calls whose
+   GPU work overlaps in time race on it and must be serialised by the caller. */
+PPDL_OPS_API int ppdl_gemm_tf32x3_static(int M, int N, int K, int batch, const float * A,
+                                         int a_m_major, long long lda, long long a_bs,
+                                         const float * B, float * C,
+                                         long long ldc_m, long long ldc_n, long long c_bs,
+                                         void * stream);
+
 /* Human-readable text of the last error of ppdl_op_launch on this thread. */
 PPDL_OPS_API const char * ppdl_op_last_error(void);
 

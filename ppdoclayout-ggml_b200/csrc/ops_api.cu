@@ -50,6 +50,11 @@ bool provided(int id) {
 
 }  // namespace
 
+namespace ppdl {
+// Lets other entry points of this library report through ppdl_op_last_error.
+void set_op_error(const char *msg) { snprintf(g_err, sizeof g_err, "%s", msg); }
+}  // namespace ppdl
+
 extern "C" {
 
 PPDL_OPS_API int ppdl_op_supported(const ppdl_op_desc *d) {
