@@ -111,6 +111,26 @@ PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float * 
                                   long long ldc_m, long long ldc_n, long long c_bs,
                                   void * stream);
 
+/* Extension (no single counterpart: the reference's conv dispatcher,
+   builder::conv at src/ppdoclayout.cpp:388-543, lowers k3-s2 and k2 convs
+   to im2col + cuBLAS SGEMM and 1x1 convs to op 3): a direct convolution on
+   the FP32-faithful tensor-core GEMM, the A tile gathered from the CHW
+   input inside the kernel (no im2col buffer).
+     y[z][oc][oy][ox] = act(bias[oc] + sum_{ic,kh,kw} weight[oc][ic][kh][kw]
+                          * x[z][ic][oy*S + kh - P][ox*S + kw - P])
+   with zero outside H x W (padding P at the top/left; the bottom/right
+   padding follows from OH/OW, as for the stem's k2 convs with padding
+   (0, 1); the last window of each axis must start inside the input,
+   (OH-1)*S - P < H).  x: pages of dense [IC][H][W] at stride x_bs;
+   y: pages of [OC][OH][OW] at stride y_bs; bias may be NULL; act 0/1/2/3 =
+   none/ReLU/SiLU/GELU.  b_split: device workspace of 2*OC*round_up(IC*K*K, 4)
+   floats, 16-byte aligned.  K 1..8 with P < K; K = 1 needs S = 1, P = 0.
+   Returns PPDL_OK / PPDL_ERR_SHAPE / PPDL_ERR_CUDA. */
+PPDL_OPS_API int ppdl_conv2d_tf32x3(const float * x, int batch, int IC, int H, int W,
+                                    long long x_bs, const float * weight, const float * bias,
+                                    int OC, int K, int S, int P, int OH, int OW, int act,
+                                    float * b_split, float * y, long long y_bs, void * stream);
+
 /* No counterpart in the reference.  ppdl_gemm_tf32x3 for callers that
    cannot allocate device memory — e.g. a ggml custom-op hook, which runs
    inside ggml's graph compute where ggml's allocator owns every buffer and

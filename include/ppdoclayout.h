@@ -124,7 +124,8 @@ PPDL_API int ppdl_dump(ppdl_ctx * ctx, const char * dir);
 /* reference :58-62 (src/ppdoclayout.cpp:1215-1223): <pfx>logits.bin (300x25),
    <pfx>boxes.bin (300x4 sigmoid cxcywh), <pfx>order.bin (300x300,
    [j + 300 i] = q_i . k_j / 8), <pfx>sel.bin (300 i32 flat q*25+c) of page 0
-   of the last call. */
+   of the last call.  Extension: <pfx>topk.bin (300 i32), the encoder tokens
+   chosen as decoder queries, in query order (op_topk300's output). */
 PPDL_API int ppdl_dump_raw(ppdl_ctx * ctx, const char * pfx);
 
 /* reference :64 (src/ppdoclayout.cpp:1225-1236) */

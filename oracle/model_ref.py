@@ -307,6 +307,7 @@ class RefModel:
             "boxes": ref.numpy().astype(np.float32),
             "order": np.ascontiguousarray(order.numpy().astype(np.float32)).reshape(-1),
             "topk": topk,
+            "enc_max": ecls.max(1).values.double().numpy(),
             "init_ref_unact": refu.numpy(),
         }
         if want_masks:

@@ -9,26 +9,32 @@
 // hi_A*hi_B + hi_A*lo_B + lo_A*hi_B in FP32 — the classic 3xTF32 scheme,
 // ~2^-21 relative per product, inside the hot path's 1e-5 gate.
 //
-// Kernel structure (persistent, one CTA per SM, 320 threads):
-//   warp 8      TMA producer: A tile (FP32 activation) + B hi/lo tiles
-//               (weights pre-split at init) into a stage of shared memory;
-//   warps 4-7   converter: split the A tile in place (hi over the raw
-//               values, lo into a twin buffer with the same layout), then
-//               fence.proxy.async so the tensor core sees the writes;
-//   warp 9      MMA issuer: one thread issues tcgen05.mma kind::tf32
-//               (M=128, N=bn, K=8) x3 per K step into a TMEM accumulator,
-//               tcgen05.commit frees the stage / publishes the tile;
-//   warps 0-3   epilogue: tcgen05.ld 32x32b from the lane quadrant of
-//               their warp, bias / residual / activation, global stores.
-// Two TMEM accumulators (2 x 256 columns) overlap a tile's epilogue with
-// the next tile's main loop.
+// Kernel structure (persistent, one CTA per SM, 384 threads):
+//   warp 6       TMA producer: A tile (FP32 activation) + B hi/lo tiles
+//                (weights pre-split at init) into a stage of shared memory;
+//   warps 4-5    converter: split the A tile in place (hi over the raw
+//                values, lo into a twin buffer with the same layout), then
+//                fence.proxy.async so the tensor core sees the writes — or,
+//                in gather mode, build the A tile from a CHW conv input
+//                (implicit GEMM, any plane stride) instead of TMA;
+//   warp 7       MMA issuer: one thread issues tcgen05.mma kind::tf32
+//                (M=128, N=bn, K=8) x3 per K step into TMEM,
+//                tcgen05.commit frees the stage / publishes the partials;
+//   warps 0-3,   epilogue: tcgen05.ld 32x32b from the lane quadrant of
+//   8-11         their warp, FP32 folding of the partials, bias / residual /
+//                activation; CHW outputs leave through shared-memory boxes
+//                and TMA stores (asynchronous, clipped at the tensor edges),
+//                other layouts through direct global stores.
+// Double-buffered TMEM slots overlap a tile's epilogue with the next tile's
+// main loop.
 //
 // Layouts: A is either M-major — a CHW activation, pixels contiguous — read
 // by TMA boxes of 32 pixels x 32 channels with the 128-byte swizzle on a
 // 32-byte atom (the one M-major form UMMA accepts for TF32; descriptor
-// layout type 1), or K-major (token-major rows, 128-byte swizzle).  B is
-// K-major [N][K] with the 128-byte swizzle.  The element-wise split does not
-// depend on the swizzle, so it runs in place on the TMA image.
+// layout type 1), or K-major (token-major rows or the gathered conv tile,
+// 128-byte swizzle).  B is K-major [N][K] with the 128-byte swizzle.  The
+// element-wise split does not depend on the swizzle, so it runs in place on
+// the TMA image.
 //
 // Every mbarrier wait is bounded (~2 s of clock64); on expiry the kernel
 // raises a device error flag, all roles drain out, pending TMA and MMA work
@@ -67,9 +73,25 @@ constexpr int kSlotCols = 128;
 constexpr int kXCol = 256;
 constexpr int kMaxBN = 128;
 
+// Epilogue staging for TMA stores of CHW outputs: per epilogue warp two
+// boxes of 32 pixels x 16 channels (2 KB each).
+constexpr int kBoxN = 16;
+constexpr int kBoxBytes = 32 * kBoxN * 4;
+constexpr int kStagingBytes = 8 * 2 * kBoxBytes;  // 32 KB
+constexpr int kCtrlBytes = 2048;                 // control block + 1024-alignment slack
+constexpr int kSmemMax = 227 * 1024;
+
+// Registers per thread: at launch (the __launch_bounds__(384, 1) maximum,
+// checked on the host before every launch) and after the setmaxnreg split.
+constexpr int kLaunchRegs = 168, kRegsIssue = 88, kRegsEpi = 208;
+static_assert(128 * kRegsIssue + 256 * kRegsEpi <= kThreads * kLaunchRegs,
+              "register split exceeds the block's register pool");
+
 struct Args {
     int M, N, K, batch, planes, a_mn, bn, stages, m_tiles, n_tiles, tiles;
+    int gather, tma_c;
     uint32_t stage_bytes, tx_bytes, idesc;
+    TcGather gg;
     TcEpilogue epi;
 };
 
@@ -100,7 +122,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 // Bounded wait: false when the phase did not complete within the time limit
 // or another role already aborted.
-__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     for (uint32_t i = 1;; i++) {
@@ -123,6 +145,28 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *tm,
         " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(x), "r"(y), "r"(z)
         : "memory");
+}
+
+// TMA store of a shared-memory box into the tensor (async proxy; the box
+// must be published with fence.proxy.async first).  Coordinates are never
+// negative here; parts of the box outside the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *tm, uint32_t src, int x, int y,
+                                             int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(tm)),
+        "r"(src), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// at most one committed store group may still be reading shared memory
+__device__ __forceinline__ void bulk_wait_read_1() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
@@ -166,6 +210,47 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// 64 columns of the warp's lane quadrant, loaded and waited for in one
+// statement (the wait and the register outputs cannot be separated)
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+        "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+        "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+        "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63 "
+        "}, [%64];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&r)[64]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {"
+        "%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, "
+        "%33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, "
+        "%49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64 "
+        "};"
+        ::"r"(taddr),
+          "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+          "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+          "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]),
+          "r"(r[32]), "r"(r[33]), "r"(r[34]), "r"(r[35]), "r"(r[36]), "r"(r[37]), "r"(r[38]), "r"(r[39]),
+          "r"(r[40]), "r"(r[41]), "r"(r[42]), "r"(r[43]), "r"(r[44]), "r"(r[45]), "r"(r[46]), "r"(r[47]),
+          "r"(r[48]), "r"(r[49]), "r"(r[50]), "r"(r[51]), "r"(r[52]), "r"(r[53]), "r"(r[54]), "r"(r[55]),
+          "r"(r[56]), "r"(r[57]), "r"(r[58]), "r"(r[59]), "r"(r[60]), "r"(r[61]), "r"(r[62]), "r"(r[63])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -208,10 +293,99 @@ __device__ __forceinline__ float tf32_rna(float x) {
     return __uint_as_float(r);
 }
 
+// Gather mode: one converter thread builds rows ct and ct + 64 of a stage's
+// A tile (pixels m0 + row, k = k0 .. k0 + 31) straight from the CHW input
+// with 4-byte cp.async copies (zero-filled outside the image or past K/M),
+// into the K-major 128-byte-swizzled layout (16-byte chunk c of row r at
+// chunk position c ^ (r & 7)); gather_split_rows later splits the same rows
+// in place once the copies have landed.  Lanes run over consecutive pixels,
+// so every copy instruction reads one contiguous (stride S) run of an input
+// row.  oy0/ox0 hold each row's top-left input coordinate (oy*S - P,
+// ox*S - P), oy0 = -64 for rows past M (below any kernel tap, and small
+// enough that oy0 * W cannot overflow).
+__device__ __forceinline__ void cp_async4(uint32_t dst, const float *src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src),
+                 "r"(valid ? 4 : 0)
+                 : "memory");
+}
+
+__device__ __forceinline__ void gather_issue(const TcGather &g, int K, const float *__restrict__ xz,
+                                             uint32_t stage, int ct, const int (&oy0)[2],
+                                             const int (&ox0)[2], int k0) {
+    uint32_t row_dst[2];
+#pragma unroll
+    for (int i = 0; i < 2; i++) row_dst[i] = stage + (uint32_t)(ct + 64 * i) * 128u;
+    const uint32_t sw = (uint32_t)(ct & 7);  // (ct + 64) & 7 == ct & 7
+    if (g.KS == 1) {
+        // pointwise conv: A(m, k) = x[k][m] (S = 1, P = 0)
+#pragma unroll 8
+        for (int j = 0; j < kBK; j++) {
+            const bool kv = k0 + j < K;
+            const float *xc = xz + (long long)(k0 + j) * g.plane;
+            const uint32_t off = ((((uint32_t)j >> 2) ^ sw) << 4) + ((uint32_t)j & 3u) * 4u;
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const bool in = kv && oy0[i] >= 0;
+                cp_async4(row_dst[i] + off, in ? xc + (oy0[i] * g.W + ox0[i]) : xz, in);
+            }
+        }
+    } else {
+        const int kk2 = g.KS * g.KS;
+        int ic = k0 / kk2;
+        const int tap = k0 - ic * kk2;
+        int kh = tap / g.KS;
+        int kw = tap - kh * g.KS;
+#pragma unroll 8
+        for (int j = 0; j < kBK; j++) {
+            const bool kv = k0 + j < K;
+            const float *xc = xz + (long long)ic * g.plane + kh * g.W + kw;
+            const uint32_t off = ((((uint32_t)j >> 2) ^ sw) << 4) + ((uint32_t)j & 3u) * 4u;
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int iy = oy0[i] + kh, ix = ox0[i] + kw;
+                const bool in = kv && (unsigned)iy < (unsigned)g.H && (unsigned)ix < (unsigned)g.W;
+                cp_async4(row_dst[i] + off, in ? xc + (oy0[i] * g.W + ox0[i]) : xz, in);
+            }
+            if (++kw == g.KS) {
+                kw = 0;
+                if (++kh == g.KS) {
+                    kh = 0;
+                    ++ic;
+                }
+            }
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// In-place 3xTF32 split of this thread's two gathered rows (hi over the
+// raw values, lo into the twin buffer), then publish them to the async proxy.
+__device__ __forceinline__ void gather_split_rows(uint8_t *stage, int ct) {
+    float4 *hi = reinterpret_cast<float4 *>(stage);
+    float4 *lo = hi + kABytes / 16;
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int r = ct + 64 * i;
+#pragma unroll
+        for (int c = 0; c < kBK / 4; c++) {
+            const int idx = r * (kBK / 4) + c;
+            const float4 v = hi[idx];
+            float4 h, l;
+            h.x = tf32_rna(v.x); h.y = tf32_rna(v.y);
+            h.z = tf32_rna(v.z); h.w = tf32_rna(v.w);
+            l.x = v.x - h.x; l.y = v.y - h.y; l.z = v.z - h.z; l.w = v.w - h.w;
+            hi[idx] = h;
+            lo[idx] = l;
+        }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 template <int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBhi,
-               const __grid_constant__ CUtensorMap tmBlo, const Args a) {
+               const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmC,
+               const __grid_constant__ Args a) {
     extern __shared__ uint8_t smem_raw[];
     // control block: 16 mbarriers + tmem base + abort flag, then 1024-aligned stages
     const uint32_t raw = smem_u32(smem_raw);
@@ -259,15 +433,88 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const uint32_t tmem_base = *tmem_slot;
     const int kblocks = (a.K + kBK - 1) / kBK;
 
-    if (warp == kWarpProducer) {
-        if (lane == 0) {
+    // register split: the producer / converter / MMA warpgroup hands
+    // registers to the two epilogue warpgroups, whose 64-float running
+    // totals would otherwise spill to local memory.  The host launches only
+    // when the kernel holds kLaunchRegs registers per thread, so the block's
+    // pool covers both shares.
+    if (warp >= 4 && warp < 8) {
+        // issue warpgroup: converter (4-5), TMA producer (6), MMA issuer (7)
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsIssue));
+        // parameters in registers (the waits below clobber memory)
+        const int ptiles = a.tiles, pmt = a.m_tiles, pnt = a.n_tiles, pbn = a.bn,
+                  pamn = a.a_mn, pgather = a.gather, pplanes = a.planes;
+        const uint32_t pstage = a.stage_bytes, ptx = a.tx_bytes, pidesc = a.idesc;
+        if (warp == kWarpProducer) {
+            if (lane == 0) {
+                long long it = 0;
+                bool ok = true;
+                for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
+                    const int z = t / (pmt * pnt);
+                    const int r = t - z * pmt * pnt;
+                    const int m0 = (r / pnt) * kBM, n0 = (r % pnt) * pbn;
+                    const int pz = z % pplanes;
+                    for (int kb = 0; kb < kblocks; kb++, it++) {
+                        const int s = (int)(it % S);
+                        const uint32_t ph = (uint32_t)((it / S) & 1);
+                        if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t st = stage0 + s * pstage;
+                        const uint32_t fb = bar_full + 8 * s;
+                        mbar_expect_tx(fb, ptx);
+                        const int k0 = kb * kBK;
+                        if (pgather) {
+                            // A is written by the converter warps
+                        } else if (pamn) {
+    #pragma unroll
+                            for (int i = 0; i < 4; i++)
+                                tma_load_3d(st + i * 4096, &tmA, fb, m0 + 32 * i, k0, z);
+                        } else {
+                            tma_load_3d(st, &tmA, fb, k0, m0, z);
+                        }
+                        tma_load_3d(st + 2 * kABytes, &tmBhi, fb, k0, n0, pz);
+                        tma_load_3d(st + 2 * kABytes + pbn * 128, &tmBlo, fb, k0, n0, pz);
+                    }
+                }
+                // drain: the last issued stages must land before the CTA may exit
+                const long long first = it > S ? it - S : 0;
+                for (long long j = first; j < it; j++) {
+                    const int s = (int)(j % S);
+                    int dummy = 0;
+                    mbar_wait(bar_full + 8 * s, (uint32_t)((j / S) & 1), (volatile int *)&dummy);
+                }
+            }
+        } else if (warp >= 4 && warp < kWarpProducer && pgather) {
+            const TcGather gg = a.gg;
+            const int pK = a.K, pM = a.M;
+            // converter, gather mode: build the A tile of each free stage from
+            // the conv input (the producer loads only B).  The copies of stage
+            // it are in flight while stage it - 1 is split and published.
+            const int ct = threadIdx.x - 128;
             long long it = 0;
+            int prev = -1;
             bool ok = true;
-            for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
-                const int z = t / (a.m_tiles * a.n_tiles);
-                const int r = t - z * a.m_tiles * a.n_tiles;
-                const int m0 = (r / a.n_tiles) * kBM, n0 = (r % a.n_tiles) * a.bn;
-                const int pz = z % a.planes;
+            for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
+                const int z = t / (pmt * pnt);
+                const int r = t - z * pmt * pnt;
+                const int m0 = (r / pnt) * kBM;
+                const float *xz = gg.x + (long long)z * gg.x_bs;
+                int oy0[2], ox0[2];
+    #pragma unroll
+                for (int i = 0; i < 2; i++) {
+                    const int m = m0 + ct + 64 * i;
+                    if (m < pM) {
+                        const int oy = m / gg.OW;
+                        const int ox = m - oy * gg.OW;
+                        oy0[i] = oy * gg.S - gg.P;
+                        ox0[i] = ox * gg.S - gg.P;
+                    } else {
+                        oy0[i] = -64;
+                        ox0[i] = 0;
+                    }
+                }
                 for (int kb = 0; kb < kblocks; kb++, it++) {
                     const int s = (int)(it % S);
                     const uint32_t ph = (uint32_t)((it / S) & 1);
@@ -275,145 +522,156 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         ok = false;
                         break;
                     }
-                    const uint32_t st = stage0 + s * a.stage_bytes;
-                    const uint32_t fb = bar_full + 8 * s;
-                    mbar_expect_tx(fb, a.tx_bytes);
-                    const int k0 = kb * kBK;
-                    if (a.a_mn) {
-#pragma unroll
-                        for (int i = 0; i < 4; i++)
-                            tma_load_3d(st + i * 4096, &tmA, fb, m0 + 32 * i, k0, z);
-                    } else {
-                        tma_load_3d(st, &tmA, fb, k0, m0, z);
+                    gather_issue(gg, pK, xz, stage0 + (uint32_t)s * pstage, ct, oy0, ox0,
+                                 kb * kBK);
+                    if (prev >= 0) {
+                        asm volatile("cp.async.wait_group 1;" ::: "memory");
+                        gather_split_rows(stage0_ptr + (size_t)prev * pstage, ct);
+                        mbar_arrive(bar_conv + 8 * prev);
                     }
-                    tma_load_3d(st + 2 * kABytes, &tmBhi, fb, k0, n0, pz);
-                    tma_load_3d(st + 2 * kABytes + a.bn * 128, &tmBlo, fb, k0, n0, pz);
+                    prev = s;
                 }
             }
-            // drain: the last issued stages must land before the CTA may exit
-            const long long first = it > S ? it - S : 0;
-            for (long long j = first; j < it; j++) {
-                const int s = (int)(j % S);
-                int dummy = 0;
-                mbar_wait(bar_full + 8 * s, (uint32_t)((j / S) & 1), (volatile int *)&dummy);
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            if (ok && prev >= 0) {
+                gather_split_rows(stage0_ptr + (size_t)prev * pstage, ct);
+                mbar_arrive(bar_conv + 8 * prev);
             }
-        }
-    } else if (warp >= 4 && warp < kWarpProducer) {
-        // converter: in-place 3xTF32 split of the A tile
-        const int ct = threadIdx.x - 128;
-        long long it = 0;
-        bool ok = true;
-        for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
-            for (int kb = 0; kb < kblocks; kb++, it++) {
-                const int s = (int)(it % S);
-                const uint32_t ph = (uint32_t)((it / S) & 1);
-                if (!mbar_wait(bar_full + 8 * s, ph, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                float4 *hi = reinterpret_cast<float4 *>(stage0_ptr + (size_t)s * a.stage_bytes);
-                float4 *lo = hi + kABytes / 16;
-#pragma unroll
-                for (int i = 0; i < kABytes / 16 / kConvThreads; i++) {
-                    const int idx = ct + kConvThreads * i;
-                    const float4 v = hi[idx];
-                    float4 h, l;
-                    h.x = tf32_rna(v.x); h.y = tf32_rna(v.y);
-                    h.z = tf32_rna(v.z); h.w = tf32_rna(v.w);
-                    l.x = v.x - h.x; l.y = v.y - h.y; l.z = v.z - h.z; l.w = v.w - h.w;
-                    hi[idx] = h;
-                    lo[idx] = l;
-                }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive(bar_conv + 8 * s);
-            }
-        }
-    } else if (warp == kWarpMma) {
-        // hi*hi products go to a fresh TMEM partial every kChunkKB k-blocks
-        // (two slots, alternating), which the epilogue folds into its running
-        // total with FP32 adds — the tensor core's own accumulation then sums
-        // at most 16 of the large terms; the two small cross products go to
-        // the tile's X slot.
-        if (lane == 0) {
-            long long it = 0, ctr = 0;
-            int tcnt = 0;
+        } else if (warp >= 4 && warp < kWarpProducer) {
+            // converter: in-place 3xTF32 split of the A tile
+            const int ct = threadIdx.x - 128;
+            long long it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x, tcnt++) {
-                const int xs = tcnt & 1;
-                if (!mbar_wait(bar_xempty + 8 * xs, (uint32_t)(((tcnt >> 1) & 1) ^ 1), abort_flag))
-                    break;
-                const uint32_t dx = tmem_base + (uint32_t)(kXCol + xs * kSlotCols);
-                for (int kb0 = 0; kb0 < kblocks && ok; kb0 += kChunkKB, ctr++) {
-                    const int p = (int)(ctr % kSlots);
-                    const uint32_t pph = (uint32_t)((ctr / kSlots) & 1);
-                    if (!mbar_wait(bar_pempty + 8 * p, pph ^ 1, abort_flag)) {
+            for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
+                for (int kb = 0; kb < kblocks; kb++, it++) {
+                    const int s = (int)(it % S);
+                    const uint32_t ph = (uint32_t)((it / S) & 1);
+                    if (!mbar_wait(bar_full + 8 * s, ph, abort_flag)) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                    const uint32_t d = tmem_base + (uint32_t)(p * kSlotCols);
-                    const int kb1 = kb0 + kChunkKB < kblocks ? kb0 + kChunkKB : kblocks;
-                    for (int kb = kb0; kb < kb1; kb++, it++) {
-                        const int s = (int)(it % S);
-                        const uint32_t ph = (uint32_t)((it / S) & 1);
-                        if (!mbar_wait(bar_conv + 8 * s, ph, abort_flag)) {
+                    float4 *hi = reinterpret_cast<float4 *>(stage0_ptr + (size_t)s * pstage);
+                    float4 *lo = hi + kABytes / 16;
+    #pragma unroll
+                    for (int i = 0; i < kABytes / 16 / kConvThreads; i++) {
+                        const int idx = ct + kConvThreads * i;
+                        const float4 v = hi[idx];
+                        float4 h, l;
+                        h.x = tf32_rna(v.x); h.y = tf32_rna(v.y);
+                        h.z = tf32_rna(v.z); h.w = tf32_rna(v.w);
+                        l.x = v.x - h.x; l.y = v.y - h.y; l.z = v.z - h.z; l.w = v.w - h.w;
+                        hi[idx] = h;
+                        lo[idx] = l;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive(bar_conv + 8 * s);
+                }
+            }
+        } else if (warp == kWarpMma) {
+            // hi*hi products go to a fresh TMEM partial every kChunkKB k-blocks
+            // (two slots, alternating), which the epilogue folds into its running
+            // total with FP32 adds — the tensor core's own accumulation then sums
+            // at most 16 of the large terms; the two small cross products go to
+            // the tile's X slot.
+            if (lane == 0) {
+                long long it = 0, ctr = 0;
+                int tcnt = 0;
+                bool ok = true;
+                for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x, tcnt++) {
+                    const int xs = tcnt & 1;
+                    if (!mbar_wait(bar_xempty + 8 * xs, (uint32_t)(((tcnt >> 1) & 1) ^ 1), abort_flag))
+                        break;
+                    const uint32_t dx = tmem_base + (uint32_t)(kXCol + xs * kSlotCols);
+                    for (int kb0 = 0; kb0 < kblocks && ok; kb0 += kChunkKB, ctr++) {
+                        const int p = (int)(ctr % kSlots);
+                        const uint32_t pph = (uint32_t)((ctr / kSlots) & 1);
+                        if (!mbar_wait(bar_pempty + 8 * p, pph ^ 1, abort_flag)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t st = stage0 + s * a.stage_bytes;
-                        const uint32_t ahi = st, alo = st + kABytes;
-                        const uint32_t bhi = st + 2 * kABytes, blo = bhi + a.bn * 128;
-#pragma unroll
-                        for (int kk = 0; kk < kBK / 8; kk++) {
-                            uint64_t dah, dal;
-                            if (a.a_mn) {  // 8 K rows = two 4-row groups of 512 B
-                                dah = smem_desc(ahi + kk * 1024, 4096, 512, 1);
-                                dal = smem_desc(alo + kk * 1024, 4096, 512, 1);
-                            } else {       // 32 bytes of K inside the swizzled 128-byte row
-                                dah = smem_desc(ahi + kk * 32, 16, 1024, 2);
-                                dal = smem_desc(alo + kk * 32, 16, 1024, 2);
+                        const uint32_t d = tmem_base + (uint32_t)(p * kSlotCols);
+                        const int kb1 = kb0 + kChunkKB < kblocks ? kb0 + kChunkKB : kblocks;
+                        for (int kb = kb0; kb < kb1; kb++, it++) {
+                            const int s = (int)(it % S);
+                            const uint32_t ph = (uint32_t)((it / S) & 1);
+                            if (!mbar_wait(bar_conv + 8 * s, ph, abort_flag) ||
+                                (pgather && !mbar_wait(bar_full + 8 * s, ph, abort_flag))) {
+                                ok = false;
+                                break;
                             }
-                            const uint64_t dbh = smem_desc(bhi + kk * 32, 16, 1024, 2);
-                            const uint64_t dbl = smem_desc(blo + kk * 32, 16, 1024, 2);
-                            umma_tf32(d, dah, dbh, a.idesc, (kb == kb0 && kk == 0) ? 0u : 1u);
-                            umma_tf32(dx, dal, dbh, a.idesc, (kb == 0 && kk == 0) ? 0u : 1u);
-                            umma_tf32(dx, dah, dbl, a.idesc, 1u);
+                            tc_fence_after();
+                            const uint32_t st = stage0 + s * pstage;
+                            const uint32_t ahi = st, alo = st + kABytes;
+                            const uint32_t bhi = st + 2 * kABytes, blo = bhi + pbn * 128;
+                            // descriptors of the four K=8 steps: A M-major (8 K rows =
+                            // two 4-row groups of 512 B) or K-major (32 bytes of K
+                            // inside the swizzled 128-byte row); B K-major
+                            auto desc_a = [&](uint32_t base, int kk) {
+                                return pamn ? smem_desc(base + kk * 1024, 4096, 512, 1)
+                                              : smem_desc(base + kk * 32, 16, 1024, 2);
+                            };
+                            // the large hi*hi products first, so that the partial is
+                            // published (and folded by the epilogue) while the
+                            // cross terms still run
+    #pragma unroll
+                            for (int kk = 0; kk < kBK / 8; kk++)
+                                umma_tf32(d, desc_a(ahi, kk), smem_desc(bhi + kk * 32, 16, 1024, 2),
+                                          pidesc, (kb == kb0 && kk == 0) ? 0u : 1u);
+                            if (kb == kb1 - 1) umma_commit(bar_pfull + 8 * p);
+    #pragma unroll
+                            for (int kk = 0; kk < kBK / 8; kk++) {
+                                const uint64_t dah = desc_a(ahi, kk), dal = desc_a(alo, kk);
+                                const uint64_t dbh = smem_desc(bhi + kk * 32, 16, 1024, 2);
+                                const uint64_t dbl = smem_desc(blo + kk * 32, 16, 1024, 2);
+                                umma_tf32(dx, dal, dbh, pidesc, (kb == 0 && kk == 0) ? 0u : 1u);
+                                umma_tf32(dx, dah, dbl, pidesc, 1u);
+                            }
+                            umma_commit(bar_empty + 8 * s);
                         }
-                        umma_commit(bar_empty + 8 * s);
+                        if (!ok) break;
                     }
                     if (!ok) break;
-                    umma_commit(bar_pfull + 8 * p);
+                    umma_commit(bar_xfull + 8 * xs);
                 }
-                if (!ok) break;
-                umma_commit(bar_xfull + 8 * xs);
+                // all issued MMAs must finish before TMEM is released
+                umma_commit(bar_done);
+                int dummy = 0;
+                mbar_wait(bar_done, 0, (volatile int *)&dummy);
             }
-            // all issued MMAs must finish before TMEM is released
-            umma_commit(bar_done);
-            int dummy = 0;
-            mbar_wait(bar_done, 0, (volatile int *)&dummy);
         }
-    } else if (warp < 4 || warp >= kWarpEpi2) {
+    } else {
+        // epilogue warpgroups (warps 0-3, 8-11)
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpi));
         // epilogue, 8 warps: two per TMEM lane quadrant (warp % 4), each
         // owning 64 of the bn <= 128 columns.  Every partial is folded into a
         // running FP32 total held in registers; the tile's cross terms are
         // added last and the total goes back into the X slot, from where a
         // compact 16-column loop applies bias / residual / activation and
         // stores (a small loop body keeps the instruction cache warm for the
-        // other roles).
-        const TcEpilogue &e = a.epi;
+        // other roles): CHW outputs through shared-memory boxes and TMA
+        // stores, other layouts with direct global stores.
+        // parameters in registers: every TMEM wait carries a memory clobber,
+        // after which fields read through the parameter block would be
+        // fetched again
+        const TcEpilogue e = a.epi;
+        const int pM = a.M, pN = a.N, pbn = a.bn, ptiles = a.tiles, pmt = a.m_tiles,
+                  pnt = a.n_tiles, ptma = a.tma_c;
         const int quad = warp & 3;
         const int c_lo = warp >= kWarpEpi2 ? kHalfCols : 0;
+        const int ew = warp < 4 ? warp : warp - 4;  // epilogue warp 0..7
+        const uint32_t staging = stage0 + (uint32_t)S * a.stage_bytes;
+        float *staging_ptr = reinterpret_cast<float *>(stage0_ptr + (size_t)S * a.stage_bytes);
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const int nchunks = (kblocks + kChunkKB - 1) / kChunkKB;
         float tot[kHalfCols];
         long long ctr = 0;
-        int tcnt = 0;
+        int tcnt = 0, nbox = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x, tcnt++) {
-            const int z = t / (a.m_tiles * a.n_tiles);
-            const int r = t - z * a.m_tiles * a.n_tiles;
-            const int m0 = (r / a.n_tiles) * kBM, n0 = (r % a.n_tiles) * a.bn;
+        for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x, tcnt++) {
+            const int z = t / (pmt * pnt);
+            const int r = t - z * pmt * pnt;
+            const int m0 = (r / pnt) * kBM, n0 = (r % pnt) * pbn;
             const int m = m0 + quad * 32 + lane;
             float *C = e.C + (long long)z * e.c_bs;
             const float *R = e.res_mode ? e.res + (long long)z * e.res_bs : nullptr;
@@ -428,7 +686,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const uint32_t part = tmem_base + lane_base + (uint32_t)(p * kSlotCols + c_lo);
 #pragma unroll
                 for (int q = 0; q < kHalfCols / 32; q++) {
-                    if (c_lo + q * 32 < a.bn) {
+                    if (c_lo + q * 32 < pbn) {
                         uint32_t v[32];
                         tmem_ld32(part + (uint32_t)(q * 32), v);
 #pragma unroll
@@ -447,7 +705,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const uint32_t xa = tmem_base + lane_base + (uint32_t)(kXCol + xs * kSlotCols + c_lo);
 #pragma unroll
             for (int q = 0; q < kHalfCols / 32; q++) {
-                if (c_lo + q * 32 < a.bn) {
+                if (c_lo + q * 32 < pbn) {
                     uint32_t v[32];
                     tmem_ld32(xa + (uint32_t)(q * 32), v);
 #pragma unroll
@@ -457,21 +715,57 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-            const bool row_ok = m < a.M;
+            const bool row_ok = m < pM;
             float *Crow = C + (long long)m * e.ldc_m;
             const float *Rrow = R ? R + (long long)m * e.res_ldm : nullptr;
-            const int c_hi = a.bn < c_lo + kHalfCols ? a.bn : c_lo + kHalfCols;
+            const int c_hi = pbn < c_lo + kHalfCols ? pbn : c_lo + kHalfCols;
             const uint32_t xt = tmem_base + lane_base + (uint32_t)(kXCol + xs * kSlotCols);
 #pragma unroll 1
             for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
                 const uint32_t xa = xt;
                 uint32_t v[16];
                 tmem_ld16(xa + (uint32_t)c0, v);
+                if (ptma) {
+                    // CHW output: the warp's 32 pixels x 16 channels go into a
+                    // staging box (lane = pixel, conflict-free rows of 128 B)
+                    // and out with one TMA store, which clips rows >= M and
+                    // channels >= N.  Two boxes per warp alternate.
+                    const int b = nbox & 1;
+                    if (nbox >= 2) {
+                        if (lane == 0) bulk_wait_read_1();
+                        __syncwarp();
+                    }
+                    float *box = staging_ptr + (size_t)(ew * 2 + b) * (kBoxBytes / 4);
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int n = n0 + c0 + j;
+                        const bool ok_n = n < pN;
+                        float x = __uint_as_float(v[j]);
+                        if (e.alpha != 1.0f) x = x * e.alpha;
+                        if (e.bias && ok_n) x = x + __ldg(e.bias + n);
+                        if (e.res_mode == 1 && ok_n && row_ok) x = x + Rrow[(long long)n * e.res_ldn];
+                        x = act_apply(x, ACT);
+                        if (e.res_mode == 2 && ok_n && row_ok) x = x + Rrow[(long long)n * e.res_ldn];
+                        box[j * 32 + lane] = x;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        // boxes wholly past the tensor edge are skipped; the
+                        // group is committed regardless to keep the count
+                        if (m0 + quad * 32 < pM && n0 + c0 < pN)
+                            tma_store_3d(&tmC, staging + (uint32_t)((ew * 2 + b) * kBoxBytes),
+                                         m0 + quad * 32, n0 + c0, z);
+                        bulk_commit();
+                    }
+                    nbox++;
+                    continue;
+                }
                 if (!row_ok) continue;
                 // row-major output (token-major linears): each thread owns a
                 // row, so 16 consecutive columns go out as four 16-byte stores
                 float *cp = Crow + (n0 + c0);
-                if (e.ldc_n == 1 && n0 + c0 + 16 <= a.N && ((uintptr_t)cp & 15) == 0 &&
+                if (e.ldc_n == 1 && n0 + c0 + 16 <= pN && ((uintptr_t)cp & 15) == 0 &&
                     (e.res_mode == 0 || e.res_ldn == 1)) {
                     float y[16];
 #pragma unroll
@@ -494,7 +788,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
                     const int n = n0 + c0 + j;
-                    if (n < a.N) {
+                    if (n < pN) {
                         float x = __uint_as_float(v[j]);
                         if (e.alpha != 1.0f) x = x * e.alpha;
                         if (e.bias) x = x + __ldg(e.bias + n);
@@ -508,6 +802,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             tc_fence_before();
             mbar_arrive(bar_xempty + 8 * xs);
         }
+        // the staging boxes must be read and the stores complete before exit
+        if (ptma && lane == 0) bulk_wait_all();
     }
 
     tc_fence_before();
@@ -525,6 +821,17 @@ __global__ void tf32_split_kernel(const float *__restrict__ w, float *__restrict
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const float v = w[i];
+    const float h = tf32_rna(v);
+    hi[i] = h;
+    lo[i] = v - h;
+}
+
+__global__ void tf32_split_pad_kernel(const float *__restrict__ w, float *__restrict__ hi,
+                                      float *__restrict__ lo, int rows, int K, int Kp) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * Kp) return;
+    const int n = (int)(i / Kp), k = (int)(i - (long long)n * Kp);
+    const float v = k < K ? w[(long long)n * K + k] : 0.0f;
     const float h = tf32_rna(v);
     hi[i] = h;
     lo[i] = v - h;
@@ -582,35 +889,84 @@ Status launch_tf32_split(const float *w, float *hi, float *lo, long long n, cuda
     return cuda_status();
 }
 
-bool tc_gemm_plan(TcGemm *g, int M, int N, int K, int batch, const float *A, int a_mn,
-                  long long lda, long long a_bs, const float *Bhi, const float *Blo, int planes,
-                  const TcEpilogue &epi) {
+Status launch_tf32_split_pad(const float *w, float *hi, float *lo, int rows, int K, int Kp,
+                             cudaStream_t st) {
+    if (rows <= 0 || K <= 0 || Kp < K) return ERR_SHAPE;
+    const long long n = (long long)rows * Kp;
+    tf32_split_pad_kernel<<<(int)((n + 255) / 256), 256, 0, st>>>(w, hi, lo, rows, K, Kp);
+    return cuda_status();
+}
+
+namespace {
+
+// Tile and stage sizing shared by both planners.
+bool plan_common(TcGemm *g, int M, int N, int K, int batch, int planes, const TcEpilogue &epi) {
     g->ok = false;
     if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || planes <= 0) return false;
-    if (K % 4) return false;  // B rows must be 16-byte multiples
-    // N tile (multiple of 16, <= 160 so that two partial slots and the total
-    // fit in the 512 TMEM columns): least padded columns, then the widest
+    // N tile (multiple of 16, <= 128 so that two partial slots and two
+    // cross-term slots fit in the 512 TMEM columns); cost model: tiles x
+    // (bn + 64), the 64 standing for the per-tile A traffic and epilogue
+    // overhead in column equivalents
     int bn = 16;
     long long best = -1;
     for (int c = 16; c <= kMaxBN; c += 16) {
-        const long long cover = (long long)((N + c - 1) / c) * c;
-        if (best < 0 || cover < best || (cover == best && c > bn)) {
-            best = cover;
+        const long long cost = (long long)((N + c - 1) / c) * (c + 64);
+        if (best < 0 || cost < best || (cost == best && c > bn)) {
+            best = cost;
             bn = c;
         }
     }
     const uint32_t stage_bytes = 2 * kABytes + 2 * 128 * bn;
-    int stages = (int)((220 * 1024 - 2048) / stage_bytes);
+    int stages = (int)((kSmemMax - kCtrlBytes - kStagingBytes) / stage_bytes);
     if (stages > kMaxStages) stages = kMaxStages;
     if (stages < 2) return false;
     g->M = M; g->N = N; g->K = K; g->batch = batch; g->planes = planes;
-    g->a_mn = a_mn; g->bn = bn; g->stages = stages;
-    g->smem = 2048 + (size_t)stages * stage_bytes;
+    g->bn = bn; g->stages = stages;
+    g->smem = kCtrlBytes + (size_t)stages * stage_bytes + kStagingBytes;
     if (g->smem < 120 * 1024) g->smem = 120 * 1024;  // one CTA per SM: TMEM is not shared
     g->m_tiles = (M + kBM - 1) / kBM;
     g->n_tiles = (N + bn - 1) / bn;
     g->tiles = g->m_tiles * g->n_tiles * batch;
     g->epi = epi;
+    return true;
+}
+
+// A CHW output (pixels contiguous) whose channel and page strides are
+// 16-byte multiples is stored by TMA through the staging boxes; any other
+// output keeps the direct global stores.
+void encode_c(TcGemm *g) {
+    const TcEpilogue &e = g->epi;
+    g->tma_c = 0;
+    if (e.ldc_m != 1 || e.ldc_n <= 0 || e.c_bs < 0 || ((uintptr_t)e.C & 15) ||
+        (e.ldc_n * 4) % 16 || (e.c_bs * 4) % 16 || (g->batch > 1 && e.c_bs == 0))
+        return;
+    if (encode3d(&g->tmC, e.C, (uint64_t)g->M, (uint64_t)g->N, (uint64_t)g->batch,
+                 (uint64_t)e.ldc_n * 4, (uint64_t)e.c_bs * 4, 32, kBoxN,
+                 CU_TENSOR_MAP_SWIZZLE_NONE))
+        g->tma_c = 1;
+}
+
+// B hi/lo tensor maps over [planes][N][ldk] halves, k < ldk (16-byte rows).
+bool encode_b(TcGemm *g, const float *Bhi, const float *Blo, int ldk) {
+    const uint64_t N = (uint64_t)g->N;
+    return encode3d(&g->tmBhi, Bhi, (uint64_t)ldk, N, (uint64_t)g->planes, (uint64_t)ldk * 4,
+                    (uint64_t)ldk * N * 4, 32, (uint32_t)g->bn, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode3d(&g->tmBlo, Blo, (uint64_t)ldk, N, (uint64_t)g->planes, (uint64_t)ldk * 4,
+                    (uint64_t)ldk * N * 4, 32, (uint32_t)g->bn, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace
+
+bool tc_gemm_plan(TcGemm *g, int M, int N, int K, int batch, const float *A, int a_mn,
+                  long long lda, long long a_bs, const float *Bhi, const float *Blo, int planes,
+                  const TcEpilogue &epi) {
+    if (K % 4) {  // B rows must be 16-byte multiples
+        g->ok = false;
+        return false;
+    }
+    if (!plan_common(g, M, N, K, batch, planes, epi)) return false;
+    g->a_mn = a_mn;
+    g->gather = 0;
     bool ok;
     if (a_mn)
         ok = encode3d(&g->tmA, A, (uint64_t)M, (uint64_t)K, (uint64_t)batch, (uint64_t)lda * 4,
@@ -618,14 +974,29 @@ bool tc_gemm_plan(TcGemm *g, int M, int N, int K, int batch, const float *A, int
     else
         ok = encode3d(&g->tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)batch, (uint64_t)lda * 4,
                       (uint64_t)a_bs * 4, 32, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
-    ok = ok && encode3d(&g->tmBhi, Bhi, (uint64_t)K, (uint64_t)N, (uint64_t)planes,
-                        (uint64_t)K * 4, (uint64_t)K * N * 4, 32, (uint32_t)bn,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
-    ok = ok && encode3d(&g->tmBlo, Blo, (uint64_t)K, (uint64_t)N, (uint64_t)planes,
-                        (uint64_t)K * 4, (uint64_t)K * N * 4, 32, (uint32_t)bn,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
-    g->ok = ok;
-    return ok;
+    g->ok = ok && encode_b(g, Bhi, Blo, K);
+    if (g->ok) encode_c(g);
+    return g->ok;
+}
+
+bool tc_gemm_plan_gather(TcGemm *g, int M, int N, int K, int batch, const TcGather &gg,
+                         const float *Bhi, const float *Blo, const TcEpilogue &epi) {
+    g->ok = false;
+    // geometry limits of the gather: taps 1..8 (the -64 row sentinel must
+    // stay below every tap), 1x1 only as a plain pointwise conv, int offsets
+    if (!gg.x || gg.KS < 1 || gg.KS > 8 || gg.S < 1 || gg.P < 0 || gg.P >= gg.KS ||
+        gg.H <= 0 || gg.W <= 0 || gg.OW <= 0 || gg.plane <= 0 || M % gg.OW != 0)
+        return false;
+    if (gg.KS == 1 && (gg.S != 1 || gg.P != 0 || gg.OW != gg.W)) return false;
+    if (K % (gg.KS * gg.KS) != 0 || (long long)K / (gg.KS * gg.KS) * gg.plane >= (1LL << 31))
+        return false;
+    if (!plan_common(g, M, N, K, batch, 1, epi)) return false;
+    g->a_mn = 0;  // the gathered tile is K-major
+    g->gather = 1;
+    g->gg = gg;
+    g->ok = encode_b(g, Bhi, Blo, (K + 3) / 4 * 4);
+    if (g->ok) encode_c(g);
+    return g->ok;
 }
 
 Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
@@ -634,24 +1005,29 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr[dev]) {
-        const int smax = 227 * 1024;
-        if (cudaFuncSetAttribute(tc_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 smax) != cudaSuccess ||
-            cudaFuncSetAttribute(tc_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 smax) != cudaSuccess ||
-            cudaFuncSetAttribute(tc_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 smax) != cudaSuccess ||
-            cudaFuncSetAttribute(tc_gemm_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 smax) != cudaSuccess)
-            return ERR_CUDA;
+        const void *fns[4] = {(const void *)tc_gemm_kernel<0>, (const void *)tc_gemm_kernel<1>,
+                              (const void *)tc_gemm_kernel<2>, (const void *)tc_gemm_kernel<3>};
+        for (const void *f : fns) {
+            // the setmaxnreg split needs exactly kLaunchRegs per thread at launch
+            cudaFuncAttributes fa;
+            if (cudaFuncGetAttributes(&fa, f) != cudaSuccess || fa.numRegs != kLaunchRegs ||
+                cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax) != cudaSuccess) {
+                cudaGetLastError();
+                return ERR_CUDA;
+            }
+        }
         attr[dev] = true;
     }
     Args a;
     a.M = g.M; a.N = g.N; a.K = g.K; a.batch = g.batch; a.planes = g.planes;
     a.a_mn = g.a_mn; a.bn = g.bn; a.stages = g.stages;
     a.m_tiles = g.m_tiles; a.n_tiles = g.n_tiles; a.tiles = g.tiles;
+    a.gather = g.gather;
+    a.tma_c = g.tma_c;
+    a.gg = g.gg;
     a.stage_bytes = 2 * kABytes + 2 * 128 * g.bn;
-    a.tx_bytes = kABytes + 2 * 128 * g.bn;
+    a.tx_bytes = (g.gather ? 0 : kABytes) + 2 * 128 * g.bn;
     a.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(g.a_mn ? 1 : 0) << 15) |
               ((uint32_t)(g.bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
     a.epi = g.epi;
@@ -659,16 +1035,20 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     if (grid > g.tiles) grid = g.tiles;
     switch (g.epi.act) {
         case ACT_RELU:
-            tc_gemm_kernel<ACT_RELU><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo, a);
+            tc_gemm_kernel<ACT_RELU><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo,
+                                                                     g.tmC, a);
             break;
         case ACT_SILU:
-            tc_gemm_kernel<ACT_SILU><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo, a);
+            tc_gemm_kernel<ACT_SILU><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo,
+                                                                     g.tmC, a);
             break;
         case ACT_GELU:
-            tc_gemm_kernel<ACT_GELU><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo, a);
+            tc_gemm_kernel<ACT_GELU><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo,
+                                                                     g.tmC, a);
             break;
         default:
-            tc_gemm_kernel<ACT_NONE><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo, a);
+            tc_gemm_kernel<ACT_NONE><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo,
+                                                                     g.tmC, a);
     }
     return cuda_status();
 }

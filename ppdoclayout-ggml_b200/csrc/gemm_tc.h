@@ -27,10 +27,28 @@ struct TcEpilogue {
     float alpha = 1.0f;
 };
 
+// Convolution read directly from a CHW input (implicit GEMM, no im2col):
+// A(m, k) = x[z][ic][oy*S + kh - P][ox*S + kw - P], zero outside H x W,
+// with m = oy*OW + ox and k = (ic*KS + kh)*KS + kw — the row order of the
+// raw conv weight [OC][IC][KS][KS], so B is that weight as [OC][IC*KS*KS].
+// Any plane size and channel stride works (no TMA on A): the converter
+// warps gather the A tile from global memory into the K-major swizzled
+// layout.  Bottom/right-only padding is expressed by OH/OW alone.
+struct TcGather {
+    const float *x = nullptr;
+    long long x_bs = 0;      // page stride (elements)
+    long long plane = 0;     // channel stride (elements), H*W for a dense CHW tensor
+    int KS = 1, S = 1, P = 0, H = 0, W = 0, OW = 0;
+};
+
 struct TcGemm {
     CUtensorMap tmA, tmBhi, tmBlo;
+    CUtensorMap tmC;     // CHW output (ldc_m == 1) stored by TMA when tma_c
+    int tma_c = 0;
     int M = 0, N = 0, K = 0, batch = 1, planes = 1;
     int a_mn = 1;        // 1: A is M-major (128B-base-32B swizzle), 0: K-major
+    int gather = 0;      // 1: A gathered by the converter warps (conv geometry gg)
+    TcGather gg;
     int bn = 128;        // N tile
     int stages = 2;
     size_t smem = 0;
@@ -42,6 +60,17 @@ struct TcGemm {
 // Pre-split a K-major weight [rows][K] into hi (low 13 mantissa bits
 // cleared) and lo = w - hi.
 Status launch_tf32_split(const float *w, float *hi, float *lo, long long n, cudaStream_t st);
+
+// The same for a [rows][K] weight stored into [rows][Kp] halves (Kp >= K,
+// columns K..Kp-1 zero), so that the halves' rows are 16-byte multiples.
+Status launch_tf32_split_pad(const float *w, float *hi, float *lo, int rows, int K, int Kp,
+                             cudaStream_t st);
+
+// Plan a convolution GEMM with a gathered A (see TcGather): M = OH*OW per
+// page, N = OC, K = IC*KS*KS, batch = pages, B hi/lo: [N][Kp] with
+// Kp = round_up(K, 4).  The epilogue addresses C(m = pixel, n = channel).
+bool tc_gemm_plan_gather(TcGemm *g, int M, int N, int K, int batch, const TcGather &gg,
+                         const float *Bhi, const float *Blo, const TcEpilogue &epi);
 
 // Plan a GEMM.  A: base pointer of page 0, a_mn ? (ld = stride of k) :
 // (ld = stride of m); batch stride a_bs (elements).  B hi/lo: [planes][N][K].

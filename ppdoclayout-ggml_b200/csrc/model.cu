@@ -123,6 +123,7 @@ public:
     float *mask_logits = nullptr;
     float *dets = nullptr;
     int32_t *sel = nullptr, *rank = nullptr, *masks = nullptr;
+    int32_t *enc_topk = nullptr;  // encoder top-300 token indices (query order)
 
     ~Model() {
         for (auto &g : graphs) cudaGraphExecDestroy(g.second);
@@ -149,6 +150,40 @@ public:
     }
     static bool tc_shape_ok(const float *p, long long plane, long long bs, int K) {
         return ((uintptr_t)p & 15) == 0 && plane % 4 == 0 && bs % 4 == 0 && K % 4 == 0;
+    }
+    // Tensor-core conv with the A tile gathered from the CHW input (implicit
+    // GEMM; also the 1x1 convs whose planes break the TMA stride rule).
+    // Returns a null plan when the geometry does not fit the gather.
+    std::shared_ptr<TcGemm> plan_conv_gather(const V &x, int OH, int OW, const float *wp, int K,
+                                             int s, int p, int OC, const TcEpilogue &e) {
+        TcGather gg;
+        gg.x = x.p; gg.x_bs = x.bs; gg.plane = x.plane();
+        gg.KS = K; gg.S = s; gg.P = p; gg.H = x.H; gg.W = x.W; gg.OW = OW;
+        const int Kc = x.C * K * K, Kp = (Kc + 3) / 4 * 4;
+        auto g = std::make_shared<TcGemm>();
+        // probe the geometry first (B pointers only enter the tensor maps)
+        if (!ok || !tc_gemm_plan_gather(g.get(), OH * OW, OC, Kc, Bmax, gg, wp, wp, e))
+            return nullptr;
+        float *hi = dalloc((long long)OC * Kp), *lo = dalloc((long long)OC * Kp);
+        if (!ok) return nullptr;
+        if (launch_tf32_split_pad(wp, hi, lo, OC, Kc, Kp, st) != OK) {
+            fail("weight split failed");
+            return nullptr;
+        }
+        if (!tc_gemm_plan_gather(g.get(), OH * OW, OC, Kc, Bmax, gg, hi, lo, e)) return nullptr;
+        return g;
+    }
+    // conv epilogue writing a CHW view
+    static TcEpilogue chw_epilogue(const V &y, const float *bp, int act, const V &res,
+                                   int res_mode) {
+        TcEpilogue e;
+        e.C = y.p; e.ldc_m = 1; e.ldc_n = y.plane(); e.c_bs = y.bs;
+        e.bias = bp; e.act = act;
+        if (res_mode) {
+            e.res = res.p; e.res_ldm = 1; e.res_ldn = res.plane(); e.res_bs = res.bs;
+            e.res_mode = res_mode;
+        }
+        return e;
     }
     // launch a planned tensor-core GEMM for the current batch: rows_per_page > 0
     // folds the pages into M, otherwise every page (x zmul planes) is a z slice
@@ -314,6 +349,15 @@ public:
                          [=]() { return run_tc(g, 0); });
                     return;
                 }
+            } else if (use_tc) {
+                auto g = plan_conv_gather(x, OH, OW, wp, 1, 1, 0, OC,
+                                          chw_epilogue(y, bp, act, res, res_mode));
+                if (g) {
+                    push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * OH * OW * IC,
+                         4.0 * ((double)IC * x.plane() + (double)OC * OH * OW),
+                         [=]() { return run_tc(g, 0); });
+                    return;
+                }
             }
             push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * OH * OW * IC,
                  4.0 * ((double)IC * x.plane() + (double)OC * OH * OW), [=]() {
@@ -382,6 +426,16 @@ public:
             return;
         }
         // k3-s2 / k2: implicit GEMM
+        if (use_tc) {
+            auto g = plan_conv_gather(x, OH, OW, wp, K, s, p, OC,
+                                      chw_epilogue(y, bp, act, res, res_mode));
+            if (g) {
+                push(name, PPDL_STEP_GEMM_IMPLICIT, 2.0 * OC * OH * OW * IC * K * K,
+                     4.0 * ((double)IC * x.plane() + (double)OC * OH * OW),
+                     [=]() { return run_tc(g, 0); });
+                return;
+            }
+        }
         push(name, PPDL_STEP_GEMM_IMPLICIT, 2.0 * OC * OH * OW * IC * K * K,
              4.0 * ((double)IC * x.plane() + (double)OC * OH * OW), [=]() {
             GemmArgs g;
@@ -411,14 +465,21 @@ public:
             return;
         }
         const float *wp = wt.p, *bp = bt.p;
+        TcEpilogue e;
+        e.C = y.p + (long long)row0 * y.D; e.ldc_m = y.D; e.ldc_n = 1; e.c_bs = y.bs();
+        e.bias = bp;
         if (use_tc && tc_shape_ok(x.p, x.plane(), x.bs, IC)) {
             const Split wsp = split(wp, (long long)OC * IC);
-            TcEpilogue e;
-            e.C = y.p + (long long)row0 * y.D; e.ldc_m = y.D; e.ldc_n = 1; e.c_bs = y.bs();
-            e.bias = bp;
             auto g = std::make_shared<TcGemm>();
             if (ok && tc_gemm_plan(g.get(), (int)x.plane(), OC, IC, Bmax, x.p, 1, x.plane(), x.bs,
                                    wsp.hi, wsp.lo, 1, e)) {
+                push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * x.plane() * IC,
+                     4.0 * ((double)IC + OC) * x.plane(), [=]() { return run_tc(g, 0); });
+                return;
+            }
+        } else if (use_tc) {
+            auto g = plan_conv_gather(x, x.H, x.W, wp, 1, 1, 0, OC, e);
+            if (g) {
                 push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * x.plane() * IC,
                      4.0 * ((double)IC + OC) * x.plane(), [=]() { return run_tc(g, 0); });
                 return;
@@ -730,6 +791,7 @@ public:
         int32_t *topk = nullptr;
         if (cudaMalloc(&topk, sizeof(int32_t) * kNQ * Bmax) != cudaSuccess) fail("cudaMalloc");
         allocs.push_back(topk);
+        enc_topk = topk;
         push("topk300", PPDL_STEP_TOPK, 0.0, 4.0 * kNTok * kNC,
              [=]() { return launch_topk(ecls.p, topk, kNTok, kNC, kNQ, nb, st); });
         if (dumps) dump_list.push_back({"topk_idx", topk, {kNQ, 1, 1, 1}, "i32", kNQ * 4});
@@ -1173,8 +1235,9 @@ PPDL_API int ppdl_dump_raw(ppdl_ctx *c, const char *pfx) {
     cudaSetDevice(m.dev);
     if (cudaStreamSynchronize(m.st) != cudaSuccess) return 2;
     std::vector<float> lg(ppdl::kNQ * ppdl::kNC), bx(ppdl::kNQ * 4), od(ppdl::kNQ * ppdl::kNQ);
-    std::vector<int32_t> sl(ppdl::kNQ);
+    std::vector<int32_t> sl(ppdl::kNQ), tk(ppdl::kNQ);
     cudaMemcpy(lg.data(), m.logits.p, lg.size() * 4, cudaMemcpyDeviceToHost);
+    cudaMemcpy(tk.data(), m.enc_topk, tk.size() * 4, cudaMemcpyDeviceToHost);
     cudaMemcpy(bx.data(), m.boxes.p, bx.size() * 4, cudaMemcpyDeviceToHost);
     cudaMemcpy(od.data(), m.order.p, od.size() * 4, cudaMemcpyDeviceToHost);
     cudaMemcpy(sl.data(), m.sel, sl.size() * 4, cudaMemcpyDeviceToHost);
@@ -1182,7 +1245,8 @@ PPDL_API int ppdl_dump_raw(ppdl_ctx *c, const char *pfx) {
     bool okw = write_file(p + "logits.bin", lg.data(), lg.size() * 4) &&
                write_file(p + "boxes.bin", bx.data(), bx.size() * 4) &&
                write_file(p + "order.bin", od.data(), od.size() * 4) &&
-               write_file(p + "sel.bin", sl.data(), sl.size() * 4);
+               write_file(p + "sel.bin", sl.data(), sl.size() * 4) &&
+               write_file(p + "topk.bin", tk.data(), tk.size() * 4);
     return okw ? 0 : 1;
 }
 

@@ -86,6 +86,37 @@ PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float *A
     return to_status(ppdl::launch_tc_gemm(g, st));
 }
 
+PPDL_OPS_API int ppdl_conv2d_tf32x3(const float *x, int batch, int IC, int H, int W,
+                                    long long x_bs, const float *weight, const float *bias,
+                                    int OC, int K, int S, int P, int OH, int OW, int act,
+                                    float *b_split, float *y, long long y_bs, void *stream) {
+    g_err[0] = 0;
+    if (!x || !weight || !b_split || !y || batch <= 0 || IC <= 0 || OC <= 0 || H <= 0 ||
+        W <= 0 || OH <= 0 || OW <= 0 || act < 0 || act > 3)
+        return fail(PPDL_ERR_SHAPE, "conv2d: bad sizes, activation or null pointer");
+    // the last window of each axis must start inside the input (rows past
+    // the bottom/right edge are the implicit zero padding)
+    if ((long long)(OH - 1) * S - P >= H || (long long)(OW - 1) * S - P >= W ||
+        (long long)OH * OW >= (1LL << 31))
+        return fail(PPDL_ERR_SHAPE, "conv2d: output %dx%d larger than the input allows", OH, OW);
+    const int Kc = IC * K * K, Kp = (Kc + 3) / 4 * 4;
+    cudaStream_t st = (cudaStream_t)stream;
+    float *hi = b_split, *lo = b_split + (long long)OC * Kp;
+    ppdl::TcEpilogue e;
+    e.C = y; e.ldc_m = 1; e.ldc_n = (long long)OH * OW; e.c_bs = y_bs;
+    e.bias = bias; e.act = act;
+    ppdl::TcGather gg;
+    gg.x = x; gg.x_bs = x_bs; gg.plane = (long long)H * W;
+    gg.KS = K; gg.S = S; gg.P = P; gg.H = H; gg.W = W; gg.OW = OW;
+    ppdl::TcGemm g;
+    if (!ppdl::tc_gemm_plan_gather(&g, OH * OW, OC, Kc, batch, gg, hi, lo, e))
+        return fail(PPDL_ERR_SHAPE, "conv2d: geometry outside the gather (K 1..8, P < K, "
+                                    "1x1 only with S=1 P=0) or misaligned b_split");
+    const ppdl::Status s = ppdl::launch_tf32_split_pad(weight, hi, lo, OC, Kc, Kp, st);
+    if (s != ppdl::OK) return to_status(s);
+    return to_status(ppdl::launch_tc_gemm(g, st));
+}
+
 PPDL_OPS_API int ppdl_op_launch(const ppdl_op_desc *d, void *stream_ptr) {
     g_err[0] = 0;
     if (!d) return fail(PPDL_ERR_SHAPE, "null descriptor");

@@ -51,8 +51,9 @@ def gpu_out(cuda, gguf_path, pages, tmp_path_factory):
     outs = ctx.infer_batch(imgs, hw)
     d = tmp_path_factory.mktemp("raw")
     assert ctx.dump_raw(str(d) + "/p0_") == 0
-    raw = {k: np.fromfile(str(d) + f"/p0_{k}.bin", dtype=np.int32 if k == "sel" else np.float32)
-           for k in ("logits", "boxes", "order", "sel")}
+    raw = {k: np.fromfile(str(d) + f"/p0_{k}.bin",
+                          dtype=np.int32 if k in ("sel", "topk") else np.float32)
+           for k in ("logits", "boxes", "order", "sel", "topk")}
     ctx.close()
     return outs, raw
 
@@ -66,11 +67,24 @@ def _margin_ok(scores, i, tol=1e-4):
 def test_raw_outputs_page0(gpu_out, ref_out):
     _, raw = gpu_out
     r = ref_out[0]
-    lg = raw["logits"].reshape(300, 25)
+    # Decoder queries are the encoder's top-300 tokens in score order.  Two
+    # FP32 implementations may order near-tied tokens differently (the test
+    # pages hold gaps of ~1e-6 inside the top 300), which permutes decoder
+    # rows; self-attention is permutation-equivariant, so rows are matched by
+    # token.  Allowed: the same 300 tokens, displaced only where the oracle's
+    # encoder scores of the two tokens differ by less than TIE.
+    TIE = 1e-5
+    gt, rt = raw["topk"], np.asarray(r["topk"], np.int64)
+    assert set(gt.tolist()) == set(rt.tolist()), "top-300 token sets differ"
+    for i in np.nonzero(gt != rt)[0]:
+        assert abs(r["enc_max"][gt[i]] - r["enc_max"][rt[i]]) < TIE, f"query {i} reordered"
+    gpos = {int(t): i for i, t in enumerate(gt)}
+    idx = np.array([gpos[int(t)] for t in rt])
+    lg = raw["logits"].reshape(300, 25)[idx]
     s_gpu, s_ref = 1 / (1 + np.exp(-lg.astype(np.float64))), 1 / (1 + np.exp(-r["logits"].astype(np.float64)))
     assert np.abs(s_gpu - s_ref).max() < 1e-4, np.abs(s_gpu - s_ref).max()
-    assert np.abs(raw["boxes"].reshape(300, 4) - r["boxes"]).max() * 1000 <= 0.01
-    od = raw["order"]
+    assert np.abs(raw["boxes"].reshape(300, 4)[idx] - r["boxes"]).max() * 1000 <= 0.01
+    od = raw["order"].reshape(300, 300)[idx][:, idx].reshape(-1)
     assert np.abs(od - r["order"]).max() / max(np.abs(r["order"]).max(), 1) < 1e-4
 
 
