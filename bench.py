@@ -352,7 +352,8 @@ def cpu_baseline_msda(budget_s=10.0, sample_pages=None):
 # ------------------------------------------------------------ forward (cfg 3)
 FWD_B = 8
 GEMM_KINDS = ("gemm_1x1", "wg_madd", "gemm_implicit", "gemm_linear")
-HBM_KINDS = ("wg_input", "wg_output", "dwconv", "msda", "mask_box", "glue", "postprocess", "topk")
+HBM_KINDS = ("wg_input", "wg_output", "dwconv", "msda", "mask_box", "glue", "postprocess", "topk",
+             "im2col")
 
 
 def _fwd_pages(rank, B):

@@ -107,6 +107,7 @@ PPDL_API void * ppdl_stream(ppdl_ctx * ctx);
 #define PPDL_STEP_TOPK          10  /* top-300 selection                 */
 #define PPDL_STEP_POSTPROCESS   11  /* order votes, top-300, masks       */
 #define PPDL_STEP_GLUE          12  /* LN, softmax, add, interp, pool... */
+#define PPDL_STEP_IM2COL        13  /* conv operand packing for the GEMM */
 typedef struct {
     char    name[48];
     int32_t kind;   /* PPDL_STEP_* */

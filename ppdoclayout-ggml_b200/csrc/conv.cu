@@ -320,9 +320,48 @@ __global__ void transpose_kernel(const float *__restrict__ x, long long xbs, flo
     }
 }
 
+// ---- im2col: the M-major GEMM operand of a KS x KS, stride-S conv -----------
+// col[b][k][m] = x[b][ic][oy*S + kh - P][ox*S + kw - P] (0 outside H x W and
+// for k >= IC*KS*KS), k = (ic*KS + kh)*KS + kw (the raw weight's row order),
+// m = oy*OW + ox < M; rows have stride ldm >= M (16-byte multiples for the
+// tensor-core GEMM's TMA), the tail m in [M, ldm) is zero.  KS = 1 is a
+// channel-plane copy into padded rows.  One block row per k (grid.y).
+__global__ void __launch_bounds__(256)
+im2col_kernel(const float *__restrict__ x, long long xbs, long long plane, float *__restrict__ col,
+              long long cbs, int Kc, int H, int W, int KS, int S, int P, int OW, int M, int ldm) {
+    const int k = blockIdx.y, b = blockIdx.z;
+    float *cr = col + (long long)b * cbs + (long long)k * ldm;
+    if (k >= Kc) {
+        for (int m = blockIdx.x * 256 + threadIdx.x; m < ldm; m += gridDim.x * 256) cr[m] = 0.0f;
+        return;
+    }
+    const int kk2 = KS * KS, ic = k / kk2, tap = k - ic * kk2, kh = tap / KS, kw = tap - kh * KS;
+    const float *xc = x + (long long)b * xbs + (long long)ic * plane;
+    for (int m = blockIdx.x * 256 + threadIdx.x; m < ldm; m += gridDim.x * 256) {
+        float v = 0.0f;
+        if (m < M) {
+            const int oy = m / OW, ox = m - oy * OW;
+            const int iy = oy * S + kh - P, ix = ox * S + kw - P;
+            if ((unsigned)iy < (unsigned)H && (unsigned)ix < (unsigned)W) v = __ldg(xc + iy * W + ix);
+        }
+        cr[m] = v;
+    }
+}
+
 inline int blocks(long long n, int t = 256) { return (int)((n + t - 1) / t); }
 
 }  // namespace
+
+Status launch_im2col(const float *x, long long xbs, long long plane, float *col, long long cbs,
+                     int Kc, int Kp, int H, int W, int KS, int S, int P, int OW, int M, int ldm,
+                     int B, cudaStream_t st) {
+    if (Kp < Kc || ldm < M || M <= 0 || B <= 0 || Kp > 65535 || B > 65535) return ERR_SHAPE;
+    int gx = blocks(ldm);
+    if (gx > 64) gx = 64;
+    im2col_kernel<<<dim3(gx, Kp, B), 256, 0, st>>>(x, xbs, plane, col, cbs, Kc, H, W, KS, S, P,
+                                                   OW, M, ldm);
+    return cuda_status();
+}
 
 Status launch_wg4_input(const float *x, long long xbs, float *dt, int IC, int H, int W, int TW,
                         int TH, int pad, int B, cudaStream_t st, int ldt) {

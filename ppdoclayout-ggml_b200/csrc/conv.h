@@ -44,6 +44,15 @@ Status launch_interp(const float *x, long long xbs, float *y, long long ybs, con
                      long long bbs, int C, int H, int W, int OH, int OW, bool bilinear, int B,
                      cudaStream_t st);
 
+// im2col of a KS x KS stride-S conv with top/left padding P (bottom/right
+// padding implied by OW and M = OH*OW) into col [B][Kp][ldm]:
+// col[k][m] = x[ic][oy*S+kh-P][ox*S+kw-P], k = (ic*KS+kh)*KS+kw < Kc, zero
+// rows for Kc <= k < Kp and zero tails for M <= m < ldm.  KS = 1 copies the
+// channel planes into rows of stride ldm (plane stride `plane` of x).
+Status launch_im2col(const float *x, long long xbs, long long plane, float *col, long long cbs,
+                     int Kc, int Kp, int H, int W, int KS, int S, int P, int OW, int M, int ldm,
+                     int B, cudaStream_t st);
+
 // y[c][r] = x[r][c] for an R x Cc matrix per page (row strides ldx, ldy)
 Status launch_transpose(const float *x, long long xbs, float *y, long long ybs, int R, int Cc,
                         long long ldx, long long ldy, int B, cudaStream_t st);

@@ -490,11 +490,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const TcGather gg = a.gg;
             const int pK = a.K, pM = a.M;
             // converter, gather mode: build the A tile of each free stage from
-            // the conv input (the producer loads only B).  The copies of stage
-            // it are in flight while stage it - 1 is split and published.
+            // the conv input (the producer loads only B).  Up to `depth` stages
+            // of copies stay in flight; the oldest is split and published once
+            // a newer one is issued.  depth <= S - 1 keeps one stage for the
+            // MMA, so the converter never waits on a stage it still holds.
             const int ct = threadIdx.x - 128;
-            long long it = 0;
-            int prev = -1;
+            const int depth = S - 1 < 3 ? S - 1 : 3;
+            long long it = 0, pub = 0;  // stages [pub, it) issued, not yet published
             bool ok = true;
             for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
                 const int z = t / (pmt * pnt);
@@ -524,18 +526,26 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     }
                     gather_issue(gg, pK, xz, stage0 + (uint32_t)s * pstage, ct, oy0, ox0,
                                  kb * kBK);
-                    if (prev >= 0) {
-                        asm volatile("cp.async.wait_group 1;" ::: "memory");
-                        gather_split_rows(stage0_ptr + (size_t)prev * pstage, ct);
-                        mbar_arrive(bar_conv + 8 * prev);
+                    if (it + 1 - pub > depth) {
+                        // at most `depth` newer groups pending -> stage pub landed
+                        if (depth >= 3)
+                            asm volatile("cp.async.wait_group 3;" ::: "memory");
+                        else if (depth == 2)
+                            asm volatile("cp.async.wait_group 2;" ::: "memory");
+                        else
+                            asm volatile("cp.async.wait_group 1;" ::: "memory");
+                        const int ps = (int)(pub % S);
+                        gather_split_rows(stage0_ptr + (size_t)ps * pstage, ct);
+                        mbar_arrive(bar_conv + 8 * ps);
+                        pub++;
                     }
-                    prev = s;
                 }
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
-            if (ok && prev >= 0) {
-                gather_split_rows(stage0_ptr + (size_t)prev * pstage, ct);
-                mbar_arrive(bar_conv + 8 * prev);
+            for (; ok && pub < it; pub++) {
+                const int ps = (int)(pub % S);
+                gather_split_rows(stage0_ptr + (size_t)ps * pstage, ct);
+                mbar_arrive(bar_conv + 8 * ps);
             }
         } else if (warp >= 4 && warp < kWarpProducer) {
             // converter: in-place 3xTF32 split of the A tile

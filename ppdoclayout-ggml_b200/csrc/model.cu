@@ -151,26 +151,36 @@ public:
     static bool tc_shape_ok(const float *p, long long plane, long long bs, int K) {
         return ((uintptr_t)p & 15) == 0 && plane % 4 == 0 && bs % 4 == 0 && K % 4 == 0;
     }
-    // Tensor-core conv with the A tile gathered from the CHW input (implicit
-    // GEMM; also the 1x1 convs whose planes break the TMA stride rule).
-    // Returns a null plan when the geometry does not fit the gather.
-    std::shared_ptr<TcGemm> plan_conv_gather(const V &x, int OH, int OW, const float *wp, int K,
-                                             int s, int p, int OC, const TcEpilogue &e) {
-        TcGather gg;
-        gg.x = x.p; gg.x_bs = x.bs; gg.plane = x.plane();
-        gg.KS = K; gg.S = s; gg.P = p; gg.H = x.H; gg.W = x.W; gg.OW = OW;
-        const int Kc = x.C * K * K, Kp = (Kc + 3) / 4 * 4;
-        auto g = std::make_shared<TcGemm>();
-        // probe the geometry first (B pointers only enter the tensor maps)
-        if (!ok || !tc_gemm_plan_gather(g.get(), OH * OW, OC, Kc, Bmax, gg, wp, wp, e))
-            return nullptr;
+    // Tensor-core conv through im2col: the operand is packed into the shared A
+    // scratch as [Kp][Mp] rows (M-major, 16-byte rows; for a 1x1 conv a plane
+    // copy into padded rows), then the TMA-fed GEMM runs on it.  Used for the
+    // k3-s2 / k2 convs and for 1x1 convs whose planes break the TMA stride
+    // rule.  Returns a null plan (caller keeps the SIMT GEMM) when the
+    // packed operand cannot be described.
+    std::shared_ptr<TcGemm> plan_conv_im2col(const V &x, int K, int s, int p, int OC, int OH,
+                                             int OW, const float *wp, const TcEpilogue &e,
+                                             const std::string &name) {
+        const int Kc = x.C * K * K, Kp = (Kc + 3) / 4 * 4, M = OH * OW;
+        const long long Mp = (M + 3) / 4 * 4;
+        if (Kp > 65535 || !ok) return nullptr;
         float *hi = dalloc((long long)OC * Kp), *lo = dalloc((long long)OC * Kp);
         if (!ok) return nullptr;
         if (launch_tf32_split_pad(wp, hi, lo, OC, Kc, Kp, st) != OK) {
             fail("weight split failed");
             return nullptr;
         }
-        if (!tc_gemm_plan_gather(g.get(), OH * OW, OC, Kc, Bmax, gg, hi, lo, e)) return nullptr;
+        wg_dt_n = std::max(wg_dt_n, (long long)Kp * Mp * Bmax);
+        auto g = std::make_shared<TcGemm>();
+        finalizers.push_back([=]() {
+            if (!tc_gemm_plan(g.get(), M, OC, Kp, Bmax, wg_dt, 1, Mp, (long long)Kp * Mp, hi, lo,
+                              1, e))
+                g->ok = false;
+        });
+        push(name + ".im2col", PPDL_STEP_IM2COL, 0.0,
+             4.0 * ((double)x.C * x.plane() + (double)Kp * Mp), [=]() {
+            return launch_im2col(x.p, x.bs, x.plane(), wg_dt, (long long)Kp * Mp, Kc, Kp, x.H,
+                                 x.W, K, s, p, OW, M, (int)Mp, nb, st);
+        });
         return g;
     }
     // conv epilogue writing a CHW view
@@ -350,12 +360,12 @@ public:
                     return;
                 }
             } else if (use_tc) {
-                auto g = plan_conv_gather(x, OH, OW, wp, 1, 1, 0, OC,
-                                          chw_epilogue(y, bp, act, res, res_mode));
+                auto g = plan_conv_im2col(x, 1, 1, 0, OC, OH, OW, wp,
+                                          chw_epilogue(y, bp, act, res, res_mode), name);
                 if (g) {
                     push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * OH * OW * IC,
                          4.0 * ((double)IC * x.plane() + (double)OC * OH * OW),
-                         [=]() { return run_tc(g, 0); });
+                         [=]() { return g->ok ? run_tc(g, 0) : ERR_SHAPE; });
                     return;
                 }
             }
@@ -427,12 +437,12 @@ public:
         }
         // k3-s2 / k2: implicit GEMM
         if (use_tc) {
-            auto g = plan_conv_gather(x, OH, OW, wp, K, s, p, OC,
-                                      chw_epilogue(y, bp, act, res, res_mode));
+            auto g = plan_conv_im2col(x, K, s, p, OC, OH, OW, wp,
+                                      chw_epilogue(y, bp, act, res, res_mode), name);
             if (g) {
                 push(name, PPDL_STEP_GEMM_IMPLICIT, 2.0 * OC * OH * OW * IC * K * K,
                      4.0 * ((double)IC * x.plane() + (double)OC * OH * OW),
-                     [=]() { return run_tc(g, 0); });
+                     [=]() { return g->ok ? run_tc(g, 0) : ERR_SHAPE; });
                 return;
             }
         }
@@ -478,10 +488,11 @@ public:
                 return;
             }
         } else if (use_tc) {
-            auto g = plan_conv_gather(x, x.H, x.W, wp, 1, 1, 0, OC, e);
+            auto g = plan_conv_im2col(x, 1, 1, 0, OC, x.H, x.W, wp, e, name);
             if (g) {
                 push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * x.plane() * IC,
-                     4.0 * ((double)IC + OC) * x.plane(), [=]() { return run_tc(g, 0); });
+                     4.0 * ((double)IC + OC) * x.plane(),
+                     [=]() { return g->ok ? run_tc(g, 0) : ERR_SHAPE; });
                 return;
             }
         }
