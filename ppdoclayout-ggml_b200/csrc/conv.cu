@@ -64,14 +64,11 @@ int sm_count() {
 __global__ void __launch_bounds__(256)
 wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ dt, int IC,
                  int H, int W, int TW, int TH, int pad, int B, int ldt) {
+    // grid (tiles, IC, B): 32-bit index arithmetic only
     const int T = TW * TH;
-    const long long n = (long long)B * IC * T;
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int tile = (int)(i % T);
-    const long long r = i / T;
-    const int ic = (int)(r % IC);
-    const int b = (int)(r / IC);
+    const int tile = blockIdx.x * blockDim.x + threadIdx.x;
+    if (tile >= T) return;
+    const int ic = blockIdx.y, b = blockIdx.z;
     const int ty = tile / TW, tx = tile - ty * TW;
     const float *xp = x + (long long)b * xbs + (long long)ic * H * W;
     float d[6][6];
@@ -113,14 +110,11 @@ wg4_output_kernel(const float *__restrict__ yt, const float *__restrict__ bias,
                   float *__restrict__ y, long long ybs, const float *__restrict__ res,
                   long long rbs, int res_mode, int OC, int OH, int OW, int TW, int TH, int act,
                   int B, int ldt) {
+    // grid (tiles, OC, B)
     const int T = TW * TH;
-    const long long n = (long long)B * OC * T;
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int tile = (int)(i % T);
-    const long long r = i / T;
-    const int oc = (int)(r % OC);
-    const int b = (int)(r / OC);
+    const int tile = blockIdx.x * blockDim.x + threadIdx.x;
+    if (tile >= T) return;
+    const int oc = blockIdx.y, b = blockIdx.z;
     const int ty = tile / TW, tx = tile - ty * TW;
     const float *m = yt + ((long long)b * 36 * OC + oc) * ldt + tile;
     float mm[36];
@@ -208,15 +202,11 @@ __global__ void __launch_bounds__(256)
 dwconv_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
               const float *__restrict__ bias, float *__restrict__ y, long long ybs, int C, int H,
               int W, int OH, int OW, int S, int P, int act, int B) {
-    const long long n = (long long)B * C * OH * OW;
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int ox = (int)(i % OW);
-    long long r = i / OW;
-    const int oy = (int)(r % OH);
-    r /= OH;
-    const int c = (int)(r % C);
-    const int b = (int)(r / C);
+    // grid (pixels, C, B)
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= OH * OW) return;
+    const int c = blockIdx.y, b = blockIdx.z;
+    const int oy = p / OW, ox = p - oy * OW;
     const float *xp = x + (long long)b * xbs + (long long)c * H * W;
     const float *wp = w + (long long)c * K * K;
     float s = 0.0f;
@@ -239,15 +229,11 @@ dwconv_kernel(const float *__restrict__ x, long long xbs, const float *__restric
 // ggml_pad(x, 1, 1) + ggml_pool_2d(MAX, 2, 2, 1, 1, 0, 0) (src/ppdoclayout.cpp:621-625)
 __global__ void maxpool2_pad_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
                                     long long ybs, int C, int H, int W, int B) {
-    const long long n = (long long)B * C * H * W;
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int ox = (int)(i % W);
-    long long r = i / W;
-    const int oy = (int)(r % H);
-    r /= H;
-    const int c = (int)(r % C);
-    const int b = (int)(r / C);
+    // grid (pixels, C, B)
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= H * W) return;
+    const int c = blockIdx.y, b = blockIdx.z;
+    const int oy = p / W, ox = p - oy * W;
     const float *xp = x + (long long)b * xbs + (long long)c * H * W;
     const float v00 = xp[(long long)oy * W + ox];
     const float v01 = ox + 1 < W ? xp[(long long)oy * W + ox + 1] : 0.0f;
@@ -264,15 +250,11 @@ __global__ void maxpool2_pad_kernel(const float *__restrict__ x, long long xbs, 
 __global__ void interp_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
                               long long ybs, const float *__restrict__ base, long long bbs, int C,
                               int H, int W, int OH, int OW, int bilinear, int B) {
-    const long long n = (long long)B * C * OH * OW;
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int ox = (int)(i % OW);
-    long long r = i / OW;
-    const int oy = (int)(r % OH);
-    r /= OH;
-    const int c = (int)(r % C);
-    const int b = (int)(r / C);
+    // grid (pixels, C, B)
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= OH * OW) return;
+    const int c = blockIdx.y, b = blockIdx.z;
+    const int oy = p / OW, ox = p - oy * OW;
     const float *xp = x + (long long)b * xbs + (long long)c * H * W;
     const float sfx = (float)OW / (float)W, sfy = (float)OH / (float)H;
     float v;
@@ -329,34 +311,56 @@ __global__ void transpose_kernel(const float *__restrict__ x, long long xbs, flo
 __global__ void __launch_bounds__(256)
 im2col_kernel(const float *__restrict__ x, long long xbs, long long plane, float *__restrict__ col,
               long long cbs, int Kc, int H, int W, int KS, int S, int P, int OW, int M, int ldm) {
+    // each thread writes 4 consecutive m with one 16-byte store (ldm % 4 == 0)
     const int k = blockIdx.y, b = blockIdx.z;
-    float *cr = col + (long long)b * cbs + (long long)k * ldm;
+    float4 *cr = reinterpret_cast<float4 *>(col + (long long)b * cbs + (long long)k * ldm);
+    const int n4 = ldm >> 2;
     if (k >= Kc) {
-        for (int m = blockIdx.x * 256 + threadIdx.x; m < ldm; m += gridDim.x * 256) cr[m] = 0.0f;
+        for (int m4 = blockIdx.x * 256 + threadIdx.x; m4 < n4; m4 += gridDim.x * 256)
+            cr[m4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         return;
     }
     const int kk2 = KS * KS, ic = k / kk2, tap = k - ic * kk2, kh = tap / KS, kw = tap - kh * KS;
     const float *xc = x + (long long)b * xbs + (long long)ic * plane;
-    for (int m = blockIdx.x * 256 + threadIdx.x; m < ldm; m += gridDim.x * 256) {
-        float v = 0.0f;
-        if (m < M) {
-            const int oy = m / OW, ox = m - oy * OW;
-            const int iy = oy * S + kh - P, ix = ox * S + kw - P;
-            if ((unsigned)iy < (unsigned)H && (unsigned)ix < (unsigned)W) v = __ldg(xc + iy * W + ix);
+    for (int m4 = blockIdx.x * 256 + threadIdx.x; m4 < n4; m4 += gridDim.x * 256) {
+        float v[4];
+        int m = m4 * 4;
+        int oy = m / OW, ox = m - oy * OW;
+#pragma unroll
+        for (int e = 0; e < 4; e++, m++) {
+            v[e] = 0.0f;
+            if (m < M) {
+                const int iy = oy * S + kh - P, ix = ox * S + kw - P;
+                if ((unsigned)iy < (unsigned)H && (unsigned)ix < (unsigned)W)
+                    v[e] = __ldg(xc + iy * W + ix);
+            }
+            if (++ox == OW) {
+                ox = 0;
+                ++oy;
+            }
         }
-        cr[m] = v;
+        cr[m4] = make_float4(v[0], v[1], v[2], v[3]);
     }
 }
 
 inline int blocks(long long n, int t = 256) { return (int)((n + t - 1) / t); }
+
+// grid of the per-plane kernels: x over the pixels (or tiles) of a plane,
+// y over channels, z over pages
+inline bool grid3_ok(long long pix, int ch, int b) {
+    return pix > 0 && pix < (1LL << 31) && ch > 0 && ch <= 65535 && b > 0 && b <= 65535;
+}
+inline dim3 grid3(long long pix, int ch, int b) { return dim3(blocks(pix), ch, b); }
 
 }  // namespace
 
 Status launch_im2col(const float *x, long long xbs, long long plane, float *col, long long cbs,
                      int Kc, int Kp, int H, int W, int KS, int S, int P, int OW, int M, int ldm,
                      int B, cudaStream_t st) {
-    if (Kp < Kc || ldm < M || M <= 0 || B <= 0 || Kp > 65535 || B > 65535) return ERR_SHAPE;
-    int gx = blocks(ldm);
+    if (Kp < Kc || ldm < M || ldm % 4 || M <= 0 || B <= 0 || Kp > 65535 || B > 65535 ||
+        ((uintptr_t)col & 15) || cbs % 4)
+        return ERR_SHAPE;
+    int gx = blocks(ldm / 4);
     if (gx > 64) gx = 64;
     im2col_kernel<<<dim3(gx, Kp, B), 256, 0, st>>>(x, xbs, plane, col, cbs, Kc, H, W, KS, S, P,
                                                    OW, M, ldm);
@@ -365,24 +369,23 @@ Status launch_im2col(const float *x, long long xbs, long long plane, float *col,
 
 Status launch_wg4_input(const float *x, long long xbs, float *dt, int IC, int H, int W, int TW,
                         int TH, int pad, int B, cudaStream_t st, int ldt) {
-    const long long n = (long long)B * IC * TW * TH;
-    if (n <= 0) return n == 0 ? OK : ERR_SHAPE;
+    if (!grid3_ok((long long)TW * TH, IC, B)) return ERR_SHAPE;
     if (ldt <= 0) ldt = TW * TH;
     if (ldt < TW * TH) return ERR_SHAPE;
-    wg4_input_kernel<<<blocks(n), 256, 0, st>>>(x, xbs, dt, IC, H, W, TW, TH, pad, B, ldt);
+    wg4_input_kernel<<<grid3((long long)TW * TH, IC, B), 256, 0, st>>>(x, xbs, dt, IC, H, W, TW,
+                                                                       TH, pad, B, ldt);
     return cuda_status();
 }
 
 Status launch_wg4_output(const float *yt, const float *bias, float *y, long long ybs,
                          const float *res, long long rbs, int res_mode, int OC, int OH, int OW,
                          int TW, int TH, int act, int B, cudaStream_t st, int ldt) {
-    const long long n = (long long)B * OC * TW * TH;
-    if (n <= 0) return n == 0 ? OK : ERR_SHAPE;
+    if (!grid3_ok((long long)TW * TH, OC, B)) return ERR_SHAPE;
     if (TW < (OW + 3) / 4 || TH < (OH + 3) / 4) return ERR_SHAPE;
     if (ldt <= 0) ldt = TW * TH;
     if (ldt < TW * TH) return ERR_SHAPE;
-    wg4_output_kernel<<<blocks(n), 256, 0, st>>>(yt, bias, y, ybs, res, rbs, res_mode, OC, OH, OW,
-                                                 TW, TH, act, B, ldt);
+    wg4_output_kernel<<<grid3((long long)TW * TH, OC, B), 256, 0, st>>>(
+        yt, bias, y, ybs, res, rbs, res_mode, OC, OH, OW, TW, TH, act, B, ldt);
     return cuda_status();
 }
 
@@ -403,14 +406,12 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
                      long long ybs, int C, int H, int W, int K, int S, int P, int act, int B,
                      cudaStream_t st) {
     const int OH = (H + 2 * P - K) / S + 1, OW = (W + 2 * P - K) / S + 1;
-    const long long n = (long long)B * C * OH * OW;
-    if (n <= 0) return ERR_SHAPE;
+    if (OH <= 0 || OW <= 0 || !grid3_ok((long long)OH * OW, C, B)) return ERR_SHAPE;
+    const dim3 g = grid3((long long)OH * OW, C, B);
     if (K == 3)
-        dwconv_kernel<3><<<blocks(n), 256, 0, st>>>(x, xbs, w, bias, y, ybs, C, H, W, OH, OW, S, P,
-                                                    act, B);
+        dwconv_kernel<3><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, C, H, W, OH, OW, S, P, act, B);
     else if (K == 5)
-        dwconv_kernel<5><<<blocks(n), 256, 0, st>>>(x, xbs, w, bias, y, ybs, C, H, W, OH, OW, S, P,
-                                                    act, B);
+        dwconv_kernel<5><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, C, H, W, OH, OW, S, P, act, B);
     else
         return ERR_UNSUPPORTED;
     return cuda_status();
@@ -418,17 +419,17 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
 
 Status launch_maxpool2_pad(const float *x, long long xbs, float *y, long long ybs, int C, int H,
                            int W, int B, cudaStream_t st) {
-    const long long n = (long long)B * C * H * W;
-    maxpool2_pad_kernel<<<blocks(n), 256, 0, st>>>(x, xbs, y, ybs, C, H, W, B);
+    if (!grid3_ok((long long)H * W, C, B)) return ERR_SHAPE;
+    maxpool2_pad_kernel<<<grid3((long long)H * W, C, B), 256, 0, st>>>(x, xbs, y, ybs, C, H, W, B);
     return cuda_status();
 }
 
 Status launch_interp(const float *x, long long xbs, float *y, long long ybs, const float *base,
                      long long bbs, int C, int H, int W, int OH, int OW, bool bilinear, int B,
                      cudaStream_t st) {
-    const long long n = (long long)B * C * OH * OW;
-    interp_kernel<<<blocks(n), 256, 0, st>>>(x, xbs, y, ybs, base, bbs, C, H, W, OH, OW,
-                                             bilinear ? 1 : 0, B);
+    if (!grid3_ok((long long)OH * OW, C, B)) return ERR_SHAPE;
+    interp_kernel<<<grid3((long long)OH * OW, C, B), 256, 0, st>>>(x, xbs, y, ybs, base, bbs, C, H,
+                                                                   W, OH, OW, bilinear ? 1 : 0, B);
     return cuda_status();
 }
 

@@ -12,6 +12,12 @@ Status launch_layernorm256(const float *x, const float *r, const float *g, const
                            float *y, long long rows, cudaStream_t st);
 // softmax over rows of length L, in place
 Status launch_softmax_rows(float *x, long long rows, int L, cudaStream_t st);
+
+// Fused attention core (attn.cu): o = softmax(q k^T * scale) v per head of 32
+// dims over token-major [B][T][ld] tensors (page stride bs), heads x 32 <= ld;
+// o must not alias q, k or v.
+Status launch_attention(const float *q, const float *k, const float *v, float *o, int T, int heads,
+                        int ld, long long bs, float scale, int B, cudaStream_t st);
 Status launch_add(const float *a, const float *b, float *y, long long n, cudaStream_t st);
 Status launch_sigmoid(const float *x, float *y, long long n, cudaStream_t st);
 // ref = sigmoid(delta + inverse_sigmoid(ref))

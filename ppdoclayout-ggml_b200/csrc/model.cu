@@ -581,32 +581,14 @@ public:
     void mha(const S &qk_in, const S &v_in, const S &out, const std::string &pfx) {
         const int T = qk_in.T;
         S q = seq(T, kDM), k = seq(T, kDM), v = seq(T, kDM), o = seq(T, kDM);
-        float *sc = dalloc((long long)kNH * T * T * Bmax);
         lin(qk_in, q, pfx + ".q");
         lin(qk_in, k, pfx + ".k");
         lin(v_in, v, pfx + ".v");
-        push(pfx + ".qk", PPDL_STEP_GEMM_LINEAR, 2.0 * kNH * T * T * kHD,
-             4.0 * ((double)kNH * T * T + 2.0 * T * kDM), [=]() {
-            GemmArgs g;  // sc[b,h][i][j] = q_i . k_j / sqrt(32)
-            g.M = T; g.N = T; g.K = kHD; g.batch = nb * kNH;
-            g.A = {q.p, kDM, 1, kNH, (long long)T * kDM, kHD};
-            g.B = {k.p, 1, kDM, kNH, (long long)T * kDM, kHD};
-            g.C = sc; g.ldc_m = T; g.ldc_n = 1; g.c_bs_hi = (long long)T * T;
-            g.alpha = 1.0f / sqrtf((float)kHD);
-            return launch_gemm_simt(g, st);
-        });
-        push(pfx + ".softmax", PPDL_STEP_GLUE, 0.0, 8.0 * kNH * T * T, [=]() {
-            return launch_softmax_rows(sc, (long long)nb * kNH * T, T, st);
-        });
-        push(pfx + ".pv", PPDL_STEP_GEMM_LINEAR, 2.0 * kNH * T * T * kHD,
-             4.0 * ((double)kNH * T * T + 2.0 * T * kDM), [=]() {
-            GemmArgs h;  // o[b][i][h*32 + d] = sum_j sc[b,h][i][j] v[b][j][h*32 + d]
-            h.M = T; h.N = kHD; h.K = T; h.batch = nb * kNH;
-            h.A = {sc, T, 1, 1, (long long)T * T, 0};
-            h.B = {v.p, kDM, 1, kNH, (long long)T * kDM, kHD};
-            h.C = o.p; h.ldc_m = kDM; h.ldc_n = 1;
-            h.c_div = kNH; h.c_bs_hi = (long long)T * kDM; h.c_bs_lo = kHD;
-            return launch_gemm_simt(h, st);
+        // softmax(q k^T / sqrt(32)) v in one launch (scores stay on chip)
+        push(pfx + ".attn", PPDL_STEP_GEMM_LINEAR, 4.0 * kNH * T * T * kHD,
+             4.0 * 4.0 * T * kDM, [=]() {
+            return launch_attention(q.p, k.p, v.p, o.p, T, kNH, kDM, (long long)T * kDM,
+                                    1.0f / sqrtf((float)kHD), nb, st);
         });
         lin(o, out, pfx + ".o");
     }
