@@ -64,11 +64,11 @@ int sm_count() {
 __global__ void __launch_bounds__(256)
 wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ dt, int IC,
                  int H, int W, int TW, int TH, int pad, int B, int ldt) {
-    // grid (tiles, IC, B): 32-bit index arithmetic only
+    // grid (IC*T / 256, B): one 32-bit division per thread
     const int T = TW * TH;
-    const int tile = blockIdx.x * blockDim.x + threadIdx.x;
-    if (tile >= T) return;
-    const int ic = blockIdx.y, b = blockIdx.z;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= IC * T) return;
+    const int ic = i / T, tile = i - ic * T, b = blockIdx.y;
     const int ty = tile / TW, tx = tile - ty * TW;
     const float *xp = x + (long long)b * xbs + (long long)ic * H * W;
     float d[6][6];
@@ -110,11 +110,11 @@ wg4_output_kernel(const float *__restrict__ yt, const float *__restrict__ bias,
                   float *__restrict__ y, long long ybs, const float *__restrict__ res,
                   long long rbs, int res_mode, int OC, int OH, int OW, int TW, int TH, int act,
                   int B, int ldt) {
-    // grid (tiles, OC, B)
+    // grid (OC*T / 256, B)
     const int T = TW * TH;
-    const int tile = blockIdx.x * blockDim.x + threadIdx.x;
-    if (tile >= T) return;
-    const int oc = blockIdx.y, b = blockIdx.z;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= OC * T) return;
+    const int oc = i / T, tile = i - oc * T, b = blockIdx.y;
     const int ty = tile / TW, tx = tile - ty * TW;
     const float *m = yt + ((long long)b * 36 * OC + oc) * ldt + tile;
     float mm[36];
@@ -202,10 +202,10 @@ __global__ void __launch_bounds__(256)
 dwconv_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
               const float *__restrict__ bias, float *__restrict__ y, long long ybs, int C, int H,
               int W, int OH, int OW, int S, int P, int act, int B) {
-    // grid (pixels, C, B)
-    const int p = blockIdx.x * blockDim.x + threadIdx.x;
-    if (p >= OH * OW) return;
-    const int c = blockIdx.y, b = blockIdx.z;
+    // grid (C*OH*OW / 256, B)
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= C * OH * OW) return;
+    const int c = i / (OH * OW), p = i - c * (OH * OW), b = blockIdx.y;
     const int oy = p / OW, ox = p - oy * OW;
     const float *xp = x + (long long)b * xbs + (long long)c * H * W;
     const float *wp = w + (long long)c * K * K;
@@ -229,10 +229,10 @@ dwconv_kernel(const float *__restrict__ x, long long xbs, const float *__restric
 // ggml_pad(x, 1, 1) + ggml_pool_2d(MAX, 2, 2, 1, 1, 0, 0) (src/ppdoclayout.cpp:621-625)
 __global__ void maxpool2_pad_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
                                     long long ybs, int C, int H, int W, int B) {
-    // grid (pixels, C, B)
-    const int p = blockIdx.x * blockDim.x + threadIdx.x;
-    if (p >= H * W) return;
-    const int c = blockIdx.y, b = blockIdx.z;
+    // grid (C*H*W / 256, B)
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= C * H * W) return;
+    const int c = i / (H * W), p = i - c * (H * W), b = blockIdx.y;
     const int oy = p / W, ox = p - oy * W;
     const float *xp = x + (long long)b * xbs + (long long)c * H * W;
     const float v00 = xp[(long long)oy * W + ox];
@@ -250,10 +250,10 @@ __global__ void maxpool2_pad_kernel(const float *__restrict__ x, long long xbs, 
 __global__ void interp_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
                               long long ybs, const float *__restrict__ base, long long bbs, int C,
                               int H, int W, int OH, int OW, int bilinear, int B) {
-    // grid (pixels, C, B)
-    const int p = blockIdx.x * blockDim.x + threadIdx.x;
-    if (p >= OH * OW) return;
-    const int c = blockIdx.y, b = blockIdx.z;
+    // grid (C*OH*OW / 256, B)
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= C * OH * OW) return;
+    const int c = i / (OH * OW), p = i - c * (OH * OW), b = blockIdx.y;
     const int oy = p / OW, ox = p - oy * OW;
     const float *xp = x + (long long)b * xbs + (long long)c * H * W;
     const float sfx = (float)OW / (float)W, sfy = (float)OH / (float)H;
@@ -345,12 +345,12 @@ im2col_kernel(const float *__restrict__ x, long long xbs, long long plane, float
 
 inline int blocks(long long n, int t = 256) { return (int)((n + t - 1) / t); }
 
-// grid of the per-plane kernels: x over the pixels (or tiles) of a plane,
-// y over channels, z over pages
+// grid of the per-page kernels: x over the channels x pixels (or tiles) of a
+// page as one 32-bit index, y over pages
 inline bool grid3_ok(long long pix, int ch, int b) {
-    return pix > 0 && pix < (1LL << 31) && ch > 0 && ch <= 65535 && b > 0 && b <= 65535;
+    return pix > 0 && ch > 0 && pix * ch < (1LL << 31) && b > 0 && b <= 65535;
 }
-inline dim3 grid3(long long pix, int ch, int b) { return dim3(blocks(pix), ch, b); }
+inline dim3 grid3(long long pix, int ch, int b) { return dim3(blocks(pix * ch), b); }
 
 }  // namespace
 

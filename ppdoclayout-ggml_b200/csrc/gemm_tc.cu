@@ -25,8 +25,8 @@
 //                activation; CHW outputs leave through shared-memory boxes
 //                and TMA stores (asynchronous, clipped at the tensor edges),
 //                other layouts through direct global stores.
-// Double-buffered TMEM slots overlap a tile's epilogue with the next tile's
-// main loop.
+// Four TMEM partial slots let the MMAs run ahead of the epilogue's folds and
+// overlap a tile's stores with the next tile's main loop.
 //
 // Layouts: A is either M-major — a CHW activation, pixels contiguous — read
 // by TMA boxes of 32 pixels x 32 channels with the 128-byte swizzle on a
@@ -63,15 +63,13 @@ constexpr uint32_t kTmemCols = 512;
 constexpr long long kTimeoutCycles = 4000000000LL;
 constexpr int kMaxStages = 4;
 constexpr int kABytes = kBM * kBK * 4;  // 16 KB
-// TMEM (512 columns): hi*hi partials P0 | P1 (chunks of kChunkKB k-blocks,
-// 16 MMA adds each) and cross-term accumulators X0 | X1 (hi*lo + lo*hi of a
-// whole tile; they are ~2^-11 of the result, so their own accumulation error
-// is negligible).  The running total lives in epilogue registers.
-constexpr int kChunkKB = 1;
-constexpr int kSlots = 2;
+// TMEM (512 columns): four partial slots of 128 columns, one k-block of all
+// three products each (4 large + 8 small MMA adds); the running total lives
+// in epilogue registers.
+constexpr int kSlots = 4;
 constexpr int kSlotCols = 128;
-constexpr int kXCol = 256;
 constexpr int kMaxBN = 128;
+static_assert(kSlots * kSlotCols <= (int)kTmemCols, "partial slots exceed TMEM");
 
 // Epilogue staging for TMA stores of CHW outputs: per epilogue warp two
 // boxes of 32 pixels x 16 channels (2 KB each).
@@ -137,6 +135,20 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
         }
     }
 }
+
+// Position in a ring of n stages or slots: index and mbarrier phase parity,
+// advanced by one step at a time (no division on the issue paths).
+struct Ring {
+    int i = 0, n;
+    uint32_t ph = 0;
+    __device__ explicit Ring(int n_) : n(n_) {}
+    __device__ __forceinline__ void next() {
+        if (++i == n) {
+            i = 0;
+            ph ^= 1u;
+        }
+    }
+};
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *tm, uint32_t bar,
                                             int x, int y, int z) {
@@ -387,13 +399,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmC,
                const __grid_constant__ Args a) {
     extern __shared__ uint8_t smem_raw[];
-    // control block: 16 mbarriers + tmem base + abort flag, then 1024-aligned stages
+    // control block: mbarriers + tmem base + abort flag, then 1024-aligned stages
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t ctrl = raw;
     const uint32_t bar_full = ctrl, bar_conv = ctrl + 8 * kMaxStages,
                    bar_empty = ctrl + 16 * kMaxStages, bar_pfull = ctrl + 24 * kMaxStages,
-                   bar_pempty = bar_pfull + 8 * kSlots, bar_xfull = bar_pempty + 8 * kSlots,
-                   bar_xempty = bar_xfull + 16, bar_done = bar_xempty + 16;
+                   bar_pempty = bar_pfull + 8 * kSlots, bar_done = bar_pempty + 8 * kSlots;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem_raw + 256);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem_raw + 260);
     const uint32_t stage0 = (raw + 512 + 1023) & ~1023u;
@@ -411,10 +422,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int i = 0; i < kSlots; i++) {
             mbar_init(bar_pfull + 8 * i, 1);
             mbar_init(bar_pempty + 8 * i, kEpiThreads);
-        }
-        for (int i = 0; i < 2; i++) {
-            mbar_init(bar_xfull + 8 * i, 1);
-            mbar_init(bar_xempty + 8 * i, kEpiThreads);
         }
         mbar_init(bar_done, 1);
         *abort_flag = 0;
@@ -448,15 +455,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (warp == kWarpProducer) {
             if (lane == 0) {
                 long long it = 0;
+                Ring rs(S);
                 bool ok = true;
                 for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
                     const int z = t / (pmt * pnt);
                     const int r = t - z * pmt * pnt;
                     const int m0 = (r / pnt) * kBM, n0 = (r % pnt) * pbn;
                     const int pz = z % pplanes;
-                    for (int kb = 0; kb < kblocks; kb++, it++) {
-                        const int s = (int)(it % S);
-                        const uint32_t ph = (uint32_t)((it / S) & 1);
+                    for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
+                        const int s = rs.i;
+                        const uint32_t ph = rs.ph;
                         if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, abort_flag)) {
                             ok = false;
                             break;
@@ -497,6 +505,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int ct = threadIdx.x - 128;
             const int depth = S - 1 < 3 ? S - 1 : 3;
             long long it = 0, pub = 0;  // stages [pub, it) issued, not yet published
+            Ring rs(S), rp(S);  // issue and publish positions
             bool ok = true;
             for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
                 const int z = t / (pmt * pnt);
@@ -517,9 +526,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         ox0[i] = 0;
                     }
                 }
-                for (int kb = 0; kb < kblocks; kb++, it++) {
-                    const int s = (int)(it % S);
-                    const uint32_t ph = (uint32_t)((it / S) & 1);
+                for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
+                    const int s = rs.i;
+                    const uint32_t ph = rs.ph;
                     if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, abort_flag)) {
                         ok = false;
                         break;
@@ -534,16 +543,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                             asm volatile("cp.async.wait_group 2;" ::: "memory");
                         else
                             asm volatile("cp.async.wait_group 1;" ::: "memory");
-                        const int ps = (int)(pub % S);
+                        const int ps = rp.i;
                         gather_split_rows(stage0_ptr + (size_t)ps * pstage, ct);
                         mbar_arrive(bar_conv + 8 * ps);
                         pub++;
+                        rp.next();
                     }
                 }
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
-            for (; ok && pub < it; pub++) {
-                const int ps = (int)(pub % S);
+            for (; ok && pub < it; pub++, rp.next()) {
+                const int ps = rp.i;
                 gather_split_rows(stage0_ptr + (size_t)ps * pstage, ct);
                 mbar_arrive(bar_conv + 8 * ps);
             }
@@ -551,11 +561,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // converter: in-place 3xTF32 split of the A tile
             const int ct = threadIdx.x - 128;
             long long it = 0;
+            Ring rs(S);
             bool ok = true;
             for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
-                for (int kb = 0; kb < kblocks; kb++, it++) {
-                    const int s = (int)(it % S);
-                    const uint32_t ph = (uint32_t)((it / S) & 1);
+                for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
+                    const int s = rs.i;
+                    const uint32_t ph = rs.ph;
                     if (!mbar_wait(bar_full + 8 * s, ph, abort_flag)) {
                         ok = false;
                         break;
@@ -578,71 +589,56 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
             }
         } else if (warp == kWarpMma) {
-            // hi*hi products go to a fresh TMEM partial every kChunkKB k-blocks
-            // (two slots, alternating), which the epilogue folds into its running
-            // total with FP32 adds — the tensor core's own accumulation then sums
-            // at most 16 of the large terms; the two small cross products go to
-            // the tile's X slot.
+            // Every k-block accumulates into a TMEM partial slot of its own
+            // (kSlots slots, round robin), which the epilogue folds into its
+            // running FP32 total.  Inside a k-block the two small cross products
+            // go in first and the four large hi*hi products last, so the tensor
+            // core's truncating accumulation acts on the large values only four
+            // times per partial (the rounding of the small ones is ~2^-11 of
+            // that).  With several slots the MMAs run ahead of the epilogue's
+            // folds instead of waiting for each one.
             if (lane == 0) {
-                long long it = 0, ctr = 0;
-                int tcnt = 0;
+                long long it = 0;
+                Ring rs(S), rp(kSlots);
                 bool ok = true;
-                for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x, tcnt++) {
-                    const int xs = tcnt & 1;
-                    if (!mbar_wait(bar_xempty + 8 * xs, (uint32_t)(((tcnt >> 1) & 1) ^ 1), abort_flag))
-                        break;
-                    const uint32_t dx = tmem_base + (uint32_t)(kXCol + xs * kSlotCols);
-                    for (int kb0 = 0; kb0 < kblocks && ok; kb0 += kChunkKB, ctr++) {
-                        const int p = (int)(ctr % kSlots);
-                        const uint32_t pph = (uint32_t)((ctr / kSlots) & 1);
-                        if (!mbar_wait(bar_pempty + 8 * p, pph ^ 1, abort_flag)) {
+                for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
+                    for (int kb = 0; kb < kblocks; kb++, it++, rs.next(), rp.next()) {
+                        const int p = rp.i;
+                        const uint32_t pph = rp.ph;
+                        const int s = rs.i;
+                        const uint32_t ph = rs.ph;
+                        if (!mbar_wait(bar_pempty + 8 * p, pph ^ 1, abort_flag) ||
+                            !mbar_wait(bar_conv + 8 * s, ph, abort_flag) ||
+                            (pgather && !mbar_wait(bar_full + 8 * s, ph, abort_flag))) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
                         const uint32_t d = tmem_base + (uint32_t)(p * kSlotCols);
-                        const int kb1 = kb0 + kChunkKB < kblocks ? kb0 + kChunkKB : kblocks;
-                        for (int kb = kb0; kb < kb1; kb++, it++) {
-                            const int s = (int)(it % S);
-                            const uint32_t ph = (uint32_t)((it / S) & 1);
-                            if (!mbar_wait(bar_conv + 8 * s, ph, abort_flag) ||
-                                (pgather && !mbar_wait(bar_full + 8 * s, ph, abort_flag))) {
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-                            const uint32_t st = stage0 + s * pstage;
-                            const uint32_t ahi = st, alo = st + kABytes;
-                            const uint32_t bhi = st + 2 * kABytes, blo = bhi + pbn * 128;
-                            // descriptors of the four K=8 steps: A M-major (8 K rows =
-                            // two 4-row groups of 512 B) or K-major (32 bytes of K
-                            // inside the swizzled 128-byte row); B K-major
-                            auto desc_a = [&](uint32_t base, int kk) {
-                                return pamn ? smem_desc(base + kk * 1024, 4096, 512, 1)
-                                              : smem_desc(base + kk * 32, 16, 1024, 2);
-                            };
-                            // the large hi*hi products first, so that the partial is
-                            // published (and folded by the epilogue) while the
-                            // cross terms still run
-    #pragma unroll
-                            for (int kk = 0; kk < kBK / 8; kk++)
-                                umma_tf32(d, desc_a(ahi, kk), smem_desc(bhi + kk * 32, 16, 1024, 2),
-                                          pidesc, (kb == kb0 && kk == 0) ? 0u : 1u);
-                            if (kb == kb1 - 1) umma_commit(bar_pfull + 8 * p);
-    #pragma unroll
-                            for (int kk = 0; kk < kBK / 8; kk++) {
-                                const uint64_t dah = desc_a(ahi, kk), dal = desc_a(alo, kk);
-                                const uint64_t dbh = smem_desc(bhi + kk * 32, 16, 1024, 2);
-                                const uint64_t dbl = smem_desc(blo + kk * 32, 16, 1024, 2);
-                                umma_tf32(dx, dal, dbh, pidesc, (kb == 0 && kk == 0) ? 0u : 1u);
-                                umma_tf32(dx, dah, dbl, pidesc, 1u);
-                            }
-                            umma_commit(bar_empty + 8 * s);
+                        const uint32_t st = stage0 + s * pstage;
+                        const uint32_t ahi = st, alo = st + kABytes;
+                        const uint32_t bhi = st + 2 * kABytes, blo = bhi + pbn * 128;
+                        // descriptors of the four K=8 steps: A M-major (8 K rows =
+                        // two 4-row groups of 512 B) or K-major (32 bytes of K
+                        // inside the swizzled 128-byte row); B K-major
+                        auto desc_a = [&](uint32_t base, int kk) {
+                            return pamn ? smem_desc(base + kk * 1024, 4096, 512, 1)
+                                        : smem_desc(base + kk * 32, 16, 1024, 2);
+                        };
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 8; kk++) {
+                            const uint64_t dbh = smem_desc(bhi + kk * 32, 16, 1024, 2);
+                            const uint64_t dbl = smem_desc(blo + kk * 32, 16, 1024, 2);
+                            umma_tf32(d, desc_a(alo, kk), dbh, pidesc, kk == 0 ? 0u : 1u);
+                            umma_tf32(d, desc_a(ahi, kk), dbl, pidesc, 1u);
                         }
-                        if (!ok) break;
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 8; kk++)
+                            umma_tf32(d, desc_a(ahi, kk), smem_desc(bhi + kk * 32, 16, 1024, 2),
+                                      pidesc, 1u);
+                        umma_commit(bar_empty + 8 * s);
+                        umma_commit(bar_pfull + 8 * p);
                     }
-                    if (!ok) break;
-                    umma_commit(bar_xfull + 8 * xs);
                 }
                 // all issued MMAs must finish before TMEM is released
                 umma_commit(bar_done);
@@ -655,8 +651,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpi));
         // epilogue, 8 warps: two per TMEM lane quadrant (warp % 4), each
         // owning 64 of the bn <= 128 columns.  Every partial is folded into a
-        // running FP32 total held in registers; the tile's cross terms are
-        // added last and the total goes back into the X slot, from where a
+        // running FP32 total held in registers; the total goes back into the
+        // tile's last partial slot, from where a
         // compact 16-column loop applies bias / residual / activation and
         // stores (a small loop body keeps the instruction cache warm for the
         // other roles): CHW outputs through shared-memory boxes and TMA
@@ -673,21 +669,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t staging = stage0 + (uint32_t)S * a.stage_bytes;
         float *staging_ptr = reinterpret_cast<float *>(stage0_ptr + (size_t)S * a.stage_bytes);
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        const int nchunks = (kblocks + kChunkKB - 1) / kChunkKB;
         float tot[kHalfCols];
         long long ctr = 0;
-        int tcnt = 0, nbox = 0;
+        Ring rp(kSlots);
+        int nbox = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x, tcnt++) {
+        for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
             const int z = t / (pmt * pnt);
             const int r = t - z * pmt * pnt;
             const int m0 = (r / pnt) * kBM, n0 = (r % pnt) * pbn;
             const int m = m0 + quad * 32 + lane;
             float *C = e.C + (long long)z * e.c_bs;
             const float *R = e.res_mode ? e.res + (long long)z * e.res_bs : nullptr;
-            for (int c = 0; c < nchunks; c++, ctr++) {
-                const int p = (int)(ctr % kSlots);
-                const uint32_t pph = (uint32_t)((ctr / kSlots) & 1);
+            uint32_t last = 0;  // slot of the tile's last partial, held for the stores
+            for (int c = 0; c < kblocks; c++, ctr++, rp.next()) {
+                const int p = rp.i;
+                const uint32_t pph = rp.ph;
                 if (!mbar_wait(bar_pfull + 8 * p, pph, abort_flag)) {
                     ok = false;
                     break;
@@ -705,22 +702,23 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                                      : tot[q * 32 + j] + __uint_as_float(v[j]);
                     }
                 }
-                tc_fence_before();
-                mbar_arrive(bar_pempty + 8 * p);
+                if (c + 1 < kblocks) {
+                    tc_fence_before();
+                    mbar_arrive(bar_pempty + 8 * p);
+                } else {
+                    last = (uint32_t)p;
+                }
             }
             if (!ok) break;
-            const int xs = tcnt & 1;
-            if (!mbar_wait(bar_xfull + 8 * xs, (uint32_t)((tcnt >> 1) & 1), abort_flag)) break;
-            tc_fence_after();
-            const uint32_t xa = tmem_base + lane_base + (uint32_t)(kXCol + xs * kSlotCols + c_lo);
+            // the total goes into the last partial's slot, read back in 16-column
+            // pieces by the store loop
+            const uint32_t xa = tmem_base + lane_base + (uint32_t)(last * kSlotCols + c_lo);
 #pragma unroll
             for (int q = 0; q < kHalfCols / 32; q++) {
                 if (c_lo + q * 32 < pbn) {
                     uint32_t v[32];
-                    tmem_ld32(xa + (uint32_t)(q * 32), v);
 #pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        v[j] = __float_as_uint(tot[q * 32 + j] + __uint_as_float(v[j]));
+                    for (int j = 0; j < 32; j++) v[j] = __float_as_uint(tot[q * 32 + j]);
                     tmem_st32(xa + (uint32_t)(q * 32), v);
                 }
             }
@@ -729,7 +727,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             float *Crow = C + (long long)m * e.ldc_m;
             const float *Rrow = R ? R + (long long)m * e.res_ldm : nullptr;
             const int c_hi = pbn < c_lo + kHalfCols ? pbn : c_lo + kHalfCols;
-            const uint32_t xt = tmem_base + lane_base + (uint32_t)(kXCol + xs * kSlotCols);
+            const uint32_t xt = tmem_base + lane_base + (uint32_t)(last * kSlotCols);
 #pragma unroll 1
             for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
                 const uint32_t xa = xt;
@@ -810,7 +808,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
             }
             tc_fence_before();
-            mbar_arrive(bar_xempty + 8 * xs);
+            mbar_arrive(bar_pempty + 8 * last);
         }
         // the staging boxes must be read and the stores complete before exit
         if (ptma && lane == 0) bulk_wait_all();
@@ -913,8 +911,8 @@ namespace {
 bool plan_common(TcGemm *g, int M, int N, int K, int batch, int planes, const TcEpilogue &epi) {
     g->ok = false;
     if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || planes <= 0) return false;
-    // N tile (multiple of 16, <= 128 so that two partial slots and two
-    // cross-term slots fit in the 512 TMEM columns); cost model: tiles x
+    // N tile (multiple of 16, <= 128 so that the four partial slots fit in
+    // the 512 TMEM columns); cost model: tiles x
     // (bn + 64), the 64 standing for the per-tile A traffic and epilogue
     // overhead in column equivalents
     int bn = 16;
