@@ -20,6 +20,21 @@ constexpr int kHeadDim = 32;  // head dim
 constexpr int kBQ = 32;       // queries per block
 constexpr int kKT = 64;       // keys per shared-memory tile
 constexpr int kThreads = 256;
+constexpr int kLD = 36;       // row stride of the Q and K/V tiles
+
+__device__ __forceinline__ void cp_async16(float *dst, const float *src, bool valid) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 __device__ __forceinline__ float warp_max32(float v) {
 #pragma unroll
@@ -33,41 +48,67 @@ __device__ __forceinline__ float warp_sum32(float v) {
 }
 
 // q, k, v, o: token-major [B][T][ld] with head h at columns h*32 .. h*32+31.
-// Shared memory: Q [32][33] | K or V tile [64][33] | scores [32][ldS].
-__global__ void __launch_bounds__(kThreads)
+// Shared memory: Q [32][36] | two K/V tiles [64][36] | scores [32][ldS], ldS
+// a multiple of 4.  Rows of 36 floats keep the 16-byte loads of a quarter
+// warp on distinct banks.  The K and V tiles stream through the two buffers
+// with cp.async, the next tile landing while the current one is used.
+__global__ void __launch_bounds__(kThreads, 2)
 attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
             float *__restrict__ o, int T, int ld, long long bs, float scale, int ldS) {
     extern __shared__ float sm[];
-    float *Qs = sm;                 // [kBQ][33]
-    float *Ts = Qs + kBQ * 33;      // [kKT][33]
-    float *Ss = Ts + kKT * 33;      // [kBQ][ldS]
+    float *Qs = sm;                 // [kBQ][kLD]
+    float *Tb = Qs + kBQ * kLD;     // [2][kKT][kLD]
+    float *Ss = Tb + 2 * kKT * kLD; // [kBQ][ldS]
     const int q0 = blockIdx.x * kBQ, h = blockIdx.y, b = blockIdx.z;
     const int t = threadIdx.x, lane = t & 31, wq = t >> 5;  // wq: query group of 4
     const long long base = (long long)b * bs + h * kHeadDim;
 
     for (int i = t; i < kBQ * kHeadDim; i += kThreads) {
         const int r = i >> 5, d = i & 31;
-        Qs[r * 33 + d] = q0 + r < T ? q[base + (long long)(q0 + r) * ld + d] : 0.0f;
+        Qs[r * kLD + d] = q0 + r < T ? q[base + (long long)(q0 + r) * ld + d] : 0.0f;
     }
+    // tile j of K or V into buffer (j & 1); rows past T are zero-filled
+    auto load_tile = [&](const float *src, int j) {
+        float *dst = Tb + (j & 1) * kKT * kLD;
+        for (int i = t; i < kKT * kHeadDim / 4; i += kThreads) {
+            const int r = i >> 3, c4 = i & 7, row = j * kKT + r;
+            const bool ok = row < T;
+            cp_async16(dst + r * kLD + 4 * c4, ok ? src + base + (long long)row * ld + 4 * c4 : src,
+                       ok);
+        }
+        cp_async_commit();
+    };
+    const int nt = (T + kKT - 1) / kKT;
     // ---- scores: thread -> queries 4wq..4wq+3, keys lane and lane+32 of a tile
-    for (int j0 = 0; j0 < T; j0 += kKT) {
-        __syncthreads();
-        for (int i = t; i < kKT * kHeadDim; i += kThreads) {
-            const int r = i >> 5, d = i & 31;
-            Ts[r * 33 + d] = j0 + r < T ? k[base + (long long)(j0 + r) * ld + d] : 0.0f;
+    load_tile(k, 0);
+    for (int jt = 0; jt < nt; jt++) {
+        const int j0 = jt * kKT;
+        if (jt + 1 < nt) {
+            load_tile(k, jt + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
+        const float *Ts = Tb + (jt & 1) * kKT * kLD;
         float acc[4][2];
 #pragma unroll
         for (int r = 0; r < 4; r++) acc[r][0] = acc[r][1] = 0.0f;
-#pragma unroll 8
-        for (int d = 0; d < kHeadDim; d++) {
-            const float k0 = Ts[lane * 33 + d], k1 = Ts[(lane + 32) * 33 + d];
+#pragma unroll 2
+        for (int d4 = 0; d4 < kHeadDim / 4; d4++) {
+            const float4 k0 = *reinterpret_cast<const float4 *>(Ts + lane * kLD + 4 * d4);
+            const float4 k1 = *reinterpret_cast<const float4 *>(Ts + (lane + 32) * kLD + 4 * d4);
 #pragma unroll
             for (int r = 0; r < 4; r++) {
-                const float qv = Qs[(wq * 4 + r) * 33 + d];
-                acc[r][0] = fmaf(qv, k0, acc[r][0]);
-                acc[r][1] = fmaf(qv, k1, acc[r][1]);
+                const float4 qv = *reinterpret_cast<const float4 *>(Qs + (wq * 4 + r) * kLD + 4 * d4);
+                acc[r][0] = fmaf(qv.x, k0.x, acc[r][0]);
+                acc[r][0] = fmaf(qv.y, k0.y, acc[r][0]);
+                acc[r][0] = fmaf(qv.z, k0.z, acc[r][0]);
+                acc[r][0] = fmaf(qv.w, k0.w, acc[r][0]);
+                acc[r][1] = fmaf(qv.x, k1.x, acc[r][1]);
+                acc[r][1] = fmaf(qv.y, k1.y, acc[r][1]);
+                acc[r][1] = fmaf(qv.z, k1.z, acc[r][1]);
+                acc[r][1] = fmaf(qv.w, k1.w, acc[r][1]);
             }
         }
 #pragma unroll
@@ -77,8 +118,9 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
                 const int j = j0 + lane + 32 * c;
                 if (j < T) Ss[(wq * 4 + r) * ldS + j] = __fmul_rn(acc[r][c], scale);
             }
+        __syncthreads();  // the buffer is refilled two tiles later
     }
-    __syncthreads();
+    load_tile(v, 0);  // lands during the softmax
     // ---- row softmax: warp wq owns rows 4wq..4wq+3
 #pragma unroll 1
     for (int r = 0; r < 4; r++) {
@@ -98,20 +140,36 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
     }
     // ---- o = p v: thread -> queries 4wq..4wq+3, dim lane
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int j0 = 0; j0 < T; j0 += kKT) {
-        __syncthreads();
-        for (int i = t; i < kKT * kHeadDim; i += kThreads) {
-            const int r = i >> 5, d = i & 31;
-            Ts[r * 33 + d] = j0 + r < T ? v[base + (long long)(j0 + r) * ld + d] : 0.0f;
+    for (int jt = 0; jt < nt; jt++) {
+        const int j0 = jt * kKT;
+        if (jt + 1 < nt) {
+            load_tile(v, jt + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
+        const float *Ts = Tb + (jt & 1) * kKT * kLD;
         const int jn = T - j0 < kKT ? T - j0 : kKT;
-#pragma unroll 4
-        for (int jj = 0; jj < jn; jj++) {
-            const float vv = Ts[jj * 33 + lane];
+        int jj = 0;
+        for (; jj + 4 <= jn; jj += 4) {
+            const float v0 = Ts[jj * kLD + lane], v1 = Ts[(jj + 1) * kLD + lane];
+            const float v2 = Ts[(jj + 2) * kLD + lane], v3 = Ts[(jj + 3) * kLD + lane];
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const float4 p = *reinterpret_cast<const float4 *>(Ss + (wq * 4 + r) * ldS + j0 + jj);
+                acc[r] = fmaf(p.x, v0, acc[r]);
+                acc[r] = fmaf(p.y, v1, acc[r]);
+                acc[r] = fmaf(p.z, v2, acc[r]);
+                acc[r] = fmaf(p.w, v3, acc[r]);
+            }
+        }
+        for (; jj < jn; jj++) {
+            const float vv = Ts[jj * kLD + lane];
 #pragma unroll
             for (int r = 0; r < 4; r++) acc[r] = fmaf(Ss[(wq * 4 + r) * ldS + j0 + jj], vv, acc[r]);
         }
+        __syncthreads();
     }
 #pragma unroll
     for (int r = 0; r < 4; r++) {
@@ -120,9 +178,10 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
     }
 }
 
+int attention_lds(int T) { return (T + 3) / 4 * 4; }
 size_t attention_smem_bytes(int T) {
-    const int ldS = (T + 3) / 4 * 4 + 1;
-    return sizeof(float) * ((size_t)kBQ * 33 + (size_t)kKT * 33 + (size_t)kBQ * ldS);
+    return sizeof(float) *
+           ((size_t)kBQ * kLD + 2 * (size_t)kKT * kLD + (size_t)kBQ * attention_lds(T));
 }
 
 }  // namespace
@@ -142,7 +201,7 @@ Status launch_attention(const float *q, const float *k, const float *v, float *o
             return ERR_CUDA;
         attr[dev] = true;
     }
-    const int ldS = (T + 3) / 4 * 4 + 1;
+    const int ldS = attention_lds(T);
     attn_kernel<<<dim3((T + kBQ - 1) / kBQ, heads, B), kThreads, smem, st>>>(q, k, v, o, T, ld,
                                                                           bs, scale, ldS);
     return cuda_status();

@@ -133,23 +133,38 @@ wg4_output_kernel(const float *__restrict__ yt, const float *__restrict__ bias,
     const float bv = bias ? bias[oc] : 0.0f;
     float *yp = y + (long long)b * ybs + (long long)oc * OH * OW;
     const float *rp = res_mode ? res + (long long)b * rbs + (long long)oc * OH * OW : nullptr;
+    // a full 4-pixel row segment goes out as one 16-byte store (and the
+    // residual comes in as one 16-byte load) when the rows allow it
+    const bool vec = (OW & 3) == 0 && 4 * tx + 3 < OW && ((uintptr_t)yp & 15) == 0 &&
+                     (!rp || ((uintptr_t)rp & 15) == 0);
 #pragma unroll
     for (int a = 0; a < 4; a++) {
         const int py = 4 * ty + a;
         if (py >= OH) break;
+        const long long off0 = (long long)py * OW + 4 * tx;
+        float4 r4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (vec && rp) r4 = *reinterpret_cast<const float4 *>(rp + off0);
+        float out[4];
 #pragma unroll
         for (int c = 0; c < 4; c++) {
-            const int px = 4 * tx + c;
-            if (px >= OW) break;
             float s = 0.0f;
 #pragma unroll
             for (int v = 0; v < 6; v++) s = fmaf(t1[a][v], c_wgA[v * 4 + c], s);
             float val = __fadd_rn(s, bv);
-            const long long off = (long long)py * OW + px;
-            if (res_mode == 1) val = __fadd_rn(val, rp[off]);
+            const float rv = !rp ? 0.0f
+                             : vec ? (c == 0 ? r4.x : c == 1 ? r4.y : c == 2 ? r4.z : r4.w)
+                             : (4 * tx + c < OW ? rp[off0 + c] : 0.0f);
+            if (res_mode == 1) val = __fadd_rn(val, rv);
             val = act_apply(val, act);
-            if (res_mode == 2) val = __fadd_rn(val, rp[off]);
-            yp[off] = val;
+            if (res_mode == 2) val = __fadd_rn(val, rv);
+            out[c] = val;
+        }
+        if (vec) {
+            *reinterpret_cast<float4 *>(yp + off0) = make_float4(out[0], out[1], out[2], out[3]);
+        } else {
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                if (4 * tx + c < OW) yp[off0 + c] = out[c];
         }
     }
 }
@@ -197,89 +212,143 @@ __global__ void wg4_kmajor_split_kernel(const float *__restrict__ wg4, float *__
 
 // ---- depthwise conv -----------------------------------------------------------
 // ggml_conv_2d_dw_direct + bias + act (src/ppdoclayout.cpp:400-404).
-template <int K>
+// A block computes a 32 x 32 output tile of one (page, channel) plane from a
+// shared-memory copy of its input window (halo included, zeros outside the
+// image), so every input is read from global memory once per tile instead of
+// K*K times through L1.  Per output: s = fma over (kh, kw) ascending — the
+// zero taps of the padding leave s unchanged — then + bias, activation.
+constexpr int kDwTW = 32, kDwTH = 32;  // 256 threads, 4 rows each
+template <int K, int S>
 __global__ void __launch_bounds__(256)
 dwconv_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
-              const float *__restrict__ bias, float *__restrict__ y, long long ybs, int C, int H,
-              int W, int OH, int OW, int S, int P, int act, int B) {
-    // grid (C*OH*OW / 256, B)
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= C * OH * OW) return;
-    const int c = i / (OH * OW), p = i - c * (OH * OW), b = blockIdx.y;
-    const int oy = p / OW, ox = p - oy * OW;
+              const float *__restrict__ bias, float *__restrict__ y, long long ybs, int H, int W,
+              int OH, int OW, int P, int act, int tiles_x) {
+    constexpr int IW = (kDwTW - 1) * S + K, IH = (kDwTH - 1) * S + K, LD = IW + 1;
+    __shared__ float tile[IH * LD];
+    const int c = blockIdx.y, b = blockIdx.z;
+    const int tyi = blockIdx.x / tiles_x;
+    const int tx0 = (blockIdx.x - tyi * tiles_x) * kDwTW, ty0 = tyi * kDwTH;
     const float *xp = x + (long long)b * xbs + (long long)c * H * W;
-    const float *wp = w + (long long)c * K * K;
-    float s = 0.0f;
-#pragma unroll
-    for (int kh = 0; kh < K; kh++) {
-        const int iy = oy * S + kh - P;
-        if (iy < 0 || iy >= H) continue;
-#pragma unroll
-        for (int kw = 0; kw < K; kw++) {
-            const int ix = ox * S + kw - P;
-            if (ix < 0 || ix >= W) continue;
-            s = fmaf(__ldg(xp + (long long)iy * W + ix), __ldg(wp + kh * K + kw), s);
-        }
+    const int ix0 = tx0 * S - P, iy0 = ty0 * S - P;
+    for (int e = threadIdx.x; e < IH * IW; e += 256) {
+        const int r = e / IW, q = e - r * IW;
+        const int iy = iy0 + r, ix = ix0 + q;
+        tile[r * LD + q] =
+            ((unsigned)iy < (unsigned)H && (unsigned)ix < (unsigned)W) ? __ldg(xp + iy * W + ix) : 0.0f;
     }
-    s = __fadd_rn(s, bias[c]);
-    y[(long long)b * ybs + (long long)c * OH * OW + (long long)oy * OW + ox] = act_apply(s, act);
+    float wk[K * K];
+#pragma unroll
+    for (int i = 0; i < K * K; i++) wk[i] = __ldg(w + (long long)c * K * K + i);
+    __syncthreads();
+    const int lx = threadIdx.x & 31, ly0 = threadIdx.x >> 5;
+    const int ox = tx0 + lx;
+    if (ox >= OW) return;
+    const float bv = __ldg(bias + c);
+    float *yp = y + (long long)b * ybs + (long long)c * OH * OW + ox;
+#pragma unroll
+    for (int r = 0; r < kDwTH / 8; r++) {
+        const int ly = ly0 + 8 * r, oy = ty0 + ly;
+        if (oy >= OH) break;
+        const float *tp = tile + (ly * S) * LD + lx * S;
+        float s = 0.0f;
+#pragma unroll
+        for (int kh = 0; kh < K; kh++)
+#pragma unroll
+            for (int kw = 0; kw < K; kw++) s = fmaf(tp[kh * LD + kw], wk[kh * K + kw], s);
+        s = __fadd_rn(s, bv);
+        yp[(long long)oy * OW] = act_apply(s, act);
+    }
 }
 
 // ---- 2x2 stride-1 max pool over the right/bottom zero-padded input ----------
 // ggml_pad(x, 1, 1) + ggml_pool_2d(MAX, 2, 2, 1, 1, 0, 0) (src/ppdoclayout.cpp:621-625)
+// 4 consecutive outputs of a row per thread (W a multiple of 4): two 16-byte
+// row loads plus the next column, one 16-byte store
 __global__ void maxpool2_pad_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
                                     long long ybs, int C, int H, int W, int B) {
-    // grid (C*H*W / 256, B)
+    // grid (C*H*W / 1024, B)
+    const int w4 = W >> 2;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= C * H * W) return;
-    const int c = i / (H * W), p = i - c * (H * W), b = blockIdx.y;
-    const int oy = p / W, ox = p - oy * W;
-    const float *xp = x + (long long)b * xbs + (long long)c * H * W;
-    const float v00 = xp[(long long)oy * W + ox];
-    const float v01 = ox + 1 < W ? xp[(long long)oy * W + ox + 1] : 0.0f;
-    const float v10 = oy + 1 < H ? xp[(long long)(oy + 1) * W + ox] : 0.0f;
-    const float v11 = (ox + 1 < W && oy + 1 < H) ? xp[(long long)(oy + 1) * W + ox + 1] : 0.0f;
-    y[(long long)b * ybs + (long long)c * H * W + (long long)oy * W + ox] =
-        fmaxf(fmaxf(v00, v01), fmaxf(v10, v11));
+    if (i >= C * H * w4) return;
+    const int c = i / (H * w4), p = i - c * (H * w4), b = blockIdx.y;
+    const int oy = p / w4, ox = (p - oy * w4) * 4;
+    const float *r0 = x + (long long)b * xbs + (long long)c * H * W + (long long)oy * W + ox;
+    const bool has_down = oy + 1 < H, has_right = ox + 4 < W;
+    const float4 a = *reinterpret_cast<const float4 *>(r0);
+    const float4 d = has_down ? *reinterpret_cast<const float4 *>(r0 + W)
+                              : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float a4 = has_right ? r0[4] : 0.0f;
+    const float d4 = (has_right && has_down) ? r0[W + 4] : 0.0f;
+    float4 o;
+    o.x = fmaxf(fmaxf(a.x, a.y), fmaxf(d.x, d.y));
+    o.y = fmaxf(fmaxf(a.y, a.z), fmaxf(d.y, d.z));
+    o.z = fmaxf(fmaxf(a.z, a.w), fmaxf(d.z, d.w));
+    o.w = fmaxf(fmaxf(a.w, a4), fmaxf(d.w, d4));
+    *reinterpret_cast<float4 *>(y + (long long)b * ybs + (long long)c * H * W + (long long)oy * W +
+                                ox) = o;
 }
 
 // ---- interpolation (ggml_interpolate, src/ppdoclayout.cpp:670-672) -----------
 // NEAREST: src = (int)(dst / sf).  BILINEAR (no align-corners): src =
 // (dst + 0.5) / sf - 0.5, floor, both taps clamped to the edge, fractional
 // weight clamped to [0, 1].  Optionally adds into y (y = base + interp).
-__global__ void interp_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
-                              long long ybs, const float *__restrict__ base, long long bbs, int C,
-                              int H, int W, int OH, int OW, int bilinear, int B) {
-    // grid (C*OH*OW / 256, B)
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= C * OH * OW) return;
-    const int c = i / (OH * OW), p = i - c * (OH * OW), b = blockIdx.y;
-    const int oy = p / OW, ox = p - oy * OW;
-    const float *xp = x + (long long)b * xbs + (long long)c * H * W;
-    const float sfx = (float)OW / (float)W, sfy = (float)OH / (float)H;
-    float v;
+__device__ __forceinline__ float interp_one(const float *__restrict__ xp, int ox, int oy, int H,
+                                            int W, float sfx, float sfy, int bilinear) {
     if (!bilinear) {
         const int sx = min((int)((float)ox / sfx), W - 1);
         const int sy = min((int)((float)oy / sfy), H - 1);
-        v = xp[(long long)sy * W + sx];
-    } else {
-        const float fx = __fsub_rn(__fdiv_rn(__fadd_rn((float)ox, 0.5f), sfx), 0.5f);
-        const float fy = __fsub_rn(__fdiv_rn(__fadd_rn((float)oy, 0.5f), sfy), 0.5f);
-        const float flx = floorf(fx), fly = floorf(fy);
-        int x0 = (int)flx, y0 = (int)fly;
-        int x1 = x0 + 1, y1 = y0 + 1;
-        const float dx = fminf(fmaxf(__fsub_rn(fx, flx), 0.0f), 1.0f);
-        const float dy = fminf(fmaxf(__fsub_rn(fy, fly), 0.0f), 1.0f);
-        x0 = max(0, min(x0, W - 1)); x1 = max(0, min(x1, W - 1));
-        y0 = max(0, min(y0, H - 1)); y1 = max(0, min(y1, H - 1));
-        const float a = xp[(long long)y0 * W + x0], bq = xp[(long long)y0 * W + x1];
-        const float cq = xp[(long long)y1 * W + x0], d = xp[(long long)y1 * W + x1];
-        v = a * (1.0f - dx) * (1.0f - dy) + bq * dx * (1.0f - dy) + cq * (1.0f - dx) * dy +
-            d * dx * dy;
+        return xp[(long long)sy * W + sx];
     }
-    const long long off = (long long)c * OH * OW + (long long)oy * OW + ox;
-    if (base) v = __fadd_rn(base[(long long)b * bbs + off], v);
-    y[(long long)b * ybs + off] = v;
+    const float fx = __fsub_rn(__fdiv_rn(__fadd_rn((float)ox, 0.5f), sfx), 0.5f);
+    const float fy = __fsub_rn(__fdiv_rn(__fadd_rn((float)oy, 0.5f), sfy), 0.5f);
+    const float flx = floorf(fx), fly = floorf(fy);
+    int x0 = (int)flx, y0 = (int)fly;
+    int x1 = x0 + 1, y1 = y0 + 1;
+    const float dx = fminf(fmaxf(__fsub_rn(fx, flx), 0.0f), 1.0f);
+    const float dy = fminf(fmaxf(__fsub_rn(fy, fly), 0.0f), 1.0f);
+    x0 = max(0, min(x0, W - 1)); x1 = max(0, min(x1, W - 1));
+    y0 = max(0, min(y0, H - 1)); y1 = max(0, min(y1, H - 1));
+    const float a = xp[(long long)y0 * W + x0], bq = xp[(long long)y0 * W + x1];
+    const float cq = xp[(long long)y1 * W + x0], d = xp[(long long)y1 * W + x1];
+    return a * (1.0f - dx) * (1.0f - dy) + bq * dx * (1.0f - dy) + cq * (1.0f - dx) * dy +
+           d * dx * dy;
+}
+
+// V consecutive output pixels of a row per thread (V = 4: one 16-byte store,
+// used when OW is a multiple of 4 and the planes are 16-byte aligned)
+template <int V>
+__global__ void interp_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
+                              long long ybs, const float *__restrict__ base, long long bbs, int C,
+                              int H, int W, int OH, int OW, int bilinear, int B) {
+    // grid (C*OH*OW / (256 V), B)
+    const int ow = OW / V;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= C * OH * ow) return;
+    const int c = i / (OH * ow), p = i - c * (OH * ow), b = blockIdx.y;
+    const int oy = p / ow, ox0 = (p - oy * ow) * V;
+    const float *xp = x + (long long)b * xbs + (long long)c * H * W;
+    const float sfx = (float)OW / (float)W, sfy = (float)OH / (float)H;
+    const long long off = (long long)c * OH * OW + (long long)oy * OW + ox0;
+    float v[V];
+#pragma unroll
+    for (int e = 0; e < V; e++) v[e] = interp_one(xp, ox0 + e, oy, H, W, sfx, sfy, bilinear);
+    if (V == 4) {
+        if (base) {
+            const float4 b4 = *reinterpret_cast<const float4 *>(base + (long long)b * bbs + off);
+            v[0] = __fadd_rn(b4.x, v[0]);
+            v[1] = __fadd_rn(b4.y, v[1]);
+            v[2] = __fadd_rn(b4.z, v[2]);
+            v[3] = __fadd_rn(b4.w, v[3]);
+        }
+        *reinterpret_cast<float4 *>(y + (long long)b * ybs + off) =
+            make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+        for (int e = 0; e < V; e++) {
+            if (base) v[e] = __fadd_rn(base[(long long)b * bbs + off + e], v[e]);
+            y[(long long)b * ybs + off + e] = v[e];
+        }
+    }
 }
 
 // ---- CHW <-> token-major ([H*W][C]) through a shared-memory tile ------------
@@ -406,12 +475,18 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
                      long long ybs, int C, int H, int W, int K, int S, int P, int act, int B,
                      cudaStream_t st) {
     const int OH = (H + 2 * P - K) / S + 1, OW = (W + 2 * P - K) / S + 1;
-    if (OH <= 0 || OW <= 0 || !grid3_ok((long long)OH * OW, C, B)) return ERR_SHAPE;
-    const dim3 g = grid3((long long)OH * OW, C, B);
-    if (K == 3)
-        dwconv_kernel<3><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, C, H, W, OH, OW, S, P, act, B);
-    else if (K == 5)
-        dwconv_kernel<5><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, C, H, W, OH, OW, S, P, act, B);
+    if (OH <= 0 || OW <= 0 || C <= 0 || C > 65535 || B <= 0 || B > 65535 || P < 0 || P >= K)
+        return ERR_SHAPE;
+    const int tiles_x = (OW + kDwTW - 1) / kDwTW, tiles_y = (OH + kDwTH - 1) / kDwTH;
+    const dim3 g(tiles_x * tiles_y, C, B);
+    if (K == 3 && S == 1)
+        dwconv_kernel<3, 1><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
+    else if (K == 3 && S == 2)
+        dwconv_kernel<3, 2><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
+    else if (K == 5 && S == 1)
+        dwconv_kernel<5, 1><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
+    else if (K == 5 && S == 2)
+        dwconv_kernel<5, 2><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
     else
         return ERR_UNSUPPORTED;
     return cuda_status();
@@ -419,8 +494,11 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
 
 Status launch_maxpool2_pad(const float *x, long long xbs, float *y, long long ybs, int C, int H,
                            int W, int B, cudaStream_t st) {
-    if (!grid3_ok((long long)H * W, C, B)) return ERR_SHAPE;
-    maxpool2_pad_kernel<<<grid3((long long)H * W, C, B), 256, 0, st>>>(x, xbs, y, ybs, C, H, W, B);
+    if (!grid3_ok((long long)H * W, C, B) || W % 4 || ((uintptr_t)x & 15) || xbs % 4 ||
+        ((uintptr_t)y & 15) || ybs % 4)
+        return ERR_SHAPE;
+    maxpool2_pad_kernel<<<grid3((long long)H * W / 4, C, B), 256, 0, st>>>(x, xbs, y, ybs, C, H, W,
+                                                                           B);
     return cuda_status();
 }
 
@@ -428,8 +506,14 @@ Status launch_interp(const float *x, long long xbs, float *y, long long ybs, con
                      long long bbs, int C, int H, int W, int OH, int OW, bool bilinear, int B,
                      cudaStream_t st) {
     if (!grid3_ok((long long)OH * OW, C, B)) return ERR_SHAPE;
-    interp_kernel<<<grid3((long long)OH * OW, C, B), 256, 0, st>>>(x, xbs, y, ybs, base, bbs, C, H,
-                                                                   W, OH, OW, bilinear ? 1 : 0, B);
+    const bool vec = OW % 4 == 0 && ((uintptr_t)y & 15) == 0 && ybs % 4 == 0 &&
+                     (!base || (((uintptr_t)base & 15) == 0 && bbs % 4 == 0));
+    if (vec)
+        interp_kernel<4><<<grid3((long long)OH * OW / 4, C, B), 256, 0, st>>>(
+            x, xbs, y, ybs, base, bbs, C, H, W, OH, OW, bilinear ? 1 : 0, B);
+    else
+        interp_kernel<1><<<grid3((long long)OH * OW, C, B), 256, 0, st>>>(
+            x, xbs, y, ybs, base, bbs, C, H, W, OH, OW, bilinear ? 1 : 0, B);
     return cuda_status();
 }
 

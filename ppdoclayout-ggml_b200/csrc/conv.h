@@ -34,7 +34,7 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
                      cudaStream_t st);
 
 // 2x2 stride-1 max pool of the input zero-padded by one row/column at the
-// end: out is H x W like the input
+// end: out is H x W like the input (W a multiple of 4, 16-byte aligned planes)
 Status launch_maxpool2_pad(const float *x, long long xbs, float *y, long long ybs, int C, int H,
                            int W, int B, cudaStream_t st);
 
