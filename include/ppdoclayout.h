@@ -98,7 +98,7 @@ PPDL_API void * ppdl_stream(ppdl_ctx * ctx);
 #define PPDL_STEP_GEMM_1X1      1   /* 1x1 conv GEMM                     */
 #define PPDL_STEP_WG_MADD       2   /* Winograd 36-plane GEMM            */
 #define PPDL_STEP_GEMM_IMPLICIT 3   /* k3-s2 / k2 implicit-GEMM conv     */
-#define PPDL_STEP_GEMM_LINEAR   4   /* linears, attention, mask GEMMs    */
+#define PPDL_STEP_GEMM_LINEAR   4   /* linears and mask GEMMs            */
 #define PPDL_STEP_WG_INPUT      5   /* Winograd input transform          */
 #define PPDL_STEP_WG_OUTPUT     6   /* Winograd output transform         */
 #define PPDL_STEP_DWCONV        7   /* depthwise conv                    */
@@ -108,6 +108,7 @@ PPDL_API void * ppdl_stream(ppdl_ctx * ctx);
 #define PPDL_STEP_POSTPROCESS   11  /* order votes, top-300, masks       */
 #define PPDL_STEP_GLUE          12  /* LN, softmax, add, interp, pool... */
 #define PPDL_STEP_IM2COL        13  /* conv operand packing for the GEMM */
+#define PPDL_STEP_ATTENTION     14  /* fused softmax(q k^T) v (SIMT FP32) */
 typedef struct {
     char    name[48];
     int32_t kind;   /* PPDL_STEP_* */

@@ -585,7 +585,7 @@ public:
         lin(qk_in, k, pfx + ".k");
         lin(v_in, v, pfx + ".v");
         // softmax(q k^T / sqrt(32)) v in one launch (scores stay on chip)
-        push(pfx + ".attn", PPDL_STEP_GEMM_LINEAR, 4.0 * kNH * T * T * kHD,
+        push(pfx + ".attn", PPDL_STEP_ATTENTION, 4.0 * kNH * T * T * kHD,
              4.0 * 4.0 * T * kDM, [=]() {
             return launch_attention(q.p, k.p, v.p, o.p, T, kNH, kDM, (long long)T * kDM,
                                     1.0f / sqrtf((float)kHD), nb, st);
