@@ -354,11 +354,11 @@ FWD_B = 8
 GEMM_KINDS = ("gemm_1x1", "wg_madd", "gemm_implicit", "gemm_linear")
 HBM_KINDS = ("wg_input", "wg_output", "dwconv", "msda", "mask_box", "glue", "postprocess", "topk",
              "im2col")
-SIMT_KINDS = ("attention",)  # FP32 CUDA-core work: reported with its FLOP rate, no roofline class
+SIMT_KINDS = ("attention",)  # FP32 CUDA-core q-k products: their FLOP rate, no roofline class
 # DRAM traffic of the tensor-core GEMM per page of one forward (sum over its
 # launches of dram__bytes_read.sum + dram__bytes_write.sum), from an ncu
 # capture of one eager forward at 2 pages; None until measured.
-TC_GEMM_DRAM_BYTES_PER_PAGE = None
+TC_GEMM_DRAM_BYTES_PER_PAGE = 1.5927e9  # 3.185 GB over the 212 launches of 2 pages
 
 
 def _fwd_pages(rank, B):
@@ -403,6 +403,11 @@ def run_forward(args, world, rank, local, pg):
     hw = np.full((B, 2), 800, np.int32)
     d_img = torch.from_numpy(pages).to(dev)
     st = torch.cuda.ExternalStream(ctx.stream_ptr(), device=dev)
+    if args.capture_once:
+        torch.cuda.synchronize(dev)
+        if ctx.infer_device(d_img.data_ptr(), B, hw) != 0 or ctx.sync() != 0:
+            raise RuntimeError("forward failed")
+        return None
 
     def step():
         rc = ctx.infer_device(d_img.data_ptr(), B, hw)
@@ -554,6 +559,9 @@ def cpu_baseline_forward(gguf, budget_s=10.0, sample_pages=None):
 def run_reference(args, world, rank):
     if rank != 0:
         return None
+    if args.workload == "gemm":
+        return {"impl": "reference", "unavailable": "the gemm workload is a kernel-level "
+                "measurement of this build only; the reference arm times the forward"}
     if args.workload == "forward":
         import synth
         gguf = synth.cached_gguf(0)
@@ -605,18 +613,93 @@ def run_reference(args, world, rank):
     raise SystemExit(f"unknown workload {args.workload}")
 
 
+# ------------------------------------------------- tensor-core GEMM, standalone
+GEMM_SHAPE = (40000, 256, 1024, 8)  # 1x1 conv 1024 -> 256 on 200 x 200 planes, 8 pages
+
+
+def run_gemm(args, world, rank, local, pg):
+    """The dominant kernel alone: ppdl_gemm_tf32x3 (3xTF32 tcgen05) on one
+    shape, A M-major (CHW activations), B [N][K] weights; each step is one
+    launch over all pages (the weight split included, as the entry point does
+    it per call).  Inputs are larger than L2."""
+    import ctypes as C
+    import torch
+    import ppdl
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    M, N, K, B = (tuple(int(v) for v in args.gemm.split(",")) if args.gemm else GEMM_SHAPE)
+    L = ppdl.lib()
+    L.ppdl_gemm_tf32x3.argtypes = ([C.c_int] * 4 + [C.c_void_p, C.c_int, C.c_longlong,
+                                   C.c_longlong, C.c_void_p, C.c_void_p, C.c_void_p]
+                                   + [C.c_longlong] * 3 + [C.c_void_p])
+    g = torch.Generator(device="cpu").manual_seed(7 + rank)
+    A = torch.randn((B, K, M), generator=g).to(dev)
+    W = (torch.randn((N, K), generator=g) / K ** 0.5).to(dev)
+    ws = torch.empty(2 * N * K, device=dev)
+    out = torch.empty((B, N, M), device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        rc = L.ppdl_gemm_tf32x3(M, N, K, B, A.data_ptr(), 1, M, M * K, W.data_ptr(),
+                                ws.data_ptr(), out.data_ptr(), 1, M, M * N, stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"ppdl_gemm_tf32x3 returned {rc}: {ppdl.last_error()}")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    barrier(pg)
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    clk = clocks.stop()
+    ms = max_over_ranks(pg, t0.elapsed_time(t1)) / args.steps
+    flops = 2.0 * M * N * K * B
+    tflops = flops * world / (ms / 1e3) / 1e12
+    hbm, bf16, peak_kind = _peaks()
+    tc = bf16 / 6.0
+    per_gpu = flops / (ms / 1e3) / 1e12
+    return {
+        "metric": "3xTF32 tensor-core GEMM TFLOP/s (dominant kernel of the forward, alone)",
+        "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 on tcgen05)",
+        "data": "seeded normal A, weights scaled by 1/sqrt(K)",
+        "config": {"workload": f"ppdl_gemm_tf32x3 M={M} N={N} K={K} x {B} pages (CHW A)",
+                   "l2": "inputs larger than L2", "parallelism": f"dp{world} (no collective)"},
+        "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2), "peak": round(tc, 1),
+                     "unit": "TFLOP/s", "frac": round(per_gpu / tc, 4),
+                     "peak_kind": f"{peak_kind} bf16 dense burst / 6 (3xTF32)",
+                     "algorithmic_bytes": 4 * (M * K * B + M * N * B + 2 * N * K)},
+        "gpu_launches": 2 * (args.steps),
+        "clocks": clk,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="forward", choices=["forward", "msda"])
+    ap.add_argument("--workload", default="forward", choices=["forward", "msda", "gemm"])
+    ap.add_argument("--gemm", default="",
+                    help="gemm workload shape M,N,K,pages (default 40000,256,1024,8)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pages", type=int, default=0,
                     help="pages per GPU per step of the forward workload (default 8, config 3); "
                          "smaller values are for profiler captures")
+    ap.add_argument("--capture-once", action="store_true",
+                    help="forward workload: set up, run one eager forward, print nothing and "
+                         "exit (the launch sequence of one forward, for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -626,6 +709,8 @@ def main():
             line = run_reference(args, world, rank)
         elif args.workload == "forward":
             line = run_forward(args, world, rank, local, pg)
+        elif args.workload == "gemm":
+            line = run_gemm(args, world, rank, local, pg)
         else:
             line = run_msda(args, world, rank, local, pg)
         if rank == 0 and line is not None:

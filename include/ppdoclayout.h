@@ -108,7 +108,8 @@ PPDL_API void * ppdl_stream(ppdl_ctx * ctx);
 #define PPDL_STEP_POSTPROCESS   11  /* order votes, top-300, masks       */
 #define PPDL_STEP_GLUE          12  /* LN, softmax, add, interp, pool... */
 #define PPDL_STEP_IM2COL        13  /* conv operand packing for the GEMM */
-#define PPDL_STEP_ATTENTION     14  /* fused softmax(q k^T) v (SIMT FP32) */
+#define PPDL_STEP_ATTENTION     14  /* q-k products on SIMT FP32: fused
+                                       softmax(q k^T) v, reading-order scores */
 typedef struct {
     char    name[48];
     int32_t kind;   /* PPDL_STEP_* */

@@ -892,7 +892,7 @@ public:
         order = seq(kNQ, kNQ);
         {
             const S o = order;
-            push("order", PPDL_STEP_GEMM_LINEAR, 2.0 * kNQ * kNQ * 64, 4.0 * kNQ * (kNQ + 128.0),
+            push("order", PPDL_STEP_ATTENTION, 2.0 * kNQ * kNQ * 64, 4.0 * kNQ * (kNQ + 128.0),
                  [=]() {  // order[b][i][j] = q_i . k_j / 8
                 GemmArgs g;
                 g.M = kNQ; g.N = kNQ; g.K = 64; g.batch = nb;
