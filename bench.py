@@ -2,9 +2,18 @@
 """Benchmark of the B200 PP-DocLayoutV3 hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload msda]
+                    [--workload forward|msda|gemm] [--pages P] [--gemm M,N,K,P]
+                    [--capture-once]
 
 Workloads
+  forward  (default) config 3 of the baseline: the full PP-DocLayoutV3 forward
+           plus the postprocess on 800x800 pages, FP32, 8 pages per GPU per
+           step, replayed from its CUDA graph with the inputs in HBM.  `value`
+           is pages/s; `e2e` is ppdl_infer_batch with host images in and
+           detections + masks out; `stages` / `top_steps` / `roofline` come
+           from the per-step device profile (ppdl_profile_steps); the CPU
+           baseline is the oracle's restatement of the forward on the host
+           threads.  The per-step working set (~6 GB) is larger than L2.
   msda     config 1 of the baseline: the MSDeformAttn operator alone, FP32,
            value [B,13125,8,32] ~ N(0,1), sampling locations
            [B,300,8,3,4,2] ~ U[0,1], weights softmax(N(0,1)) over 12, at
@@ -12,15 +21,23 @@ Workloads
            smaller B are parity-test cases).  One step = one launch over the
            batch.  The 430 MB value tensor is larger than the 126 MB L2, so
            nothing stays cached between steps.
+  gemm     the forward's dominant kernel alone: ppdl_gemm_tf32x3 (3xTF32 on
+           tcgen05) on one shape, default the 200x200-plane 1x1 conv 1024 ->
+           256 over 8 pages.
+
+`--capture-once` (forward): set up, run one eager forward and exit — the
+launch sequence of one forward, for profiler captures.
 
 Multi-GPU: one process per GPU (torchrun), every rank runs its own pages
 (weak scaling, no data-path collective); the timed region is bracketed by a
 gloo barrier + device synchronise and the slowest rank's time is reported.
 
-`--impl reference` times the reference's own CPU operator (op_msdeform of
-src/ppdoclayout.cpp:142-198, compiled from the reference sources into
-oracle/_ref/, or the oracle restatement when that build is absent) on all
-host cores, rank 0 only.
+`--impl reference` times the reference's CPU path of the workload on all
+host cores, rank 0 only: for the forward the oracle's restatement (the
+reference's ggml CPU graph cannot be built here), for msda the reference's
+own op_msdeform (src/ppdoclayout.cpp:142-198, compiled from the reference
+sources into oracle/_ref/, or the oracle restatement when that build is
+absent).
 """
 from __future__ import annotations
 
