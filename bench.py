@@ -123,7 +123,11 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------- distributed
-def dist_setup(args):
+def dist_setup(args, timeout_s: float = 120.0):
+    """Rank layout from the torchrun environment; a gloo group (timing
+    barrier and max/sum reductions only) when there are several ranks.  The
+    group timeout bounds every collective, so a rank that died makes the
+    others fail instead of waiting."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -133,7 +137,7 @@ def dist_setup(args):
         import torch.distributed as dist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("gloo", rank=rank, world_size=world,
-                                timeout=datetime.timedelta(seconds=120))
+                                timeout=datetime.timedelta(seconds=timeout_s))
         pg = dist
     return world, rank, local, pg
 
@@ -159,6 +163,12 @@ def sum_over_ranks(pg, v: float) -> float:
     t = torch.tensor([v], dtype=torch.float64)
     pg.all_reduce(t, op=pg.ReduceOp.SUM)
     return float(t.item())
+
+
+def job_rate(units_per_rank_step: float, steps: int, world: int, ms_max: float) -> float:
+    """Whole-job throughput: the units all ranks processed divided by the
+    slowest rank's device time (weak scaling: every rank does the same work)."""
+    return units_per_rank_step * steps * world / (ms_max / 1e3)
 
 
 # ------------------------------------------------------------------ MSDA (cfg 1)
@@ -452,7 +462,7 @@ def run_forward(args, world, rank, local, pg):
     clk = clocks.stop()
     total_ms = t0.elapsed_time(t1)
     total_ms_max = max_over_ranks(pg, total_ms)
-    value = B * K * world / (total_ms_max / 1e3)
+    value = job_rate(B, K, world, total_ms_max)
 
     # per-step device profile of one eager forward (kernel classes, roofline)
     steps = ctx.profile_steps(B)
