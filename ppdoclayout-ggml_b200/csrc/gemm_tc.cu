@@ -727,6 +727,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             float *Crow = C + (long long)m * e.ldc_m;
             const float *Rrow = R ? R + (long long)m * e.res_ldm : nullptr;
             const int c_hi = pbn < c_lo + kHalfCols ? pbn : c_lo + kHalfCols;
+            const bool ops = ACT != ACT_NONE || e.alpha != 1.0f || e.bias || e.res_mode;
             const uint32_t xt = tmem_base + lane_base + (uint32_t)(last * kSlotCols);
 #pragma unroll 1
             for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
@@ -744,17 +745,37 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         __syncwarp();
                     }
                     float *box = staging_ptr + (size_t)(ew * 2 + b) * (kBoxBytes / 4);
+                    // raw values first (16 stores), then alpha / bias / residual
+                    // / activation in a rolled loop over the box: a small loop
+                    // body, executed once per tile, keeps instruction fetch short
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const int n = n0 + c0 + j;
-                        const bool ok_n = n < pN;
-                        float x = __uint_as_float(v[j]);
-                        if (e.alpha != 1.0f) x = x * e.alpha;
-                        if (e.bias && ok_n) x = x + __ldg(e.bias + n);
-                        if (e.res_mode == 1 && ok_n && row_ok) x = x + Rrow[(long long)n * e.res_ldn];
-                        x = act_apply(x, ACT);
-                        if (e.res_mode == 2 && ok_n && row_ok) x = x + Rrow[(long long)n * e.res_ldn];
-                        box[j * 32 + lane] = x;
+                    for (int j = 0; j < 16; j++) box[j * 32 + lane] = __uint_as_float(v[j]);
+                    if (ops) {
+                        // four columns at a time: their bias and residual loads
+                        // are issued together, the op order per element is
+                        // alpha, + bias, + residual (mode 1), act, + residual (2)
+#pragma unroll 1
+                        for (int j0 = 0; j0 < 16; j0 += 4) {
+                            float bb[4], rr[4];
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                const int n = n0 + c0 + j0 + u;
+                                const bool ok_n = n < pN;
+                                bb[u] = (e.bias && ok_n) ? __ldg(e.bias + n) : 0.0f;
+                                rr[u] = (e.res_mode && ok_n && row_ok)
+                                            ? Rrow[(long long)n * e.res_ldn] : 0.0f;
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                float x = box[(j0 + u) * 32 + lane];
+                                if (e.alpha != 1.0f) x = x * e.alpha;
+                                if (e.bias) x = x + bb[u];
+                                if (e.res_mode == 1) x = x + rr[u];
+                                x = act_apply(x, ACT);
+                                if (e.res_mode == 2) x = x + rr[u];
+                                box[(j0 + u) * 32 + lane] = x;
+                            }
+                        }
                     }
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     __syncwarp();
