@@ -22,9 +22,9 @@
 //                tcgen05.commit frees the stage / publishes the partials;
 //   warps 0-3,   epilogue: tcgen05.ld 32x32b from the lane quadrant of
 //   8-11         their warp, FP32 folding of the partials, bias / residual /
-//                activation; CHW outputs leave through shared-memory boxes
-//                and TMA stores (asynchronous, clipped at the tensor edges),
-//                other layouts through direct global stores.
+//                activation; CHW and token-major outputs leave through
+//                shared-memory boxes and TMA stores (asynchronous, clipped at
+//                the tensor edges), other layouts through direct stores.
 // Four TMEM partial slots let the MMAs run ahead of the epilogue's folds and
 // overlap a tile's stores with the next tile's main loop.
 //
@@ -734,7 +734,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const uint32_t xa = xt;
                 uint32_t v[16];
                 tmem_ld16(xa + (uint32_t)c0, v);
-                if (ptma) {
+                if (ptma == 1) {
                     // CHW output: the warp's 32 pixels x 16 channels go into a
                     // staging box (lane = pixel, conflict-free rows of 128 B)
                     // and out with one TMA store, which clips rows >= M and
@@ -785,6 +785,63 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         if (m0 + quad * 32 < pM && n0 + c0 < pN)
                             tma_store_3d(&tmC, staging + (uint32_t)((ew * 2 + b) * kBoxBytes),
                                          m0 + quad * 32, n0 + c0, z);
+                        bulk_commit();
+                    }
+                    nbox++;
+                    continue;
+                }
+                if (ptma == 2) {
+                    // token-major output: the warp's 32 rows x 16 columns go into
+                    // a row-major staging box (lane = row, four 16-byte stores)
+                    // and out with one TMA store; the ops pass walks the box
+                    // linearly, so consecutive lanes touch consecutive words
+                    const int b = nbox & 1;
+                    if (nbox >= 2) {
+                        if (lane == 0) bulk_wait_read_1();
+                        __syncwarp();
+                    }
+                    float *box = staging_ptr + (size_t)(ew * 2 + b) * (kBoxBytes / 4);
+                    float4 *row4 = reinterpret_cast<float4 *>(box + lane * 16);
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        row4[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                              __uint_as_float(v[4 * q + 2]),
+                                              __uint_as_float(v[4 * q + 3]));
+                    if (ops) {
+                        __syncwarp();  // the pass reads the other lanes' rows
+#pragma unroll 1
+                        for (int i0 = 0; i0 < 16; i0 += 4) {
+                            float bb[4], rr[4];
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                const int idx = (i0 + u) * 32 + lane;
+                                const int n = n0 + c0 + (idx & 15);
+                                const int mr = m0 + quad * 32 + (idx >> 4);
+                                const bool okk = n < pN && mr < pM;
+                                bb[u] = (e.bias && okk) ? __ldg(e.bias + n) : 0.0f;
+                                rr[u] = (e.res_mode && okk)
+                                            ? R[(long long)mr * e.res_ldm + (long long)n * e.res_ldn]
+                                            : 0.0f;
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                const int idx = (i0 + u) * 32 + lane;
+                                float x = box[idx];
+                                if (e.alpha != 1.0f) x = x * e.alpha;
+                                if (e.bias) x = x + bb[u];
+                                if (e.res_mode == 1) x = x + rr[u];
+                                x = act_apply(x, ACT);
+                                if (e.res_mode == 2) x = x + rr[u];
+                                box[idx] = x;
+                            }
+                        }
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (m0 + quad * 32 < pM && n0 + c0 < pN)
+                            tma_store_3d(&tmC, staging + (uint32_t)((ew * 2 + b) * kBoxBytes),
+                                         n0 + c0, m0 + quad * 32, z);
                         bulk_commit();
                     }
                     nbox++;
@@ -960,19 +1017,28 @@ bool plan_common(TcGemm *g, int M, int N, int K, int batch, int planes, const Tc
     return true;
 }
 
-// A CHW output (pixels contiguous) whose channel and page strides are
-// 16-byte multiples is stored by TMA through the staging boxes; any other
-// output keeps the direct global stores.
+// An output whose strides are 16-byte multiples — CHW (pixels contiguous)
+// or token-major (columns contiguous) — is stored by TMA through the
+// staging boxes; any other output keeps the direct global stores.
 void encode_c(TcGemm *g) {
     const TcEpilogue &e = g->epi;
     g->tma_c = 0;
-    if (e.ldc_m != 1 || e.ldc_n <= 0 || e.c_bs < 0 || ((uintptr_t)e.C & 15) ||
-        (e.ldc_n * 4) % 16 || (e.c_bs * 4) % 16 || (g->batch > 1 && e.c_bs == 0))
+    if (e.c_bs < 0 || ((uintptr_t)e.C & 15) || (e.c_bs * 4) % 16 ||
+        (g->batch > 1 && e.c_bs == 0))
         return;
-    if (encode3d(&g->tmC, e.C, (uint64_t)g->M, (uint64_t)g->N, (uint64_t)g->batch,
-                 (uint64_t)e.ldc_n * 4, (uint64_t)e.c_bs * 4, 32, kBoxN,
-                 CU_TENSOR_MAP_SWIZZLE_NONE))
-        g->tma_c = 1;
+    if (e.ldc_m == 1 && e.ldc_n > 0 && (e.ldc_n * 4) % 16 == 0) {
+        // CHW: pixels contiguous, boxes of 32 pixels x 16 channels
+        if (encode3d(&g->tmC, e.C, (uint64_t)g->M, (uint64_t)g->N, (uint64_t)g->batch,
+                     (uint64_t)e.ldc_n * 4, (uint64_t)e.c_bs * 4, 32, kBoxN,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+            g->tma_c = 1;
+    } else if (e.ldc_n == 1 && e.ldc_m > 0 && (e.ldc_m * 4) % 16 == 0) {
+        // token-major: columns contiguous, boxes of 16 columns x 32 rows
+        if (encode3d(&g->tmC, e.C, (uint64_t)g->N, (uint64_t)g->M, (uint64_t)g->batch,
+                     (uint64_t)e.ldc_m * 4, (uint64_t)e.c_bs * 4, kBoxN, 32,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+            g->tma_c = 2;
+    }
 }
 
 // B hi/lo tensor maps over [planes][N][ldk] halves, k < ldk (16-byte rows).

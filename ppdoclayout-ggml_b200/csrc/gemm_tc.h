@@ -43,7 +43,7 @@ struct TcGather {
 
 struct TcGemm {
     CUtensorMap tmA, tmBhi, tmBlo;
-    CUtensorMap tmC;     // CHW output (ldc_m == 1) stored by TMA when tma_c
+    CUtensorMap tmC;     // output stored by TMA: tma_c 1 = CHW, 2 = token-major rows
     int tma_c = 0;
     int M = 0, N = 0, K = 0, batch = 1, planes = 1;
     int a_mn = 1;        // 1: A is M-major (128B-base-32B swizzle), 0: K-major
