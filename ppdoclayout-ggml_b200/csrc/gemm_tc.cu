@@ -9,32 +9,41 @@
 // hi_A*hi_B + hi_A*lo_B + lo_A*hi_B in FP32 — the classic 3xTF32 scheme,
 // ~2^-21 relative per product, inside the hot path's 1e-5 gate.
 //
-// Kernel structure (persistent, one CTA per SM, 384 threads):
-//   warp 6       TMA producer: A tile (FP32 activation) + B hi/lo tiles
+// Kernel structure (persistent, one CTA per SM, 512 threads):
+//   warp 12      TMA producer: A tile (FP32 activation) + B hi/lo tiles
 //                (weights pre-split at init) into a stage of shared memory;
-//   warps 4-5    converter: split the A tile in place (hi over the raw
-//                values, lo into a twin buffer with the same layout), then
-//                fence.proxy.async so the tensor core sees the writes — or,
-//                in gather mode, build the A tile from a CHW conv input
-//                (implicit GEMM, any plane stride) instead of TMA;
-//   warp 7       MMA issuer: one thread issues tcgen05.mma kind::tf32
-//                (M=128, N=bn, K=8) x3 per K step into TMEM,
-//                tcgen05.commit frees the stage / publishes the partials;
+//   warps 4-7    converter, one warp per TMEM lane quadrant: each thread
+//                reads one row of the stage's A tile (32 k values), splits
+//                it into TF32 hi / lo and writes both into a TMEM A stage
+//                with tcgen05.st — or, in gather mode, first builds its row
+//                from a CHW conv input (implicit GEMM, any plane stride);
+//   warps 13-14  MMA issuers: one thread each, taking alternate k-blocks,
+//                issues tcgen05.mma kind::tf32 with A read from TMEM and B
+//                from shared memory (M=128, N=bn, K=8), x3 per K step; one
+//                tcgen05.commit per k-block frees the stage, the TMEM A
+//                stage and publishes the partial;
 //   warps 0-3,   epilogue: tcgen05.ld 32x32b from the lane quadrant of
 //   8-11         their warp, FP32 folding of the partials, bias / residual /
 //                activation; CHW and token-major outputs leave through
 //                shared-memory boxes and TMA stores (asynchronous, clipped at
-//                the tensor edges), other layouts through direct stores.
-// Four TMEM partial slots let the MMAs run ahead of the epilogue's folds and
+//                the tensor edges), other layouts through direct stores;
+//   warp 15      idle (it completes the fourth warpgroup's register split).
+// The A operand comes from TMEM because a TF32 MMA that reads both operands
+// from shared memory runs at 153 cycles per 128x128x8 step on the B200
+// against 64 with A in TMEM (measured back to back on one SM).
+// An MMA issue blocks until the tensor pipe accepts it, so a lone issuing
+// thread leaves the pipe idle through its waits and bookkeeping between
+// k-blocks; with two, one thread's bookkeeping overlaps the other's MMAs
+// (each tcgen05.commit tracks only its own thread's MMAs, and alternate
+// k-blocks use disjoint TMEM slots and A stages).
+// Three TMEM partial slots let the MMAs run ahead of the epilogue's folds and
 // overlap a tile's stores with the next tile's main loop.
 //
 // Layouts: A is either M-major — a CHW activation, pixels contiguous — read
-// by TMA boxes of 32 pixels x 32 channels with the 128-byte swizzle on a
-// 32-byte atom (the one M-major form UMMA accepts for TF32; descriptor
-// layout type 1), or K-major (token-major rows or the gathered conv tile,
-// 128-byte swizzle).  B is K-major [N][K] with the 128-byte swizzle.  The
-// element-wise split does not depend on the swizzle, so it runs in place on
-// the TMA image.
+// by one TMA box of 128 pixels x 32 channels without swizzle (a converter
+// lane reads its pixel down the 32 channel rows), or K-major (token-major
+// rows or the gathered conv tile, 128-byte swizzle: a lane reads the eight
+// 16-byte chunks of its row).  B is K-major [N][K] with the 128-byte swizzle.
 //
 // Every mbarrier wait is bounded (~2 s of clock64); on expiry the kernel
 // raises a device error flag, all roles drain out, pending TMA and MMA work
@@ -53,23 +62,32 @@ __device__ int g_tc_error = 0;
 namespace {
 
 constexpr int kBM = 128, kBK = 32;
-// warps 0-3 and 8-11 epilogue, 4-5 converter, 6 TMA producer, 7 MMA issuer
-constexpr int kThreads = 384;
-constexpr int kWarpProducer = 6, kWarpMma = 7, kWarpEpi2 = 8;
-constexpr int kConvThreads = 64;
+// warps 0-3 and 8-11 epilogue, 4-7 converter, 12 TMA producer, 13 MMA issuer
+constexpr int kThreads = 512;
+constexpr int kWarpConv = 4, kWarpEpi2 = 8, kWarpProducer = 12, kWarpMma = 13, kMmaWarps = 2;
+constexpr int kConvThreads = 128;
 constexpr int kEpiThreads = 256;
 constexpr int kHalfCols = 64;  // columns of the N tile per epilogue warp
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kTimeoutCycles = 4000000000LL;
-constexpr int kMaxStages = 4;
+constexpr int kMaxStages = 6;
 constexpr int kABytes = kBM * kBK * 4;  // 16 KB
-// TMEM (512 columns): four partial slots of 128 columns, one k-block of all
-// three products each (4 large + 8 small MMA adds); the running total lives
-// in epilogue registers.
-constexpr int kSlots = 4;
+// TMEM (512 columns): three partial slots of 128 columns, one k-block of all
+// three products each (4 large + 8 small MMA adds; the running total lives
+// in epilogue registers), then two A stages of 64 columns (hi in the first
+// 32, lo in the next 32; lane = row of the A tile, column = k).
+constexpr int kSlots = 3;
 constexpr int kSlotCols = 128;
+constexpr int kAStages = 2;
+constexpr int kACol0 = kSlots * kSlotCols;
+constexpr int kACols = 2 * kBK;
 constexpr int kMaxBN = 128;
-static_assert(kSlots * kSlotCols <= (int)kTmemCols, "partial slots exceed TMEM");
+static_assert(kACol0 + kAStages * kACols <= (int)kTmemCols, "TMEM columns exceeded");
+// Waiters on a stage's empty barrier (the epilogue for a partial, the
+// converter for a TMEM A stage) rely on the stage ring being at least as
+// long as the slot and A-stage rings, so that a barrier cannot complete a
+// second phase before they look; the planner keeps stages >= kMinStages.
+constexpr int kMinStages = kSlots > kAStages ? kSlots : kAStages;
 
 // Epilogue staging for TMA stores of CHW outputs: per epilogue warp two
 // boxes of 32 pixels x 16 channels (2 KB each).
@@ -79,10 +97,13 @@ constexpr int kStagingBytes = 8 * 2 * kBoxBytes;  // 32 KB
 constexpr int kCtrlBytes = 2048;                 // control block + 1024-alignment slack
 constexpr int kSmemMax = 227 * 1024;
 
-// Registers per thread: at launch (the __launch_bounds__(384, 1) maximum,
-// checked on the host before every launch) and after the setmaxnreg split.
-constexpr int kLaunchRegs = 168, kRegsIssue = 88, kRegsEpi = 208;
-static_assert(128 * kRegsIssue + 256 * kRegsEpi <= kThreads * kLaunchRegs,
+// Registers per thread: at launch (the __launch_bounds__(512, 1) maximum,
+// checked on the host before every launch) and after the setmaxnreg split
+// (converter and producer / MMA warpgroups down, the two epilogue
+// warpgroups up; each role sets its count in its own branch, because after a
+// join the compiler may only assume the smaller one).
+constexpr int kLaunchRegs = 128, kRegsConv = 96, kRegsMma = 48, kRegsEpi = 184;
+static_assert(128 * kRegsConv + 128 * kRegsMma + 256 * kRegsEpi <= kThreads * kLaunchRegs,
               "register split exceeds the block's register pool");
 
 struct Args {
@@ -191,13 +212,14 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
     return d;
 }
 
-__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                          uint32_t accumulate) {
+// D (TMEM) (+)= A (TMEM, 128 lanes x 8 columns) * B (shared-memory descriptor)
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                             uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -299,22 +321,28 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         "r"(r[15])
         : "memory");
 }
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+        : "memory");
+}
 __device__ __forceinline__ float tf32_rna(float x) {
     uint32_t r;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
     return __uint_as_float(r);
 }
 
-// Gather mode: one converter thread builds rows ct and ct + 64 of a stage's
-// A tile (pixels m0 + row, k = k0 .. k0 + 31) straight from the CHW input
-// with 4-byte cp.async copies (zero-filled outside the image or past K/M),
-// into the K-major 128-byte-swizzled layout (16-byte chunk c of row r at
-// chunk position c ^ (r & 7)); gather_split_rows later splits the same rows
-// in place once the copies have landed.  Lanes run over consecutive pixels,
-// so every copy instruction reads one contiguous (stride S) run of an input
-// row.  oy0/ox0 hold each row's top-left input coordinate (oy*S - P,
-// ox*S - P), oy0 = -64 for rows past M (below any kernel tap, and small
-// enough that oy0 * W cannot overflow).
+// Gather mode: converter thread ct builds row ct of a stage's A tile
+// (pixel m0 + ct, k = k0 .. k0 + 31) straight from the CHW input with 4-byte
+// cp.async copies (zero-filled outside the image or past K/M), into the
+// K-major 128-byte-swizzled layout (16-byte chunk c of row r at chunk
+// position c ^ (r & 7)), the layout of a TMA-loaded K-major tile; the same
+// thread later reads the row back for the split (split_row_kmajor).  Lanes
+// run over consecutive pixels, so every copy instruction reads one
+// contiguous (stride S) run of an input row.  oy0/ox0 hold the row's
+// top-left input coordinate (oy*S - P, ox*S - P), oy0 = -64 for rows past M
+// (below any kernel tap, and small enough that oy0 * W cannot overflow).
 __device__ __forceinline__ void cp_async4(uint32_t dst, const float *src, bool valid) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src),
                  "r"(valid ? 4 : 0)
@@ -322,24 +350,18 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const float *src, bool v
 }
 
 __device__ __forceinline__ void gather_issue(const TcGather &g, int K, const float *__restrict__ xz,
-                                             uint32_t stage, int ct, const int (&oy0)[2],
-                                             const int (&ox0)[2], int k0) {
-    uint32_t row_dst[2];
-#pragma unroll
-    for (int i = 0; i < 2; i++) row_dst[i] = stage + (uint32_t)(ct + 64 * i) * 128u;
-    const uint32_t sw = (uint32_t)(ct & 7);  // (ct + 64) & 7 == ct & 7
+                                             uint32_t stage, int ct, int oy0, int ox0, int k0) {
+    const uint32_t row_dst = stage + (uint32_t)ct * 128u;
+    const uint32_t sw = (uint32_t)(ct & 7);
     if (g.KS == 1) {
         // pointwise conv: A(m, k) = x[k][m] (S = 1, P = 0)
+        const bool in_m = oy0 >= 0;
+        const float *xm = xz + (in_m ? oy0 * g.W + ox0 : 0);
 #pragma unroll 8
         for (int j = 0; j < kBK; j++) {
-            const bool kv = k0 + j < K;
-            const float *xc = xz + (long long)(k0 + j) * g.plane;
+            const bool in = in_m && k0 + j < K;
             const uint32_t off = ((((uint32_t)j >> 2) ^ sw) << 4) + ((uint32_t)j & 3u) * 4u;
-#pragma unroll
-            for (int i = 0; i < 2; i++) {
-                const bool in = kv && oy0[i] >= 0;
-                cp_async4(row_dst[i] + off, in ? xc + (oy0[i] * g.W + ox0[i]) : xz, in);
-            }
+            cp_async4(row_dst + off, in ? xm + (long long)(k0 + j) * g.plane : xz, in);
         }
     } else {
         const int kk2 = g.KS * g.KS;
@@ -352,12 +374,9 @@ __device__ __forceinline__ void gather_issue(const TcGather &g, int K, const flo
             const bool kv = k0 + j < K;
             const float *xc = xz + (long long)ic * g.plane + kh * g.W + kw;
             const uint32_t off = ((((uint32_t)j >> 2) ^ sw) << 4) + ((uint32_t)j & 3u) * 4u;
-#pragma unroll
-            for (int i = 0; i < 2; i++) {
-                const int iy = oy0[i] + kh, ix = ox0[i] + kw;
-                const bool in = kv && (unsigned)iy < (unsigned)g.H && (unsigned)ix < (unsigned)g.W;
-                cp_async4(row_dst[i] + off, in ? xc + (oy0[i] * g.W + ox0[i]) : xz, in);
-            }
+            const int iy = oy0 + kh, ix = ox0 + kw;
+            const bool in = kv && (unsigned)iy < (unsigned)g.H && (unsigned)ix < (unsigned)g.W;
+            cp_async4(row_dst + off, in ? xc + (oy0 * g.W + ox0) : xz, in);
             if (++kw == g.KS) {
                 kw = 0;
                 if (++kh == g.KS) {
@@ -370,27 +389,43 @@ __device__ __forceinline__ void gather_issue(const TcGather &g, int K, const flo
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// In-place 3xTF32 split of this thread's two gathered rows (hi over the
-// raw values, lo into the twin buffer), then publish them to the async proxy.
-__device__ __forceinline__ void gather_split_rows(uint8_t *stage, int ct) {
-    float4 *hi = reinterpret_cast<float4 *>(stage);
-    float4 *lo = hi + kABytes / 16;
+// 3xTF32 split of 8 values into TMEM: hi = x with the low 13 mantissa bits
+// cleared (exactly TF32), lo = x - hi (exact in FP32); hi goes to columns
+// col .. col + 7 of the warp's lane quadrant, lo 32 columns further.
+__device__ __forceinline__ void split_store8(uint32_t col, const float (&x)[8]) {
+    uint32_t h[8], l[8];
 #pragma unroll
-    for (int i = 0; i < 2; i++) {
-        const int r = ct + 64 * i;
-#pragma unroll
-        for (int c = 0; c < kBK / 4; c++) {
-            const int idx = r * (kBK / 4) + c;
-            const float4 v = hi[idx];
-            float4 h, l;
-            h.x = tf32_rna(v.x); h.y = tf32_rna(v.y);
-            h.z = tf32_rna(v.z); h.w = tf32_rna(v.w);
-            l.x = v.x - h.x; l.y = v.y - h.y; l.z = v.z - h.z; l.w = v.w - h.w;
-            hi[idx] = h;
-            lo[idx] = l;
-        }
+    for (int u = 0; u < 8; u++) {
+        h[u] = __float_as_uint(x[u]) & 0xFFFFE000u;
+        l[u] = __float_as_uint(x[u] - __uint_as_float(h[u]));
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tmem_st8(col, h);
+    tmem_st8(col + kBK, l);
+}
+
+// The thread's row r of a K-major 128-byte-swizzled A tile (TMA-loaded or
+// gathered) into the TMEM A stage at column col.
+__device__ __forceinline__ void split_row_kmajor(const uint8_t *tile, int r, uint32_t col) {
+    const float4 *row = reinterpret_cast<const float4 *>(tile + (size_t)r * 128);
+#pragma unroll
+    for (int h = 0; h < 4; h++) {
+        const float4 v0 = row[(2 * h) ^ (r & 7)], v1 = row[(2 * h + 1) ^ (r & 7)];
+        const float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        split_store8(col + 8 * h, x);
+    }
+}
+
+// The thread's row r (a pixel) of an M-major A tile stored as 32 channel
+// rows of 128 pixels (no swizzle) into the TMEM A stage at column col.
+__device__ __forceinline__ void split_row_mmajor(const uint8_t *tile, int r, uint32_t col) {
+    const float *t = reinterpret_cast<const float *>(tile) + r;
+#pragma unroll
+    for (int h = 0; h < 4; h++) {
+        float x[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) x[u] = t[(8 * h + u) * kBM];
+        split_store8(col + 8 * h, x);
+    }
 }
 
 template <int ACT>
@@ -400,11 +435,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                const __grid_constant__ Args a) {
     extern __shared__ uint8_t smem_raw[];
     // control block: mbarriers + tmem base + abort flag, then 1024-aligned stages
+    //   full[s]   TMA bytes of stage s landed (producer arrive + tx)
+    //   empty[s]  the MMAs of the k-block in stage s completed (one
+    //             tcgen05.commit): stage s is free, and so are that
+    //             k-block's TMEM A stage and its partial slot may be folded
+    //   afull[j]  TMEM A stage j written by the 128 converter threads
+    //   pempty[p] partial slot p folded by the 256 epilogue threads
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t ctrl = raw;
-    const uint32_t bar_full = ctrl, bar_conv = ctrl + 8 * kMaxStages,
-                   bar_empty = ctrl + 16 * kMaxStages, bar_pfull = ctrl + 24 * kMaxStages,
-                   bar_pempty = bar_pfull + 8 * kSlots, bar_done = bar_pempty + 8 * kSlots;
+    const uint32_t bar_full = ctrl, bar_empty = ctrl + 8 * kMaxStages,
+                   bar_afull = ctrl + 16 * kMaxStages, bar_pempty = bar_afull + 8 * kAStages,
+                   bar_done = bar_pempty + 8 * kSlots;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem_raw + 256);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem_raw + 260);
     const uint32_t stage0 = (raw + 512 + 1023) & ~1023u;
@@ -416,14 +457,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(bar_full + 8 * s, 1);
-            mbar_init(bar_conv + 8 * s, kConvThreads);
             mbar_init(bar_empty + 8 * s, 1);
         }
-        for (int i = 0; i < kSlots; i++) {
-            mbar_init(bar_pfull + 8 * i, 1);
-            mbar_init(bar_pempty + 8 * i, kEpiThreads);
-        }
-        mbar_init(bar_done, 1);
+        for (int j = 0; j < kAStages; j++) mbar_init(bar_afull + 8 * j, kConvThreads);
+        for (int i = 0; i < kSlots; i++) mbar_init(bar_pempty + 8 * i, kEpiThreads);
+        mbar_init(bar_done, kMmaWarps);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -440,14 +478,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const uint32_t tmem_base = *tmem_slot;
     const int kblocks = (a.K + kBK - 1) / kBK;
 
-    // register split: the producer / converter / MMA warpgroup hands
+    // register split: the converter and producer / MMA warpgroups hand
     // registers to the two epilogue warpgroups, whose 64-float running
     // totals would otherwise spill to local memory.  The host launches only
     // when the kernel holds kLaunchRegs registers per thread, so the block's
     // pool covers both shares.
-    if (warp >= 4 && warp < 8) {
-        // issue warpgroup: converter (4-5), TMA producer (6), MMA issuer (7)
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsIssue));
+    if (warp >= kWarpProducer) {
+        // producer / MMA warpgroup
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsMma));
         // parameters in registers (the waits below clobber memory)
         const int ptiles = a.tiles, pmt = a.m_tiles, pnt = a.n_tiles, pbn = a.bn,
                   pamn = a.a_mn, pgather = a.gather, pplanes = a.planes;
@@ -476,14 +514,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         if (pgather) {
                             // A is written by the converter warps
                         } else if (pamn) {
-    #pragma unroll
-                            for (int i = 0; i < 4; i++)
-                                tma_load_3d(st + i * 4096, &tmA, fb, m0 + 32 * i, k0, z);
+                            tma_load_3d(st, &tmA, fb, m0, k0, z);
                         } else {
                             tma_load_3d(st, &tmA, fb, k0, m0, z);
                         }
-                        tma_load_3d(st + 2 * kABytes, &tmBhi, fb, k0, n0, pz);
-                        tma_load_3d(st + 2 * kABytes + pbn * 128, &tmBlo, fb, k0, n0, pz);
+                        tma_load_3d(st + kABytes, &tmBhi, fb, k0, n0, pz);
+                        tma_load_3d(st + kABytes + pbn * 128, &tmBlo, fb, k0, n0, pz);
                     }
                 }
                 // drain: the last issued stages must land before the CTA may exit
@@ -494,101 +530,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     mbar_wait(bar_full + 8 * s, (uint32_t)((j / S) & 1), (volatile int *)&dummy);
                 }
             }
-        } else if (warp >= 4 && warp < kWarpProducer && pgather) {
-            const TcGather gg = a.gg;
-            const int pK = a.K, pM = a.M;
-            // converter, gather mode: build the A tile of each free stage from
-            // the conv input (the producer loads only B).  Up to `depth` stages
-            // of copies stay in flight; the oldest is split and published once
-            // a newer one is issued.  depth <= S - 1 keeps one stage for the
-            // MMA, so the converter never waits on a stage it still holds.
-            const int ct = threadIdx.x - 128;
-            const int depth = S - 1 < 3 ? S - 1 : 3;
-            long long it = 0, pub = 0;  // stages [pub, it) issued, not yet published
-            Ring rs(S), rp(S);  // issue and publish positions
-            bool ok = true;
-            for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
-                const int z = t / (pmt * pnt);
-                const int r = t - z * pmt * pnt;
-                const int m0 = (r / pnt) * kBM;
-                const float *xz = gg.x + (long long)z * gg.x_bs;
-                int oy0[2], ox0[2];
-    #pragma unroll
-                for (int i = 0; i < 2; i++) {
-                    const int m = m0 + ct + 64 * i;
-                    if (m < pM) {
-                        const int oy = m / gg.OW;
-                        const int ox = m - oy * gg.OW;
-                        oy0[i] = oy * gg.S - gg.P;
-                        ox0[i] = ox * gg.S - gg.P;
-                    } else {
-                        oy0[i] = -64;
-                        ox0[i] = 0;
-                    }
-                }
-                for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
-                    const int s = rs.i;
-                    const uint32_t ph = rs.ph;
-                    if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    gather_issue(gg, pK, xz, stage0 + (uint32_t)s * pstage, ct, oy0, ox0,
-                                 kb * kBK);
-                    if (it + 1 - pub > depth) {
-                        // at most `depth` newer groups pending -> stage pub landed
-                        if (depth >= 3)
-                            asm volatile("cp.async.wait_group 3;" ::: "memory");
-                        else if (depth == 2)
-                            asm volatile("cp.async.wait_group 2;" ::: "memory");
-                        else
-                            asm volatile("cp.async.wait_group 1;" ::: "memory");
-                        const int ps = rp.i;
-                        gather_split_rows(stage0_ptr + (size_t)ps * pstage, ct);
-                        mbar_arrive(bar_conv + 8 * ps);
-                        pub++;
-                        rp.next();
-                    }
-                }
-            }
-            asm volatile("cp.async.wait_all;" ::: "memory");
-            for (; ok && pub < it; pub++, rp.next()) {
-                const int ps = rp.i;
-                gather_split_rows(stage0_ptr + (size_t)ps * pstage, ct);
-                mbar_arrive(bar_conv + 8 * ps);
-            }
-        } else if (warp >= 4 && warp < kWarpProducer) {
-            // converter: in-place 3xTF32 split of the A tile
-            const int ct = threadIdx.x - 128;
-            long long it = 0;
-            Ring rs(S);
-            bool ok = true;
-            for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
-                for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
-                    const int s = rs.i;
-                    const uint32_t ph = rs.ph;
-                    if (!mbar_wait(bar_full + 8 * s, ph, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    float4 *hi = reinterpret_cast<float4 *>(stage0_ptr + (size_t)s * pstage);
-                    float4 *lo = hi + kABytes / 16;
-    #pragma unroll
-                    for (int i = 0; i < kABytes / 16 / kConvThreads; i++) {
-                        const int idx = ct + kConvThreads * i;
-                        const float4 v = hi[idx];
-                        float4 h, l;
-                        h.x = tf32_rna(v.x); h.y = tf32_rna(v.y);
-                        h.z = tf32_rna(v.z); h.w = tf32_rna(v.w);
-                        l.x = v.x - h.x; l.y = v.y - h.y; l.z = v.z - h.z; l.w = v.w - h.w;
-                        hi[idx] = h;
-                        lo[idx] = l;
-                    }
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    mbar_arrive(bar_conv + 8 * s);
-                }
-            }
-        } else if (warp == kWarpMma) {
+        } else if (warp < kWarpMma + kMmaWarps) {
             // Every k-block accumulates into a TMEM partial slot of its own
             // (kSlots slots, round robin), which the epilogue folds into its
             // running FP32 total.  Inside a k-block the two small cross products
@@ -598,52 +540,142 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // that).  With several slots the MMAs run ahead of the epilogue's
             // folds instead of waiting for each one.
             if (lane == 0) {
-                long long it = 0;
-                Ring rs(S), rp(kSlots);
+                // this thread issues the k-blocks it with it % kMmaWarps == q
+                const int q = warp - kWarpMma;
+                int it = 0;
+                Ring rs(S), rp(kSlots), ra(kAStages);
                 bool ok = true;
                 for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
-                    for (int kb = 0; kb < kblocks; kb++, it++, rs.next(), rp.next()) {
-                        const int p = rp.i;
-                        const uint32_t pph = rp.ph;
-                        const int s = rs.i;
-                        const uint32_t ph = rs.ph;
-                        if (!mbar_wait(bar_pempty + 8 * p, pph ^ 1, abort_flag) ||
-                            !mbar_wait(bar_conv + 8 * s, ph, abort_flag) ||
-                            (pgather && !mbar_wait(bar_full + 8 * s, ph, abort_flag))) {
+                    for (int kb = 0; kb < kblocks;
+                         kb++, it++, rs.next(), rp.next(), ra.next()) {
+                        if (it % kMmaWarps != q) continue;
+                        // the A stage is written only after the stage's TMA landed,
+                        // so afull also covers the B operand
+                        if (!mbar_wait(bar_pempty + 8 * rp.i, rp.ph ^ 1, abort_flag) ||
+                            !mbar_wait(bar_afull + 8 * ra.i, ra.ph, abort_flag)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t d = tmem_base + (uint32_t)(p * kSlotCols);
-                        const uint32_t st = stage0 + s * pstage;
-                        const uint32_t ahi = st, alo = st + kABytes;
-                        const uint32_t bhi = st + 2 * kABytes, blo = bhi + pbn * 128;
-                        // descriptors of the four K=8 steps: A M-major (8 K rows =
-                        // two 4-row groups of 512 B) or K-major (32 bytes of K
-                        // inside the swizzled 128-byte row); B K-major
-                        auto desc_a = [&](uint32_t base, int kk) {
-                            return pamn ? smem_desc(base + kk * 1024, 4096, 512, 1)
-                                        : smem_desc(base + kk * 32, 16, 1024, 2);
-                        };
+                        const uint32_t d = tmem_base + (uint32_t)(rp.i * kSlotCols);
+                        const uint32_t ahi = tmem_base + (uint32_t)(kACol0 + ra.i * kACols);
+                        const uint32_t alo = ahi + kBK;
+                        const uint32_t bhi = stage0 + rs.i * pstage + kABytes;
+                        // B K-major: the K=8 step kk is 32 bytes into the swizzled
+                        // row, i.e. +2 in the descriptor's start-address field
+                        // (which cannot carry: shared addresses stay below 256 KB)
+                        const uint64_t dbh = smem_desc(bhi, 16, 1024, 2);
+                        const uint64_t dbl = smem_desc(bhi + pbn * 128, 16, 1024, 2);
 #pragma unroll
                         for (int kk = 0; kk < kBK / 8; kk++) {
-                            const uint64_t dbh = smem_desc(bhi + kk * 32, 16, 1024, 2);
-                            const uint64_t dbl = smem_desc(blo + kk * 32, 16, 1024, 2);
-                            umma_tf32(d, desc_a(alo, kk), dbh, pidesc, kk == 0 ? 0u : 1u);
-                            umma_tf32(d, desc_a(ahi, kk), dbl, pidesc, 1u);
+                            umma_tf32_ts(d, alo + 8 * kk, dbh + 2 * kk, pidesc, kk == 0 ? 0u : 1u);
+                            umma_tf32_ts(d, ahi + 8 * kk, dbl + 2 * kk, pidesc, 1u);
                         }
 #pragma unroll
                         for (int kk = 0; kk < kBK / 8; kk++)
-                            umma_tf32(d, desc_a(ahi, kk), smem_desc(bhi + kk * 32, 16, 1024, 2),
-                                      pidesc, 1u);
-                        umma_commit(bar_empty + 8 * s);
-                        umma_commit(bar_pfull + 8 * p);
+                            umma_tf32_ts(d, ahi + 8 * kk, dbh + 2 * kk, pidesc, 1u);
+                        umma_commit(bar_empty + 8 * rs.i);
                     }
                 }
-                // all issued MMAs must finish before TMEM is released
+                // all issued MMAs must finish before TMEM is released (both
+                // issuers commit; the phase completes after the later one)
                 umma_commit(bar_done);
                 int dummy = 0;
                 mbar_wait(bar_done, 0, (volatile int *)&dummy);
+            }
+        }
+    } else if (warp >= kWarpConv && warp < kWarpEpi2) {
+        // converter warpgroup
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsConv));
+        // parameters in registers (the waits below clobber memory)
+        const int ptiles = a.tiles, pmt = a.m_tiles, pnt = a.n_tiles, pbn = a.bn,
+                  pamn = a.a_mn, pgather = a.gather, pplanes = a.planes;
+        const uint32_t pstage = a.stage_bytes, ptx = a.tx_bytes, pidesc = a.idesc;
+        {
+            // converter: thread ct owns row ct of every A tile (TMEM lane ct,
+            // the lane quadrant of its warp).  For k-block i it writes TMEM A
+            // stage i % 2 once the MMAs of k-block i - 2 (the stage's last
+            // reader) completed — the empty barrier of that k-block's shared
+            // stage, tracked by the lagging ring rw.
+            const int ct = threadIdx.x - kWarpConv * 32;
+            const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+            // the gather geometry stays in the parameter space (constant
+            // cache), which keeps the converter inside its register share
+            const TcGather &gg = a.gg;
+            // gather mode: copies of up to `depth` k-blocks stay in flight; the
+            // oldest is split once a newer one is issued.  A gathered row is
+            // read back only by the thread that copied it, so a stage's A
+            // region is free again once that k-block was split (depth < S).
+            const int depth = S - 1 < 3 ? S - 1 : 3;
+            int it = 0, pub = 0;  // k-blocks [pub, it) issued, not yet split (gather)
+            Ring rs(S), rp(S), rw(S), ra(kAStages);  // issue, split, TMEM wait, A stage
+            bool ok = true;
+            // split the k-block at ring position rp into TMEM A stage ra
+            // (lane 0 waits for the warp and the verdict is shared, so the
+            // warp-collective TMEM stores always run converged)
+            auto publish = [&](int i) -> bool {
+                bool good = true;
+                if (lane == 0)
+                    good = mbar_wait(bar_full + 8 * rp.i, rp.ph, abort_flag) &&
+                           (i < kAStages || mbar_wait(bar_empty + 8 * rw.i, rw.ph, abort_flag));
+                if (!__shfl_sync(0xffffffffu, good ? 1 : 0, 0)) return false;
+                if (i >= kAStages) rw.next();
+                tc_fence_after();
+                const uint8_t *tile = stage0_ptr + (size_t)rp.i * pstage;
+                const uint32_t col = tmem_base + lane_base + (uint32_t)(kACol0 + ra.i * kACols);
+                if (pamn && !pgather)
+                    split_row_mmajor(tile, ct, col);
+                else
+                    split_row_kmajor(tile, ct, col);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                mbar_arrive(bar_afull + 8 * ra.i);
+                rp.next();
+                ra.next();
+                return true;
+            };
+            for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
+                const int z = t / (pmt * pnt);
+                const int r = t - z * pmt * pnt;
+                const int m0 = (r / pnt) * kBM;
+                const float *xz = pgather ? gg.x + (long long)z * gg.x_bs : nullptr;
+                int oy0 = -64, ox0 = 0;
+                if (pgather && m0 + ct < a.M) {
+                    const int oy = (m0 + ct) / gg.OW;
+                    const int ox = m0 + ct - oy * gg.OW;
+                    oy0 = oy * gg.S - gg.P;
+                    ox0 = ox * gg.S - gg.P;
+                }
+                for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
+                    if (!pgather) {
+                        if (!publish(it)) {
+                            ok = false;
+                            break;
+                        }
+                        continue;
+                    }
+                    gather_issue(gg, a.K, xz, stage0 + (uint32_t)rs.i * pstage, ct, oy0, ox0,
+                                 kb * kBK);
+                    if (it + 1 - pub > depth) {
+                        // at most `depth` newer groups pending -> k-block pub landed
+                        if (depth >= 3)
+                            asm volatile("cp.async.wait_group 3;" ::: "memory");
+                        else if (depth == 2)
+                            asm volatile("cp.async.wait_group 2;" ::: "memory");
+                        else
+                            asm volatile("cp.async.wait_group 1;" ::: "memory");
+                        if (!publish(pub)) {
+                            ok = false;
+                            break;
+                        }
+                        pub++;
+                    }
+                }
+            }
+            if (pgather) {
+                asm volatile("cp.async.wait_all;" ::: "memory");
+                for (; ok && pub < it; pub++)
+                    if (!publish(pub)) ok = false;
             }
         }
     } else {
@@ -671,7 +703,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         float tot[kHalfCols];
         long long ctr = 0;
-        Ring rp(kSlots);
+        // rp: partial slot of the k-block, re: its shared stage, whose empty
+        // barrier completes when the k-block's MMAs (and so its partial) did
+        Ring rp(kSlots), re(S);
         int nbox = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
@@ -682,10 +716,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             float *C = e.C + (long long)z * e.c_bs;
             const float *R = e.res_mode ? e.res + (long long)z * e.res_bs : nullptr;
             uint32_t last = 0;  // slot of the tile's last partial, held for the stores
-            for (int c = 0; c < kblocks; c++, ctr++, rp.next()) {
+            for (int c = 0; c < kblocks; c++, ctr++, rp.next(), re.next()) {
                 const int p = rp.i;
-                const uint32_t pph = rp.ph;
-                if (!mbar_wait(bar_pfull + 8 * p, pph, abort_flag)) {
+                if (!mbar_wait(bar_empty + 8 * re.i, re.ph, abort_flag)) {
                     ok = false;
                     break;
                 }
@@ -989,8 +1022,8 @@ namespace {
 bool plan_common(TcGemm *g, int M, int N, int K, int batch, int planes, const TcEpilogue &epi) {
     g->ok = false;
     if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || planes <= 0) return false;
-    // N tile (multiple of 16, <= 128 so that the four partial slots fit in
-    // the 512 TMEM columns); cost model: tiles x
+    // N tile (multiple of 16, <= 128 so that the partial slots and the A
+    // stages fit in the 512 TMEM columns); cost model: tiles x
     // (bn + 64), the 64 standing for the per-tile A traffic and epilogue
     // overhead in column equivalents
     int bn = 16;
@@ -1002,10 +1035,10 @@ bool plan_common(TcGemm *g, int M, int N, int K, int batch, int planes, const Tc
             bn = c;
         }
     }
-    const uint32_t stage_bytes = 2 * kABytes + 2 * 128 * bn;
+    const uint32_t stage_bytes = kABytes + 2 * 128 * bn;
     int stages = (int)((kSmemMax - kCtrlBytes - kStagingBytes) / stage_bytes);
     if (stages > kMaxStages) stages = kMaxStages;
-    if (stages < 2) return false;
+    if (stages < kMinStages) return false;
     g->M = M; g->N = N; g->K = K; g->batch = batch; g->planes = planes;
     g->bn = bn; g->stages = stages;
     g->smem = kCtrlBytes + (size_t)stages * stage_bytes + kStagingBytes;
@@ -1065,7 +1098,7 @@ bool tc_gemm_plan(TcGemm *g, int M, int N, int K, int batch, const float *A, int
     bool ok;
     if (a_mn)
         ok = encode3d(&g->tmA, A, (uint64_t)M, (uint64_t)K, (uint64_t)batch, (uint64_t)lda * 4,
-                      (uint64_t)a_bs * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+                      (uint64_t)a_bs * 4, kBM, kBK, CU_TENSOR_MAP_SWIZZLE_NONE);
     else
         ok = encode3d(&g->tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)batch, (uint64_t)lda * 4,
                       (uint64_t)a_bs * 4, 32, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -1121,10 +1154,11 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     a.gather = g.gather;
     a.tma_c = g.tma_c;
     a.gg = g.gg;
-    a.stage_bytes = 2 * kABytes + 2 * 128 * g.bn;
+    a.stage_bytes = kABytes + 2 * 128 * g.bn;
     a.tx_bytes = (g.gather ? 0 : kABytes) + 2 * 128 * g.bn;
-    a.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(g.a_mn ? 1 : 0) << 15) |
-              ((uint32_t)(g.bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+    // FP32 accumulate, TF32 A and B, both K-major (A comes from TMEM), N, M
+    a.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(g.bn >> 3) << 17) |
+              ((uint32_t)(kBM >> 4) << 24);
     a.epi = g.epi;
     int grid = sm_count();
     if (grid > g.tiles) grid = g.tiles;
