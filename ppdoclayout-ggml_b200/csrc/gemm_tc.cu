@@ -683,12 +683,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpi));
         // epilogue, 8 warps: two per TMEM lane quadrant (warp % 4), each
         // owning 64 of the bn <= 128 columns.  Every partial is folded into a
-        // running FP32 total held in registers; the total goes back into the
-        // tile's last partial slot, from where a
-        // compact 16-column loop applies bias / residual / activation and
-        // stores (a small loop body keeps the instruction cache warm for the
-        // other roles): CHW outputs through shared-memory boxes and TMA
-        // stores, other layouts with direct global stores.
+        // running FP32 total held in registers and its slot freed at once, so
+        // the MMAs of the next tile never wait for this tile's stores.  The
+        // totals leave in 16-column chunks through a shared-memory box, where
+        // a rolled loop applies bias / residual / activation (a small loop
+        // body keeps the instruction cache warm for the other roles): CHW and
+        // token-major outputs by TMA stores, other layouts by direct stores.
         // parameters in registers: every TMEM wait carries a memory clobber,
         // after which fields read through the parameter block would be
         // fetched again
@@ -696,7 +696,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int pM = a.M, pN = a.N, pbn = a.bn, ptiles = a.tiles, pmt = a.m_tiles,
                   pnt = a.n_tiles, ptma = a.tma_c;
         const int quad = warp & 3;
-        const int c_lo = warp >= kWarpEpi2 ? kHalfCols : 0;
+        // the two warpgroups split the N tile in 16-column units: [0, half)
+        // and [half, bn), half <= kHalfCols (a narrow tile keeps both busy)
+        const int half = ((pbn + 31) / 32) * 16;
+        const int c_lo = warp >= kWarpEpi2 ? half : 0;
+        const int c_hi = warp >= kWarpEpi2 ? pbn : half;
         const int ew = warp < 4 ? warp : warp - 4;  // epilogue warp 0..7
         const uint32_t staging = stage0 + (uint32_t)S * a.stage_bytes;
         float *staging_ptr = reinterpret_cast<float *>(stage0_ptr + (size_t)S * a.stage_bytes);
@@ -715,7 +719,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int m = m0 + quad * 32 + lane;
             float *C = e.C + (long long)z * e.c_bs;
             const float *R = e.res_mode ? e.res + (long long)z * e.res_bs : nullptr;
-            uint32_t last = 0;  // slot of the tile's last partial, held for the stores
             for (int c = 0; c < kblocks; c++, ctr++, rp.next(), re.next()) {
                 const int p = rp.i;
                 if (!mbar_wait(bar_empty + 8 * re.i, re.ph, abort_flag)) {
@@ -726,7 +729,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const uint32_t part = tmem_base + lane_base + (uint32_t)(p * kSlotCols + c_lo);
 #pragma unroll
                 for (int q = 0; q < kHalfCols / 32; q++) {
-                    if (c_lo + q * 32 < pbn) {
+                    if (c_lo + q * 32 < c_hi) {
                         uint32_t v[32];
                         tmem_ld32(part + (uint32_t)(q * 32), v);
 #pragma unroll
@@ -735,38 +738,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                                      : tot[q * 32 + j] + __uint_as_float(v[j]);
                     }
                 }
-                if (c + 1 < kblocks) {
-                    tc_fence_before();
-                    mbar_arrive(bar_pempty + 8 * p);
-                } else {
-                    last = (uint32_t)p;
-                }
+                // the slot is free as soon as it is folded, the tile's last one
+                // included: the stores below work from the register totals
+                tc_fence_before();
+                mbar_arrive(bar_pempty + 8 * p);
             }
             if (!ok) break;
-            // the total goes into the last partial's slot, read back in 16-column
-            // pieces by the store loop
-            const uint32_t xa = tmem_base + lane_base + (uint32_t)(last * kSlotCols + c_lo);
-#pragma unroll
-            for (int q = 0; q < kHalfCols / 32; q++) {
-                if (c_lo + q * 32 < pbn) {
-                    uint32_t v[32];
-#pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] = __float_as_uint(tot[q * 32 + j]);
-                    tmem_st32(xa + (uint32_t)(q * 32), v);
-                }
-            }
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             const bool row_ok = m < pM;
             float *Crow = C + (long long)m * e.ldc_m;
             const float *Rrow = R ? R + (long long)m * e.res_ldm : nullptr;
-            const int c_hi = pbn < c_lo + kHalfCols ? pbn : c_lo + kHalfCols;
             const bool ops = ACT != ACT_NONE || e.alpha != 1.0f || e.bias || e.res_mode;
-            const uint32_t xt = tmem_base + lane_base + (uint32_t)(last * kSlotCols);
-#pragma unroll 1
-            for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-                const uint32_t xa = xt;
-                uint32_t v[16];
-                tmem_ld16(xa + (uint32_t)c0, v);
+            // one 16-column chunk of the register totals: staged through a
+            // shared-memory box and a TMA store, or stored directly
+            auto store_chunk = [&](int c0, const float (&v)[16]) {
                 if (ptma == 1) {
                     // CHW output: the warp's 32 pixels x 16 channels go into a
                     // staging box (lane = pixel, conflict-free rows of 128 B)
@@ -782,7 +766,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     // / activation in a rolled loop over the box: a small loop
                     // body, executed once per tile, keeps instruction fetch short
 #pragma unroll
-                    for (int j = 0; j < 16; j++) box[j * 32 + lane] = __uint_as_float(v[j]);
+                    for (int j = 0; j < 16; j++) box[j * 32 + lane] = v[j];
                     if (ops) {
                         // four columns at a time: their bias and residual loads
                         // are issued together, the op order per element is
@@ -821,7 +805,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         bulk_commit();
                     }
                     nbox++;
-                    continue;
+                    return;
                 }
                 if (ptma == 2) {
                     // token-major output: the warp's 32 rows x 16 columns go into
@@ -837,9 +821,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     float4 *row4 = reinterpret_cast<float4 *>(box + lane * 16);
 #pragma unroll
                     for (int q = 0; q < 4; q++)
-                        row4[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                                              __uint_as_float(v[4 * q + 2]),
-                                              __uint_as_float(v[4 * q + 3]));
+                        row4[q] = make_float4(v[4 * q], v[4 * q + 1],
+                                              v[4 * q + 2],
+                                              v[4 * q + 3]);
                     if (ops) {
                         __syncwarp();  // the pass reads the other lanes' rows
 #pragma unroll 1
@@ -878,37 +862,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         bulk_commit();
                     }
                     nbox++;
-                    continue;
+                    return;
                 }
-                if (!row_ok) continue;
-                // row-major output (token-major linears): each thread owns a
-                // row, so 16 consecutive columns go out as four 16-byte stores
-                float *cp = Crow + (n0 + c0);
-                if (e.ldc_n == 1 && n0 + c0 + 16 <= pN && ((uintptr_t)cp & 15) == 0 &&
-                    (e.res_mode == 0 || e.res_ldn == 1)) {
-                    float y[16];
+                if (!row_ok) return;
+                // any other layout (strides that TMA cannot take): the raw
+                // values go through the thread's own column of a box, then a
+                // rolled loop applies the ops and stores with the output strides
+                float *box = staging_ptr + (size_t)(ew * 2) * (kBoxBytes / 4);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const int n = n0 + c0 + j;
-                        float x = __uint_as_float(v[j]);
-                        if (e.alpha != 1.0f) x = x * e.alpha;
-                        if (e.bias) x = x + __ldg(e.bias + n);
-                        if (e.res_mode == 1) x = x + Rrow[n];
-                        x = act_apply(x, ACT);
-                        if (e.res_mode == 2) x = x + Rrow[n];
-                        y[j] = x;
-                    }
-                    float4 *c4 = reinterpret_cast<float4 *>(cp);
-#pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        c4[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
-                    continue;
-                }
-#pragma unroll
+                for (int j = 0; j < 16; j++) box[j * 32 + lane] = v[j];
+#pragma unroll 1
                 for (int j = 0; j < 16; j++) {
                     const int n = n0 + c0 + j;
                     if (n < pN) {
-                        float x = __uint_as_float(v[j]);
+                        float x = box[j * 32 + lane];
                         if (e.alpha != 1.0f) x = x * e.alpha;
                         if (e.bias) x = x + __ldg(e.bias + n);
                         if (e.res_mode == 1) x = x + Rrow[(long long)n * e.res_ldn];
@@ -917,9 +884,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         Crow[(long long)n * e.ldc_n] = x;
                     }
                 }
+            };
+#pragma unroll
+            for (int cq = 0; cq < kHalfCols / 16; cq++) {
+                if (c_lo + 16 * cq < c_hi) {
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] = tot[16 * cq + j];
+                    store_chunk(c_lo + 16 * cq, v);
+                }
             }
-            tc_fence_before();
-            mbar_arrive(bar_pempty + 8 * last);
         }
         // the staging boxes must be read and the stores complete before exit
         if (ptma && lane == 0) bulk_wait_all();
