@@ -389,14 +389,15 @@ __device__ __forceinline__ void gather_issue(const TcGather &g, int K, const flo
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// 3xTF32 split of 8 values into TMEM: hi = x with the low 13 mantissa bits
-// cleared (exactly TF32), lo = x - hi (exact in FP32); hi goes to columns
-// col .. col + 7 of the warp's lane quadrant, lo 32 columns further.
+// 3xTF32 split of 8 values into TMEM: hi = x rounded to the nearest TF32
+// (cvt.rna), lo = x - hi (exact in FP32, either sign, so the tensor core's
+// truncation of lo carries no bias); hi goes to columns col .. col + 7 of
+// the warp's lane quadrant, lo 32 columns further.
 __device__ __forceinline__ void split_store8(uint32_t col, const float (&x)[8]) {
     uint32_t h[8], l[8];
 #pragma unroll
     for (int u = 0; u < 8; u++) {
-        h[u] = __float_as_uint(x[u]) & 0xFFFFE000u;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h[u]) : "f"(x[u]));
         l[u] = __float_as_uint(x[u] - __uint_as_float(h[u]));
     }
     tmem_st8(col, h);
