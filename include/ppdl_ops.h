@@ -131,6 +131,22 @@ PPDL_OPS_API int ppdl_conv2d_tf32x3(const float * x, int batch, int IC, int H, i
                                     int OC, int K, int S, int P, int OH, int OW, int act,
                                     float * b_split, float * y, long long y_bs, void * stream);
 
+/* Extension (the reference's depthwise conv is ggml_conv_2d_dw_direct,
+   src/ppdoclayout.cpp:400-404, a ggml op rather than a tagged PPDL op):
+   the depthwise conv of the backbone's downsampling and light blocks.
+     y[z][c][oy][ox] = act(sum_{kh,kw} weight[c][kh][kw]
+                           * x[z][c][oy*S + kh - P][ox*S + kw - P] + bias[c])
+   in FP32, taps accumulated by fma in (kh, kw) order, zero outside H x W,
+   OH = (H + 2P - K) / S + 1 (same for OW).  x: pages of [C][H][W] at stride
+   x_bs; y: pages of [C][OH][OW] at stride y_bs; bias may be NULL; act
+   0/1/2/3 = none/ReLU/SiLU/GELU.  K 3 or 5, S 1 or 2 (else
+   PPDL_ERR_UNSUPPORTED), 0 <= P < K.  Returns PPDL_OK / PPDL_ERR_SHAPE /
+   PPDL_ERR_UNSUPPORTED / PPDL_ERR_CUDA. */
+PPDL_OPS_API int ppdl_depthwise_conv2d(const float * x, int batch, int C, int H, int W,
+                                       long long x_bs, const float * weight, const float * bias,
+                                       int K, int S, int P, int act, float * y, long long y_bs,
+                                       void * stream);
+
 /* No counterpart in the reference.  ppdl_gemm_tf32x3 for callers that
    cannot allocate device memory — e.g. a ggml custom-op hook, which runs
    inside ggml's graph compute where ggml's allocator owns every buffer and

@@ -214,49 +214,135 @@ __global__ void wg4_kmajor_split_kernel(const float *__restrict__ wg4, float *__
 // ggml_conv_2d_dw_direct + bias + act (src/ppdoclayout.cpp:400-404).
 // A block computes a 32 x 32 output tile of one (page, channel) plane from a
 // shared-memory copy of its input window (halo included, zeros outside the
-// image), so every input is read from global memory once per tile instead of
-// K*K times through L1.  Per output: s = fma over (kh, kw) ascending — the
-// zero taps of the padding leave s unchanged — then + bias, activation.
-constexpr int kDwTW = 32, kDwTH = 32;  // 256 threads, 4 rows each
+// image), filled row by row with coalesced loads, so every input is read
+// from global memory once per tile.  A thread computes 4 consecutive outputs
+// of one row: per kernel row it reads the 3*S + K window values they share
+// once into registers (8 threads per output row, 4 rows per warp; the row
+// pitch is 1 mod 32, so the 4 rows of a warp fall in different banks).  Per
+// output: s = fma over (kh, kw) ascending — the zero taps of the padding
+// leave s unchanged — then + bias, activation.
+// 4-byte global -> shared copy; valid = false writes a zero without reading
+__device__ __forceinline__ void cp_async_zfill4(uint32_t dst, const float *src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src),
+                 "r"(valid ? 4 : 0)
+                 : "memory");
+}
+
+constexpr int kDwTW = 32, kDwTH = 32;  // 256 threads: 8 x 4-output groups x 32 rows
+constexpr size_t kDwPlaneSmemMax = 64 * 1024;  // whole-plane form up to this much input
 template <int K, int S>
 __global__ void __launch_bounds__(256)
 dwconv_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
               const float *__restrict__ bias, float *__restrict__ y, long long ybs, int H, int W,
               int OH, int OW, int P, int act, int tiles_x) {
-    constexpr int IW = (kDwTW - 1) * S + K, IH = (kDwTH - 1) * S + K, LD = IW + 1;
+    constexpr int IW = (kDwTW - 1) * S + K, IH = (kDwTH - 1) * S + K;
+    constexpr int LD = (IW + 30) / 32 * 32 + 1;  // >= IW, 1 mod 32
+    constexpr int NV = 3 * S + K;                // window columns of 4 outputs
     __shared__ float tile[IH * LD];
     const int c = blockIdx.y, b = blockIdx.z;
     const int tyi = blockIdx.x / tiles_x;
     const int tx0 = (blockIdx.x - tyi * tiles_x) * kDwTW, ty0 = tyi * kDwTH;
     const float *xp = x + (long long)b * xbs + (long long)c * H * W;
     const int ix0 = tx0 * S - P, iy0 = ty0 * S - P;
-    for (int e = threadIdx.x; e < IH * IW; e += 256) {
-        const int r = e / IW, q = e - r * IW;
-        const int iy = iy0 + r, ix = ix0 + q;
-        tile[r * LD + q] =
-            ((unsigned)iy < (unsigned)H && (unsigned)ix < (unsigned)W) ? __ldg(xp + iy * W + ix) : 0.0f;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // asynchronous 4-byte copies (zero-filled outside the image), all of a
+    // thread's in flight at once rather than one load-to-store round trip each
+    const uint32_t tile_s = (uint32_t)__cvta_generic_to_shared(tile);
+    for (int r = warp; r < IH; r += 8) {
+        const int iy = iy0 + r;
+        const bool row_in = (unsigned)iy < (unsigned)H;
+        const float *xr = xp + (long long)iy * W;
+        for (int q = lane; q < IW; q += 32) {
+            const int ix = ix0 + q;
+            const bool in = row_in && (unsigned)ix < (unsigned)W;
+            cp_async_zfill4(tile_s + (uint32_t)(r * LD + q) * 4u, in ? xr + ix : xp, in);
+        }
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     float wk[K * K];
 #pragma unroll
     for (int i = 0; i < K * K; i++) wk[i] = __ldg(w + (long long)c * K * K + i);
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    const int lx = threadIdx.x & 31, ly0 = threadIdx.x >> 5;
-    const int ox = tx0 + lx;
-    if (ox >= OW) return;
-    const float bv = __ldg(bias + c);
-    float *yp = y + (long long)b * ybs + (long long)c * OH * OW + ox;
+    const int xg = threadIdx.x & 7, ly = threadIdx.x >> 3;
+    const int ox0 = tx0 + 4 * xg, oy = ty0 + ly;
+    if (ox0 >= OW || oy >= OH) return;
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const float *tp = tile + (ly * S) * LD + 4 * S * xg;
 #pragma unroll
-    for (int r = 0; r < kDwTH / 8; r++) {
-        const int ly = ly0 + 8 * r, oy = ty0 + ly;
-        if (oy >= OH) break;
-        const float *tp = tile + (ly * S) * LD + lx * S;
-        float s = 0.0f;
+    for (int kh = 0; kh < K; kh++) {
+        float v[NV];
 #pragma unroll
-        for (int kh = 0; kh < K; kh++)
+        for (int i = 0; i < NV; i++) v[i] = tp[kh * LD + i];
 #pragma unroll
-            for (int kw = 0; kw < K; kw++) s = fmaf(tp[kh * LD + kw], wk[kh * K + kw], s);
-        s = __fadd_rn(s, bv);
-        yp[(long long)oy * OW] = act_apply(s, act);
+        for (int o = 0; o < 4; o++)
+#pragma unroll
+            for (int kw = 0; kw < K; kw++) s[o] = fmaf(v[o * S + kw], wk[kh * K + kw], s[o]);
+    }
+    const float bv = bias ? __ldg(bias + c) : 0.0f;
+    float *yp = y + (long long)b * ybs + (long long)c * OH * OW + (long long)oy * OW + ox0;
+#pragma unroll
+    for (int o = 0; o < 4; o++)
+        if (ox0 + o < OW) yp[o] = act_apply(__fadd_rn(s[o], bv), act);
+}
+
+// Whole-plane form for planes whose padded input fits in shared memory (the
+// light blocks' 50x50 and 25x25 planes, the 100 -> 50 and 50 -> 25
+// downsamples): one block per (page, channel) reads the plane exactly once,
+// row by row, into a zero-bordered copy (border P), then computes every
+// output as above, 4 consecutive outputs of a row per work item, and writes
+// the plane contiguously.  The tiled kernel re-reads halo rows and columns
+// of neighbouring tiles and wastes threads on partly empty edge tiles.
+template <int K, int S>
+__global__ void __launch_bounds__(256)
+dwconv_plane_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
+                    const float *__restrict__ bias, float *__restrict__ y, long long ybs, int H,
+                    int W, int OH, int OW, int P, int act, int ld) {
+    extern __shared__ float plane[];  // (H + 2P) rows of ld >= W + 2P floats
+    constexpr int NV = 3 * S + K;
+    const int c = blockIdx.x, b = blockIdx.y;
+    const float *xp = x + (long long)b * xbs + (long long)c * H * W;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int HP = H + 2 * P, WP = W + 2 * P;
+    const uint32_t plane_s = (uint32_t)__cvta_generic_to_shared(plane);
+    for (int r = warp; r < HP; r += 8) {
+        const int iy = r - P;
+        const bool row_in = (unsigned)iy < (unsigned)H;
+        const float *xr = xp + (long long)iy * W;
+        for (int q = lane; q < WP; q += 32) {
+            const int ix = q - P;
+            const bool in = row_in && (unsigned)ix < (unsigned)W;
+            cp_async_zfill4(plane_s + (uint32_t)(r * ld + q) * 4u, in ? xr + ix : xp, in);
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    float wk[K * K];
+#pragma unroll
+    for (int i = 0; i < K * K; i++) wk[i] = __ldg(w + (long long)c * K * K + i);
+    const float bv = bias ? __ldg(bias + c) : 0.0f;
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    const int ng = (OW + 3) >> 2;  // 4-output groups per row
+    float *yp = y + (long long)b * ybs + (long long)c * OH * OW;
+    for (int item = threadIdx.x; item < OH * ng; item += 256) {
+        const int oy = item / ng, g = item - oy * ng;
+        const int ox0 = 4 * g;
+        float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const float *tp = plane + (oy * S) * ld + ox0 * S;
+#pragma unroll
+        for (int kh = 0; kh < K; kh++) {
+            float v[NV];
+#pragma unroll
+            for (int i = 0; i < NV; i++) v[i] = tp[kh * ld + i];
+#pragma unroll
+            for (int o = 0; o < 4; o++)
+#pragma unroll
+                for (int kw = 0; kw < K; kw++) s[o] = fmaf(v[o * S + kw], wk[kh * K + kw], s[o]);
+        }
+        float *yr = yp + (long long)oy * OW + ox0;
+#pragma unroll
+        for (int o = 0; o < 4; o++)
+            if (ox0 + o < OW) yr[o] = act_apply(__fadd_rn(s[o], bv), act);
     }
 }
 
@@ -477,6 +563,44 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
     const int OH = (H + 2 * P - K) / S + 1, OW = (W + 2 * P - K) / S + 1;
     if (OH <= 0 || OW <= 0 || C <= 0 || C > 65535 || B <= 0 || B > 65535 || P < 0 || P >= K)
         return ERR_SHAPE;
+    // whole-plane form: the zero-bordered input plane plus the columns the
+    // last 4-output group reads past it, row pitch 1 mod 32
+    const int need_w = 4 * S * ((OW + 3) / 4) - S + K;  // columns the last group reads
+    const int WP = W + 2 * P > need_w ? W + 2 * P : need_w;
+    const int ld = (WP + 30) / 32 * 32 + 1;
+    const int HPR = (OH - 1) * S + K > H + 2 * P ? (OH - 1) * S + K : H + 2 * P;
+    const size_t plane_bytes = (size_t)HPR * ld * 4;
+    if (plane_bytes <= kDwPlaneSmemMax) {
+        const dim3 g(C, B);
+        const int sm = (int)plane_bytes;
+        int dev = 0;
+        cudaGetDevice(&dev);
+#define PPDL_DW_PLANE(KK, SS)                                                                     \
+    do {                                                                                         \
+        static bool attr[64] = {false};                                                          \
+        if (dev >= 64 || !attr[dev]) {                                                           \
+            if (cudaFuncSetAttribute(dwconv_plane_kernel<KK, SS>,                                \
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,                \
+                                     (int)kDwPlaneSmemMax) != cudaSuccess)                       \
+                return ERR_CUDA;                                                                 \
+            if (dev < 64) attr[dev] = true;                                                      \
+        }                                                                                        \
+        dwconv_plane_kernel<KK, SS><<<g, 256, sm, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW,   \
+                                                        P, act, ld);                             \
+    } while (0)
+        if (K == 3 && S == 1)
+            PPDL_DW_PLANE(3, 1);
+        else if (K == 3 && S == 2)
+            PPDL_DW_PLANE(3, 2);
+        else if (K == 5 && S == 1)
+            PPDL_DW_PLANE(5, 1);
+        else if (K == 5 && S == 2)
+            PPDL_DW_PLANE(5, 2);
+        else
+            return ERR_UNSUPPORTED;
+#undef PPDL_DW_PLANE
+        return cuda_status();
+    }
     const int tiles_x = (OW + kDwTW - 1) / kDwTW, tiles_y = (OH + kDwTH - 1) / kDwTH;
     const dim3 g(tiles_x * tiles_y, C, B);
     if (K == 3 && S == 1)

@@ -12,6 +12,7 @@
 
 #include "../../include/ppdl_ops.h"
 #include "kernels.h"
+#include "conv.h"
 #include "gemm_tc.h"
 #include "ops_internal.h"
 
@@ -84,6 +85,20 @@ PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float *A
         return fail(PPDL_ERR_SHAPE, "gemm: operands violate the TMA rules (16-byte alignment, "
                                     "strides and K multiples of 4)");
     return to_status(ppdl::launch_tc_gemm(g, st));
+}
+
+PPDL_OPS_API int ppdl_depthwise_conv2d(const float *x, int batch, int C, int H, int W,
+                                       long long x_bs, const float *weight, const float *bias,
+                                       int K, int S, int P, int act, float *y, long long y_bs,
+                                       void *stream) {
+    g_err[0] = 0;
+    if (!x || !weight || !y || batch <= 0 || C <= 0 || H <= 0 || W <= 0 || act < 0 || act > 3)
+        return fail(PPDL_ERR_SHAPE, "depthwise conv: bad sizes, activation or null pointer");
+    if (!((K == 3 || K == 5) && (S == 1 || S == 2)))
+        return fail(PPDL_ERR_UNSUPPORTED, "depthwise conv: K %lld, stride %lld (3 or 5, 1 or 2)", K,
+                    S);
+    return to_status(ppdl::launch_dwconv(x, x_bs, weight, bias, y, y_bs, C, H, W, K, S, P, act,
+                                         batch, (cudaStream_t)stream));
 }
 
 PPDL_OPS_API int ppdl_conv2d_tf32x3(const float *x, int batch, int IC, int H, int W,
