@@ -492,6 +492,8 @@ def run_forward(args, world, rank, local, pg):
     gsteps = [s for s in steps if s[1] in GEMM_KINDS]
     g_ms = sum(s[2] for s in gsteps)
     g_fl = sum(s[3] for s in gsteps) * B
+    if g_ms <= 0:
+        raise RuntimeError("per-step profile returned no GEMM time")
     achieved = g_fl / (g_ms / 1e3) / 1e12
     roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(tc, 1),
             "unit": "TFLOP/s", "frac": round(achieved / tc, 4),

@@ -91,9 +91,10 @@ PPDL_API void * ppdl_stream(ppdl_ctx * ctx);
 
 /* extension: per-step device profile — the counterpart of the reference's
    PPDL_PROFILE phase profile (src/ppdoclayout.cpp:995-1050).  Runs the
-   forward of the n pages of the last call once more, eagerly, with a CUDA
-   event after every step, and fills up to max entries.  Returns the number
-   of steps written, or -1. */
+   forward of the n pages of the last call once more with a CUDA event after
+   every step — captured into a CUDA graph and replayed, so the times are
+   device time without host launch gaps (eagerly if the capture fails) — and
+   fills up to max entries.  Returns the number of steps written, or -1. */
 #define PPDL_STEP_OTHER         0
 #define PPDL_STEP_GEMM_1X1      1   /* 1x1 conv GEMM                     */
 #define PPDL_STEP_WG_MADD       2   /* Winograd 36-plane GEMM            */

@@ -1253,15 +1253,32 @@ PPDL_API int ppdl_profile_steps(ppdl_ctx *c, int n, ppdl_step_stat *out, int max
     std::vector<cudaEvent_t> ev(ns + 1);
     for (auto &e : ev) cudaEventCreate(&e);
     m.nb = n;
-    cudaEventRecord(ev[0], m.st);
+    // the steps with an event after each, captured into a CUDA graph and
+    // replayed (twice, the second timed), so that the times are device time
+    // without the host's launch gaps; eager if the capture fails
+    // (inside a capture only an "external" record becomes an event-record
+    // node; a plain one would merely mark a dependency)
+    auto enqueue = [&](unsigned flags) -> bool {
+        if (cudaEventRecordWithFlags(ev[0], m.st, flags) != cudaSuccess) return false;
+        for (int i = 0; i < ns; i++)
+            if (m.plan[i].fn() != ppdl::OK ||
+                cudaEventRecordWithFlags(ev[i + 1], m.st, flags) != cudaSuccess)
+                return false;
+        return true;
+    };
     int rc = 0;
-    for (int i = 0; i < ns; i++) {
-        if (m.plan[i].fn() != ppdl::OK) {
-            rc = -1;
-            break;
-        }
-        cudaEventRecord(ev[i + 1], m.st);
+    cudaGraph_t gr = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    bool graphed = false;
+    if (cudaStreamBeginCapture(m.st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+        const bool ok = enqueue(cudaEventRecordExternal);
+        if (cudaStreamEndCapture(m.st, &gr) == cudaSuccess && ok &&
+            cudaGraphInstantiate(&ge, gr, 0) == cudaSuccess)
+            graphed = cudaGraphLaunch(ge, m.st) == cudaSuccess &&
+                      cudaGraphLaunch(ge, m.st) == cudaSuccess;
     }
+    cudaGetLastError();
+    if (!graphed && !enqueue(cudaEventRecordDefault)) rc = -1;
     if (cudaStreamSynchronize(m.st) != cudaSuccess) rc = -1;
     int w = 0;
     if (rc == 0) {
@@ -1275,6 +1292,8 @@ PPDL_API int ppdl_profile_steps(ppdl_ctx *c, int n, ppdl_step_stat *out, int max
             s.bytes = m.plan[i].bytes;
         }
     }
+    if (ge) cudaGraphExecDestroy(ge);
+    if (gr) cudaGraphDestroy(gr);
     for (auto &e : ev) cudaEventDestroy(e);
     return rc == 0 ? w : -1;
 }

@@ -85,6 +85,22 @@ def test_tc_gemm_k_major(cuda, M, N, K):
     assert err < RTOL, err
 
 
+# Large shapes (many tiles per SM, several k-blocks): an N tail of 44
+# columns, an odd M with a partial last tile, both A layouts, a K tail,
+# batches.
+@pytest.mark.parametrize("M,N,K,batch,a_m_major", [
+    (40000, 300, 128, 1, 1),   # N tail: 300 = 2 x 128 + 44
+    (20037, 128, 160, 2, 1),   # odd M
+    (40000, 256, 256, 1, 0),   # K-major A (token-major rows)
+    (19000, 96, 232, 2, 0),    # K-major, N = 96, K tail (232 = 7.25 x 32)
+])
+def test_tc_gemm_large(cuda, M, N, K, batch, a_m_major):
+    got, ref = _gemm(cuda, M, N, K, batch, a_m_major, seed=M + 3 * N + K)
+    assert np.isfinite(got).all()
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err < RTOL, err
+
+
 def test_tc_gemm_rejects_unaligned_strides(cuda):
     L = _lib()
     A = torch.zeros(625 * 64, device=cuda)
