@@ -61,7 +61,7 @@ int sm_count() {
 // ---- Winograd input transform -----------------------------------------------
 // thread per (page, ic, tile); dt[(b*36 + p)*IC + ic][T] (the reference's
 // (T, IC, 36) plane layout per page)
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 4)
 wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ dt, int IC,
                  int H, int W, int TW, int TH, int pad, int B, int ldt) {
     // grid (IC*T / 256, B): one 32-bit division per thread
@@ -105,7 +105,10 @@ wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__
 }
 
 // ---- Winograd output transform ----------------------------------------------
-__global__ void __launch_bounds__(256)
+// (both transforms are held to 64 registers, four 256-thread blocks per SM:
+// their loads are independent and latency-bound, so more warps in flight
+// beat the few extra registers)
+__global__ void __launch_bounds__(256, 4)
 wg4_output_kernel(const float *__restrict__ yt, const float *__restrict__ bias,
                   float *__restrict__ y, long long ybs, const float *__restrict__ res,
                   long long rbs, int res_mode, int OC, int OH, int OW, int TW, int TH, int act,

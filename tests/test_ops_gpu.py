@@ -99,6 +99,28 @@ def test_topk_vs_golden(cuda, golden_dir, seed):
     np.testing.assert_array_equal(out.cpu().numpy(), g["out"])
 
 
+def test_topk_mass_ties_and_extremes(cuda, orc):
+    # the selection is a radix select over (max-logit bits, index) keys: a page
+    # where every token ties (the winners are the 300 lowest indices), one with
+    # a few hundred ties straddling the 300th place, one with +-inf and the
+    # largest/smallest finite logits
+    a = np.full_like(cases.topk_inputs(31), 0.25)
+    b = cases.topk_inputs(32)
+    b[::40] = 3.0                      # 329 tokens tie at the top
+    c = cases.topk_inputs(33)
+    c[5, 3] = np.inf
+    c[77] = -np.inf
+    c[100, 0] = np.finfo(np.float32).max
+    c[101, 1] = -np.finfo(np.float32).max
+    lg = np.stack([a, b, c]).astype(np.float32)
+    out = torch.empty((3, 300), dtype=torch.int32, device=cuda)
+    ppdl.check(ppdl.op_launch(ppdl.OP_TOPK, out, [_dev(lg, cuda)]))
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    np.testing.assert_array_equal(got, orc.topk(lg))
+    np.testing.assert_array_equal(got[0], np.arange(300))
+
+
 def test_topk_batched_with_signed_zero_ties(cuda, orc):
     lg = np.stack([cases.topk_inputs(31), cases.topk_inputs(32)])
     lg[0, 200:260] = -0.0
