@@ -9,6 +9,7 @@
 // masks cross PCIe.
 #include "common.cuh"
 #include "dec.h"
+#include "select.cuh"
 
 namespace ppdl {
 
@@ -115,13 +116,16 @@ __global__ void refine_kernel(const float *__restrict__ delta, float *__restrict
     ref[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
 }
 
-// y[b][t][:] = x[b][t][:] * v[t]
-__global__ void row_scale_kernel(const float *__restrict__ x, const float *__restrict__ v,
-                                 float *__restrict__ y, long long rows_per_page, int D, long long n) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const long long t = (i / D) % rows_per_page;
-    y[i] = __fmul_rn(x[i], v[t]);
+// y[b][t][:] = x[b][t][:] * v[t]; four elements per thread (D % 4 == 0),
+// 32-bit index arithmetic (n / 4 < 2^31)
+__global__ void row_scale_kernel(const float4 *__restrict__ x, const float *__restrict__ v,
+                                 float4 *__restrict__ y, unsigned rows_per_page, unsigned d4,
+                                 unsigned n4) {
+    const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n4) return;
+    const float s = v[(i / d4) % rows_per_page];
+    const float4 a = x[i];
+    y[i] = make_float4(__fmul_rn(a.x, s), __fmul_rn(a.y, s), __fmul_rn(a.z, s), __fmul_rn(a.w, s));
 }
 
 // y[b][i][:] = x[b][idx[b][i]][:]
@@ -145,11 +149,15 @@ __global__ void pp_votes_rank_kernel(const float *__restrict__ order, int32_t *_
     const int b = blockIdx.x;
     const float *o = order + (long long)b * kNQ * kNQ;
     for (int j = threadIdx.x; j < kNQ; j += blockDim.x) {
+        // the same sum in the same order; the diagonal adds an exact +0 (acc
+        // starts at +0 and only grows), so the loop can be unrolled and the
+        // loads of ten terms are in flight together
         float acc = 0.0f;
+#pragma unroll 10
         for (int i = 0; i < kNQ; i++) {
-            if (i == j) continue;
             const float diff = __fsub_rn(o[j + kNQ * i], o[i + kNQ * j]);
-            acc = __fadd_rn(acc, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-diff))));
+            const float term = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-diff)));
+            acc = __fadd_rn(acc, i == j ? 0.0f : term);
         }
         s_votes[j] = acc;
     }
@@ -166,48 +174,26 @@ __global__ void pp_votes_rank_kernel(const float *__restrict__ order, int32_t *_
 }
 
 // top-300 of the 7500 sigmoid scores (ties to the lower flat index) and the
-// detections rows; one block per page, bitonic sort of 8192 keys
+// detections rows; one block per page, block radix select (select.cuh)
 __global__ void __launch_bounds__(1024)
 pp_select_kernel(const float *__restrict__ logits, const float *__restrict__ boxes,
                  const int32_t *__restrict__ rank, const int32_t *__restrict__ ori_hw,
                  float *__restrict__ dets, int32_t *__restrict__ sel) {
-    constexpr int N = kNQ * kNC, N2 = 8192;
-    extern __shared__ unsigned long long s_key[];  // N2 keys (64 KB, dynamic)
+    constexpr int N = kNQ * kNC;
+    extern __shared__ unsigned long long s_key[];  // N keys (dynamic)
+    __shared__ unsigned long long s_top[kSelectMax];
     const int b = blockIdx.x;
     const float *lg = logits + (long long)b * N;
-    for (int i = threadIdx.x; i < N2; i += blockDim.x) {
-        unsigned long long key = 0ull;
-        if (i < N) {
-            float sc = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-lg[i])));
-            if (sc == 0.0f) sc = 0.0f;
-            unsigned u = __float_as_uint(sc);
-            u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-            key = ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)i);
-        }
-        s_key[i] = key;
-    }
+    for (int i = threadIdx.x; i < N; i += blockDim.x)
+        s_key[i] = select_key(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-lg[i]))), (unsigned)i);
     __syncthreads();
-    for (int k = 2; k <= N2; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < N2; i += blockDim.x) {
-                const int ixj = i ^ j;
-                if (ixj > i) {
-                    const unsigned long long a = s_key[i], c = s_key[ixj];
-                    if (((i & k) == 0) ? (a < c) : (a > c)) {
-                        s_key[i] = c;
-                        s_key[ixj] = a;
-                    }
-                }
-            }
-            __syncthreads();
-        }
-    }
+    block_select_top(s_key, N, kNQ, s_top);
     const float sf_h = __fdiv_rn((float)kImg, (float)ori_hw[2 * b]);
     const float sf_w = __fdiv_rn((float)kImg, (float)ori_hw[2 * b + 1]);
     const float oh = floorf(__fadd_rn(__fdiv_rn((float)kImg, sf_h), 0.5f));
     const float ow = floorf(__fadd_rn(__fdiv_rn((float)kImg, sf_w), 0.5f));
     for (int r = threadIdx.x; r < kNQ; r += blockDim.x) {
-        const int flat = (int)(0xFFFFFFFFu - (unsigned)(s_key[r] & 0xFFFFFFFFull));
+        const int flat = (int)select_index(s_top[r]);
         const int q = flat / kNC, c = flat - q * kNC;
         const float *bx = boxes + ((long long)b * kNQ + q) * 4;
         float *o = dets + ((long long)b * kNQ + r) * 7;
@@ -267,7 +253,11 @@ Status launch_refine(const float *delta, float *ref, long long n, cudaStream_t s
 Status launch_row_scale(const float *x, const float *v, float *y, long long rows_per_page, int D,
                         int B, cudaStream_t st) {
     const long long n = (long long)B * rows_per_page * D;
-    row_scale_kernel<<<blocks(n), 256, 0, st>>>(x, v, y, rows_per_page, D, n);
+    if (D % 4 || n / 4 >= (1LL << 31) || ((uintptr_t)x & 15) || ((uintptr_t)y & 15))
+        return ERR_SHAPE;
+    row_scale_kernel<<<blocks(n / 4), 256, 0, st>>>(
+        reinterpret_cast<const float4 *>(x), v, reinterpret_cast<float4 *>(y),
+        (unsigned)rows_per_page, (unsigned)(D / 4), (unsigned)(n / 4));
     return cuda_status();
 }
 
@@ -284,7 +274,7 @@ Status launch_postprocess(const float *logits, const float *boxes, const float *
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
-    const int smem = 8192 * (int)sizeof(unsigned long long);
+    const int smem = kNQ * kNC * (int)sizeof(unsigned long long);
     if (dev < 64 && !attr_set[dev]) {
         if (cudaFuncSetAttribute(pp_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  smem) != cudaSuccess)

@@ -8,16 +8,13 @@
 // (order-preserving bits of its max logit << 32 | ~index), so "descending
 // key" is exactly the reference order including the tie rule; -0.0 is
 // folded to +0.0 first because the reference compares values, under which
-// the two zeros tie.  The keys are unique, so the nq largest are exactly
-// the keys >= the nq-th largest, which a radix select finds: eight passes
-// over the keys in shared memory, each building a 256-bin histogram of the
-// next byte among the keys that match the prefix found so far (lanes with
-// the same bin add once per warp), and one scan of the bins (the logits
-// reach the keys through shared memory, 512 tokens at a time).  The nq
-// winners are compacted and bitonic-sorted (nq <= 512), and their indices
-// written out.  Larger nq fall back to a bitonic sort of all keys.
+// the two zeros tie.  The keys are unique; the nq largest come from the
+// block radix select of select.cuh (the logits reach the keys through
+// shared memory, 512 tokens at a time).  Larger nq fall back to a bitonic
+// sort of all keys.
 #include "common.cuh"
 #include "kernels.h"
+#include "select.cuh"
 
 namespace ppdl {
 
@@ -67,16 +64,14 @@ topk_kernel(const float *__restrict__ lg, int32_t *__restrict__ out, int ntok, i
             (int32_t)(0xFFFFFFFFu - (unsigned)(s_key[r] & 0xFFFFFFFFull));
 }
 
-constexpr int kSelMax = 512;  // largest nq the radix-select form handles
 constexpr size_t kSelSmemMax = 200 * 1024;  // its dynamic shared memory: keys + staged logits
 
+// key of token q: its max logit over the classes, in the reference's order
+// (the first of equal values kept: std::max), and its index
 __device__ __forceinline__ unsigned long long topk_key(const float *p, int nc, int q) {
     float m = p[0];
     for (int c = 1; c < nc; c++) m = (m < p[c]) ? p[c] : m;  // std::max
-    if (m == 0.0f) m = 0.0f;                                 // -0 ties +0
-    unsigned u = __float_as_uint(m);
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)q);
+    return select_key(m, (unsigned)q);
 }
 
 constexpr int kChunk = 512;  // tokens whose logits are staged in shared memory at a time
@@ -86,14 +81,11 @@ topk_select_kernel(const float *__restrict__ lg, int32_t *__restrict__ out, int 
                    int nq) {
     extern __shared__ unsigned long long s_key[];  // ntok keys, then kChunk x nc logits
     float *s_lg = reinterpret_cast<float *>(s_key + ntok);
-    __shared__ unsigned s_hist[256];
-    __shared__ unsigned long long s_sel[kSelMax];
-    __shared__ unsigned long long s_prefix, s_mask;
-    __shared__ unsigned s_need, s_cnt;
+    __shared__ unsigned long long s_sel[kSelectMax];
     const float *lb = lg + (size_t)blockIdx.x * ntok * nc;
     // keys: the page's logits pass through shared memory in chunks of tokens
     // (asynchronous coalesced 4-byte copies, all in flight together), then a
-    // thread takes the max over its token's classes in the reference's order
+    // thread takes the max over its token's classes
     const uint32_t s_lg_addr = (uint32_t)__cvta_generic_to_shared(s_lg);
     for (int t0 = 0; t0 < ntok; t0 += kChunk) {
         const int n = (ntok - t0 < kChunk ? ntok - t0 : kChunk) * nc;
@@ -108,67 +100,9 @@ topk_select_kernel(const float *__restrict__ lg, int32_t *__restrict__ out, int 
         if (threadIdx.x < kChunk && q < ntok) s_key[q] = topk_key(s_lg + threadIdx.x * nc, nc, q);
         __syncthreads();
     }
-    if (threadIdx.x == 0) {
-        s_prefix = 0ull;
-        s_mask = 0ull;
-        s_need = (unsigned)nq;  // winners still to place at or below the current prefix
-        s_cnt = 0;
-    }
-    const int lane = threadIdx.x & 31;
-    for (int shift = 56; shift >= 0; shift -= 8) {
-        for (int b = threadIdx.x; b < 256; b += kThreads) s_hist[b] = 0;
-        __syncthreads();
-        const unsigned long long prefix = s_prefix, mask = s_mask;
-        for (int q0 = 0; q0 < ntok; q0 += kThreads) {
-            const int q = q0 + threadIdx.x;
-            const bool in = q < ntok && (s_key[q] & mask) == prefix;
-            const unsigned bin = in ? (unsigned)(s_key[q] >> shift) & 255u : 256u;
-            // lanes of a warp with the same bin add once
-            const unsigned same = __match_any_sync(0xffffffffu, bin);
-            if (in && lane == __ffs(same) - 1) atomicAdd(&s_hist[bin], __popc(same));
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            // the bin holding the need-th largest key among the matching ones
-            unsigned above = 0, need = s_need;
-            int b = 255;
-            for (; b > 0; b--) {
-                if (above + s_hist[b] >= need) break;
-                above += s_hist[b];
-            }
-            s_prefix = prefix | ((unsigned long long)b << shift);
-            s_mask = mask | (255ull << shift);
-            s_need = need - above;
-        }
-        __syncthreads();
-    }
-    // s_prefix is now the nq-th largest key: the winners are the keys >= it
-    const unsigned long long thr = s_prefix;
-    for (int q = threadIdx.x; q < ntok; q += kThreads) {
-        const unsigned long long k = s_key[q];
-        if (k >= thr) s_sel[atomicAdd(&s_cnt, 1u)] = k;
-    }
-    for (int i = nq + threadIdx.x; i < kSelMax; i += kThreads) s_sel[i] = 0ull;
-    __syncthreads();
-    // bitonic sort of the kSelMax entries, descending
-    for (int k = 2; k <= kSelMax; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < kSelMax; i += kThreads) {
-                const int ixj = i ^ j;
-                if (ixj > i) {
-                    const unsigned long long a = s_sel[i], b = s_sel[ixj];
-                    const bool desc = (i & k) == 0;
-                    if (desc ? (a < b) : (a > b)) {
-                        s_sel[i] = b;
-                        s_sel[ixj] = a;
-                    }
-                }
-            }
-            __syncthreads();
-        }
-    }
+    block_select_top(s_key, ntok, nq, s_sel);
     for (int r = threadIdx.x; r < nq; r += kThreads)
-        out[(size_t)blockIdx.x * nq + r] = (int32_t)(0xFFFFFFFFu - (unsigned)(s_sel[r] & 0xFFFFFFFFull));
+        out[(size_t)blockIdx.x * nq + r] = (int32_t)select_index(s_sel[r]);
 }
 
 }  // namespace
@@ -193,7 +127,7 @@ Status launch_topk(const float *lg, int32_t *out, int ntok, int nc, int nq, int 
         attr_set[dev] = true;
     }
     const size_t sel_smem = (size_t)ntok * sizeof(unsigned long long) + (size_t)kChunk * nc * 4;
-    if (nq <= kSelMax && sel_smem <= kSelSmemMax)
+    if (nq <= kSelectMax && sel_smem <= kSelSmemMax)
         topk_select_kernel<<<batch, kThreads, sel_smem, stream>>>(lg, out, ntok, nc, nq);
     else
         topk_kernel<<<batch, kThreads, smem, stream>>>(lg, out, ntok, nc, nq, n2);
