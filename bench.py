@@ -509,15 +509,18 @@ def run_forward(args, world, rank, local, pg):
         roof["algorithmic_bytes_per_launch"] = round(
             sum(s[4] for s in gsteps) * B / max(1, len(gsteps)))
 
-    # ---- e2e: ppdl_infer_batch with host images, dets + masks back to host
-    ctx.infer_batch(pages, hw)
+    # ---- e2e: ppdl_infer_batch with the pages in pinned host memory; the
+    # dets and int32 masks come back into the context's pinned buffers and
+    # are read there (views, no extra host copy)
+    h_pages = torch.from_numpy(pages).pin_memory().numpy()
+    ctx.infer_batch(h_pages, hw, copy=False)
     barrier(pg)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e2e_steps = max(3, min(K, 5))
     e0.record(st)
     for _ in range(e2e_steps):
-        ctx.infer_batch(pages, hw)
+        res = ctx.infer_batch(h_pages, hw, copy=False)
     e1.record(st)
     torch.cuda.synchronize(dev)
     barrier(pg)
@@ -553,7 +556,8 @@ def run_forward(args, world, rank, local, pg):
         "roofline": roof,
         "e2e": {"value": round(e2e_val, 2), "unit": "pages/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "path": "ppdl_infer_batch (host images in, dets + int32 masks out)"},
+                "path": "ppdl_infer_batch (pinned host images in, dets + int32 masks out "
+                        "into pinned host buffers)"},
         "gpu_launches": len(steps) * K,
         "clocks": clk,
     }

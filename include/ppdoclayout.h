@@ -94,7 +94,8 @@ PPDL_API void * ppdl_stream(ppdl_ctx * ctx);
    forward of the n pages of the last call once more with a CUDA event after
    every step — captured into a CUDA graph and replayed, so the times are
    device time without host launch gaps (eagerly if the capture fails) — and
-   fills up to max entries.  Returns the number of steps written, or -1. */
+   fills up to max entries.  The steps run one after another here, so each
+   time is the step alone.  Returns the number of steps written, or -1. */
 #define PPDL_STEP_OTHER         0
 #define PPDL_STEP_GEMM_1X1      1   /* 1x1 conv GEMM                     */
 #define PPDL_STEP_WG_MADD       2   /* Winograd 36-plane GEMM            */
@@ -119,6 +120,15 @@ typedef struct {
     double  bytes;  /* algorithmic bytes per page */
 } ppdl_step_stat;
 PPDL_API int ppdl_profile_steps(ppdl_ctx * ctx, int n, ppdl_step_stat * out, int max);
+
+/* extension: timeline of the forward as it runs — its steps on their lanes
+   (CUDA streams inside the captured forward: lane 0 the decoder chain, 1 the
+   value projections, 2 projections beside the chain), with an event after
+   every step on its own lane.  end_ms[i] = end of step i (the order of
+   ppdl_profile_steps) from the start of the forward, lane[i] its lane.
+   Returns the number of steps written, or -1 (also when the capture fails). */
+PPDL_API int ppdl_profile_timeline(ppdl_ctx * ctx, int n, float * end_ms, int32_t * lane,
+                                   int max);
 
 /* reference :54-56 (src/ppdoclayout.cpp:1193-1213): writes the intermediate
    tensors of page 0 of the last call plus shapes.txt.  Non-zero when dumps

@@ -998,13 +998,18 @@ bool plan_common(TcGemm *g, int M, int N, int K, int batch, int planes, const Tc
     g->ok = false;
     if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || planes <= 0) return false;
     // N tile (multiple of 16, <= 128 so that the partial slots and the A
-    // stages fit in the 512 TMEM columns); cost model: tiles x
-    // (bn + 64), the 64 standing for the per-tile A traffic and epilogue
-    // overhead in column equivalents
+    // stages fit in the 512 TMEM columns); cost model: the tiles one CTA
+    // runs, ceil(tiles / SMs), x (bn + 64), the 64 standing for the per-tile
+    // A traffic and epilogue overhead in column equivalents.  A GEMM of a
+    // few dozen row tiles (the decoder's 2400 rows) thus takes narrower N
+    // tiles and spreads over more SMs.
+    const long long row_tiles = (long long)((M + kBM - 1) / kBM) * batch;
+    const long long sms = sm_count();
     int bn = 16;
     long long best = -1;
     for (int c = 16; c <= kMaxBN; c += 16) {
-        const long long cost = (long long)((N + c - 1) / c) * (c + 64);
+        const long long tiles = row_tiles * ((N + c - 1) / c);
+        const long long cost = (tiles + sms - 1) / sms * (c + 64);
         if (best < 0 || cost < best || (cost == best && c > bn)) {
             best = cost;
             bn = c;
@@ -1136,6 +1141,7 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
               ((uint32_t)(kBM >> 4) << 24);
     a.epi = g.epi;
     int grid = sm_count();
+    if (g.max_ctas > 0 && grid > g.max_ctas) grid = g.max_ctas;
     if (grid > g.tiles) grid = g.tiles;
     switch (g.epi.act) {
         case ACT_RELU:

@@ -53,6 +53,7 @@ struct TcGemm {
     int stages = 2;
     size_t smem = 0;
     int m_tiles = 0, n_tiles = 0, tiles = 0;
+    int max_ctas = 0;    // > 0: at most this many CTAs (SMs left to concurrent launches)
     TcEpilogue epi;
     bool ok = false;
 };

@@ -84,12 +84,26 @@ struct Dump {
 
 // One launch group of the plan: a name, a kernel class (PPDL_STEP_*), the
 // algorithmic FLOPs and bytes per page, and the closure that enqueues it.
+// Steps run on lanes (streams) inside the forward: lane 0 is the context's
+// stream; a step waits for the plan events in `waits` (each recorded after
+// an earlier step of another lane) and records event `record` after itself.
+// Latency-bound decoder launches that use a few dozen SMs then overlap with
+// each other and with the value projections.
 struct Step {
     std::string name;
     int kind;
     double flops, bytes;
     std::function<Status()> fn;
+    int lane = 0;
+    std::vector<int> waits;
+    int record = -1;
 };
+
+constexpr int kLanes = 3;
+#ifndef PPDL_VP_CTAS
+#define PPDL_VP_CTAS 64
+#endif
+constexpr int kVpCtas = PPDL_VP_CTAS;  // SMs a value projection may hold (of 148)
 
 #define TRY(x)                         \
     do {                               \
@@ -109,6 +123,10 @@ public:
     std::unordered_map<std::string, WT> w;
     std::vector<void *> allocs;
     std::vector<Step> plan;
+    int lane = 0, lane_last[kLanes] = {-1, -1, -1}, n_events = 0;
+    std::vector<int> pending;
+    cudaStream_t lanes[kLanes] = {};
+    std::vector<cudaEvent_t> events;  // n_events plan events + kLanes fork/join
     std::map<int, cudaGraphExec_t> graphs;
     std::vector<Dump> dump_list;
 
@@ -128,7 +146,9 @@ public:
     ~Model() {
         for (auto &g : graphs) cudaGraphExecDestroy(g.second);
         for (void *p : allocs) cudaFree(p);
-        if (st) cudaStreamDestroy(st);
+        for (auto e : events) cudaEventDestroy(e);
+        for (int l = 0; l < kLanes; l++)
+            if (lanes[l]) cudaStreamDestroy(lanes[l]);
     }
 
     // Tensor-core (3xTF32) GEMMs for every contraction whose operands satisfy
@@ -212,7 +232,28 @@ public:
 
     template <typename F>
     void push(const std::string &name, int kind, double flops, double bytes, F fn) {
-        plan.push_back(Step{name, kind, flops, bytes, std::function<Status()>(fn)});
+        Step s{name, kind, flops, bytes, std::function<Status()>(fn)};
+        s.lane = lane;
+        s.waits.swap(pending);
+        lane_last[lane] = (int)plan.size();
+        plan.push_back(std::move(s));
+    }
+    // event recorded after the latest step of the current lane (all of that
+    // lane's steps so far are done when it fires)
+    int mark() {
+        const int li = lane_last[lane];
+        if (li < 0) {
+            fail("mark on an empty lane");
+            return 0;
+        }
+        if (plan[li].record < 0) plan[li].record = n_events++;
+        return plan[li].record;
+    }
+    // the next step pushed on the current lane waits for event e
+    void after(int e) { pending.push_back(e); }
+    void on_lane(int l) {
+        if (!pending.empty()) fail("lane switch with pending waits");
+        lane = l;
     }
 
     void fail(const std::string &m) {
@@ -510,7 +551,7 @@ public:
 
     // y = act(x W^T + b) (+ res), rows of all pages folded into M
     void lin(const S &x, const S &y, const std::string &name, int act = ACT_NONE,
-             const S &res = S()) {
+             const S &res = S(), int max_ctas = 0) {
         const WT &wt = W(name + ".weight");
         const WT &bt = W(name + ".bias");
         if (!ok) return;
@@ -531,6 +572,7 @@ public:
             auto g = std::make_shared<TcGemm>();
             if (ok && tc_gemm_plan(g.get(), Bmax * x.T, out, in, 1, x.p, 0, in, 0, wsp.hi, wsp.lo, 1,
                                    e)) {
+                g->max_ctas = max_ctas;
                 const int T = x.T;
                 push(name, PPDL_STEP_GEMM_LINEAR, 2.0 * x.T * out * in,
                      4.0 * ((double)x.T * (in + out) + (double)in * out),
@@ -577,14 +619,25 @@ public:
         lin(h2, y, pfx + ".2");
     }
 
-    // MHA, 8 heads x 32, q/k from qk_in, v from v_in (src/ppdoclayout.cpp:572-587)
-    void mha(const S &qk_in, const S &v_in, const S &out, const std::string &pfx) {
+    // MHA, 8 heads x 32, q/k from qk_in, v from v_in (src/ppdoclayout.cpp:572-587).
+    // Called on lane 0 with qk_in and v_in written there; k and v are
+    // projected on lane 2 beside q.  A caller that projected v earlier (on
+    // lane 2) passes it as v_pre.
+    void mha(const S &qk_in, const S &v_in, const S &out, const std::string &pfx,
+             const S &v_pre = S()) {
         const int T = qk_in.T;
-        S q = seq(T, kDM), k = seq(T, kDM), v = seq(T, kDM), o = seq(T, kDM);
-        lin(qk_in, q, pfx + ".q");
+        S q = seq(T, kDM), k = seq(T, kDM), o = seq(T, kDM);
+        S v = v_pre.p ? v_pre : seq(T, kDM);
+        const int e_in = mark();
+        on_lane(2);
+        after(e_in);
+        if (!v_pre.p) lin(v_in, v, pfx + ".v");
         lin(qk_in, k, pfx + ".k");
-        lin(v_in, v, pfx + ".v");
+        const int e_kv = mark();
+        on_lane(0);
+        lin(qk_in, q, pfx + ".q");
         // softmax(q k^T / sqrt(32)) v in one launch (scores stay on chip)
+        after(e_kv);
         push(pfx + ".attn", PPDL_STEP_ATTENTION, 4.0 * kNH * T * T * kHD,
              4.0 * 4.0 * T * kDM, [=]() {
             return launch_attention(q.p, k.p, v.p, o.p, T, kNH, kDM, (long long)T * kDM,
@@ -770,6 +823,23 @@ public:
         conv1x1_tok(n16, source, 10000, "dec_in1");
         conv1x1_tok(n32, source, 12500, "dec_in2");
         dump_seq("source", source);
+        // the six layers' value projections of `source` (:836) on lane 1,
+        // beside the encoder head and the decoder chain, each on at most
+        // kVpCtas SMs so that the chain keeps the rest
+        S values[6];
+        int e_vp[6];
+        {
+            const int e_src = mark();
+            on_lane(1);
+            after(e_src);
+            for (int i = 0; i < 6; i++) {
+                values[i] = seq(kNTok, kDM);
+                lin(source, values[i], "dec" + std::to_string(i) + ".ca.vp", ACT_NONE, S(),
+                    kVpCtas);
+                e_vp[i] = mark();
+            }
+            on_lane(0);
+        }
         S memory = seq(kNTok, kDM), eo = seq(kNTok, kDM), om = seq(kNTok, kDM);
         S ecls = seq(kNTok, kNC);
         {
@@ -839,22 +909,38 @@ public:
              [=]() { return launch_sigmoid(refu.p, ref.p, (long long)nb * refu.bs(), st); });
 
         // ---- decoder layers (:824-851)
+        // lane 2 takes the projections off the chain: v of the self-attention
+        // (from x, beside the previous layer's box head and this layer's query
+        // position MLP), k beside q, and the attention weights beside the
+        // sampling offsets
         S x = target;
-        S value = seq(kNTok, kDM);
+        int e_x = mark();
         for (int i = 0; i < 6; i++) {
             const std::string dp = "dec" + std::to_string(i);
+            const S value = values[i];
+            S v = seq(kNQ, kDM);
+            on_lane(2);
+            after(e_x);
+            lin(x, v, dp + ".sa.v");
+            on_lane(0);
             S qp1 = seq(kNQ, (int)W("qpos.0.weight").ne[1]), qpos = seq(kNQ, kDM);
             lin(ref, qp1, "qpos.0", ACT_RELU);
             lin(qp1, qpos, "qpos.1");
             S qk2 = seq(kNQ, kDM), sa = seq(kNQ, kDM), x1 = seq(kNQ, kDM);
             add(x, qpos, qk2);
-            mha(qk2, x, sa, dp + ".sa");
+            mha(qk2, x, sa, dp + ".sa", v);
             ln(x, x1, dp + ".ln1", sa);
             S z = seq(kNQ, kDM), offs = seq(kNQ, 192), aw = seq(kNQ, 96), ca = seq(kNQ, kDM);
             add(x1, qpos, z);
-            lin(source, value, dp + ".ca.vp");
-            lin(z, offs, dp + ".ca.so");
+            const int e_z = mark();
+            on_lane(2);
+            after(e_z);
             lin(z, aw, dp + ".ca.aw");
+            const int e_aw = mark();
+            on_lane(0);
+            lin(z, offs, dp + ".ca.so");
+            after(e_aw);
+            after(e_vp[i]);
             push(dp + ".msda", PPDL_STEP_MSDA, 0.0,
                  4.0 * ((double)kNTok * kDM + kNQ * (192.0 + 96.0 + 4.0 + kDM)), [=]() {
                 return launch_msda(value.p, offs.p, aw.p, ref.p, ca.p, kNQ, nb, false, st);
@@ -870,6 +956,7 @@ public:
             static const char *hn[6] = {"hidden0", "hidden1", "hidden2",
                                         "hidden3", "hidden4", "hidden5"};
             dump_seq(hn[i], x3);
+            e_x = mark();
             S delta = seq(kNQ, 4);
             mlp3(x3, delta, "bbox_head");
             push(dp + ".refine", PPDL_STEP_GLUE, 0.0, 12.0 * ref.bs(),
@@ -886,7 +973,10 @@ public:
         mlp3(outq, mq6, "mq");
         mask_logits = dalloc((long long)kNQ * kMaskPix * Bmax);
         mask_gemm(mq6, mask_logits);
+        // the reading-order head on lane 2, beside the class/mask heads
         S oh = seq(kNQ, kDM), gp = seq(kNQ, 128);
+        on_lane(2);
+        after(e_x);
         lin(x, oh, "order5");
         lin(oh, gp, "gp");
         order = seq(kNQ, kNQ);
@@ -903,6 +993,8 @@ public:
                 return launch_gemm_simt(g, st);
             });
         }
+        const int e_order = mark();
+        on_lane(0);
         // ---- postprocess (:927-993)
         dets = dalloc((long long)kNQ * 7 * Bmax);
         if (cudaMalloc(&sel, sizeof(int32_t) * kNQ * Bmax) != cudaSuccess) fail("cudaMalloc");
@@ -915,6 +1007,7 @@ public:
         {
             const S lg = logits, bx = boxes, od = order;
             const float *mlp = mask_logits;
+            after(e_order);
             push("postprocess", PPDL_STEP_POSTPROCESS, 0.0,
                  4.0 * ((double)kNQ * kNQ + 2.0 * kNQ * kMaskPix), [=]() {
                 return launch_postprocess(lg.p, bx.p, od.p, mlp, ori_hw, rank, dets, sel, masks, nb,
@@ -945,6 +1038,12 @@ public:
             fail("no CUDA device / stream");
             return false;
         }
+        lanes[0] = st;
+        for (int l = 1; l < kLanes; l++)
+            if (cudaStreamCreateWithFlags(&lanes[l], cudaStreamNonBlocking) != cudaSuccess) {
+                fail("stream creation failed");
+                return false;
+            }
         if (!load(path)) return false;
         // host constants (src/ppdoclayout.cpp:887-923), float64 math as there
         std::vector<float> hp((size_t)kDM * 625), hv(kNTok);
@@ -981,11 +1080,55 @@ public:
         cudaMemcpy(valid, hv.data(), hv.size() * 4, cudaMemcpyHostToDevice);
         build();
         if (!ok) return false;
+        if (lane != 0 || !pending.empty()) {
+            fail("plan ends off lane 0 or with pending waits");
+            return false;
+        }
+        events.resize(n_events + kLanes);
+        for (auto &e : events)
+            if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+                e = nullptr;
+                fail("event creation failed");
+                return false;
+            }
         if (cudaStreamSynchronize(st) != cudaSuccess) {
             fail("weight transform failed");
             return false;
         }
         return true;
+    }
+
+    // Enqueues the plan on its lanes: every side lane first waits for the
+    // work already on lane 0 (fork) and lane 0 ends by waiting for every side
+    // lane (join), so the forward is ordered on the context's stream as one
+    // unit, eager or captured.  The launch closures read `st` when called, so
+    // it names the step's lane while the step is enqueued.
+    Status exec(const std::function<bool(int)> &after_step = nullptr) {
+        cudaStream_t main = lanes[0];
+        const int fork = n_events, join = n_events + 1;
+        if (cudaEventRecord(events[fork], main) != cudaSuccess) return ERR_CUDA;
+        for (int l = 1; l < kLanes; l++)
+            if (cudaStreamWaitEvent(lanes[l], events[fork], 0) != cudaSuccess) return ERR_CUDA;
+        Status s = OK;
+        for (size_t i = 0; i < plan.size(); i++) {
+            const Step &f = plan[i];
+            st = lanes[f.lane];
+            for (int e : f.waits)
+                if (cudaStreamWaitEvent(st, events[e], 0) != cudaSuccess) s = ERR_CUDA;
+            if (s == OK) s = f.fn();
+            if (s == OK && after_step && !after_step((int)i)) s = ERR_CUDA;
+            if (s == OK && f.record >= 0 && cudaEventRecord(events[f.record], st) != cudaSuccess)
+                s = ERR_CUDA;
+            if (s != OK) break;
+        }
+        st = main;
+        for (int l = 1; l < kLanes; l++) {  // join even after an error (ends a capture cleanly)
+            const int e = join + l - 1;
+            if (cudaEventRecord(events[e], lanes[l]) != cudaSuccess ||
+                cudaStreamWaitEvent(main, events[e], 0) != cudaSuccess)
+                s = s == OK ? ERR_CUDA : s;
+        }
+        return s;
     }
 
     // Runs the plan for n pages: eagerly the first time (sets kernel
@@ -996,16 +1139,12 @@ public:
         if (it != graphs.end()) {
             return cudaGraphLaunch(it->second, st) == cudaSuccess ? OK : ERR_CUDA;
         }
-        for (auto &f : plan) TRY(f.fn());
+        TRY(exec());
         if (cudaStreamSynchronize(st) != cudaSuccess) return ERR_CUDA;
         cudaGraph_t g = nullptr;
         if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
             return OK;  // eager result stands; no graph
-        Status s = OK;
-        for (auto &f : plan) {
-            s = f.fn();
-            if (s != OK) break;
-        }
+        const Status s = exec();
         if (cudaStreamEndCapture(st, &g) != cudaSuccess || s != OK) {
             if (g) cudaGraphDestroy(g);
             cudaGetLastError();
@@ -1244,6 +1383,46 @@ PPDL_API int ppdl_dump_raw(ppdl_ctx *c, const char *pfx) {
 }
 
 PPDL_API void *ppdl_stream(ppdl_ctx *c) { return c ? (void *)c->m->st : nullptr; }
+
+PPDL_API int ppdl_profile_timeline(ppdl_ctx *c, int n, float *end_ms, int32_t *lane, int max) {
+    if (!c || !end_ms || !lane || max <= 0 || n < 1 || n > c->m->Bmax || !c->computed) return -1;
+    ppdl::Model &m = *c->m;
+    cudaSetDevice(m.dev);
+    const int ns = (int)m.plan.size();
+    std::vector<cudaEvent_t> ev(ns + 1);
+    for (auto &e : ev) cudaEventCreate(&e);
+    m.nb = n;
+    // the forward on its lanes, captured with an "external" event-record
+    // node after every step on the step's own lane, replayed twice (the
+    // second timed): end time of each step from the start of the forward
+    int rc = 0;
+    cudaGraph_t gr = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    bool graphed = false;
+    if (cudaStreamBeginCapture(m.st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+        bool ok = cudaEventRecordWithFlags(ev[0], m.st, cudaEventRecordExternal) == cudaSuccess;
+        ok = ok && m.exec([&](int i) {
+            return cudaEventRecordWithFlags(ev[i + 1], m.st, cudaEventRecordExternal) ==
+                   cudaSuccess;
+        }) == ppdl::OK;
+        if (cudaStreamEndCapture(m.st, &gr) == cudaSuccess && ok &&
+            cudaGraphInstantiate(&ge, gr, 0) == cudaSuccess)
+            graphed = cudaGraphLaunch(ge, m.st) == cudaSuccess &&
+                      cudaGraphLaunch(ge, m.st) == cudaSuccess;
+    }
+    cudaGetLastError();
+    if (!graphed || cudaStreamSynchronize(m.st) != cudaSuccess) rc = -1;
+    int w = 0;
+    if (rc == 0)
+        for (int i = 0; i < ns && w < max; i++, w++) {
+            cudaEventElapsedTime(&end_ms[w], ev[0], ev[i + 1]);
+            lane[w] = m.plan[i].lane;
+        }
+    if (ge) cudaGraphExecDestroy(ge);
+    if (gr) cudaGraphDestroy(gr);
+    for (auto &e : ev) cudaEventDestroy(e);
+    return rc == 0 ? w : -1;
+}
 
 PPDL_API int ppdl_profile_steps(ppdl_ctx *c, int n, ppdl_step_stat *out, int max) {
     if (!c || !out || max <= 0 || n < 1 || n > c->m->Bmax || !c->computed) return -1;

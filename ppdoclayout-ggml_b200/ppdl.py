@@ -170,8 +170,15 @@ class Context:
         masks = np.ctypeslib.as_array(res.masks, (NUM_DETS, MASK_HW, MASK_HW)).copy()
         return dets, masks, res.infer_ms
 
-    def infer_batch(self, images, ori_hw):
-        """n pages [n,3,800,800] -> list of (dets, masks) (copies)."""
+    def infer_batch(self, images, ori_hw, copy=True):
+        """n pages [n,3,800,800] -> list of (dets, masks).
+
+        copy=True returns arrays the caller owns.  copy=False returns views
+        of the context's pinned host buffers (what ppdl_infer_batch's
+        ppdl_result points at), valid until the next inference on this
+        context; it skips the 48 MB-per-page host copy of the masks.  Pages
+        given in pinned host memory (e.g. a pinned torch tensor's .numpy())
+        are copied to the device at full PCIe speed."""
         import numpy as np
         imgs = np.ascontiguousarray(images, dtype=np.float32)
         hw = np.ascontiguousarray(ori_hw, dtype=np.int32).reshape(-1, 2)
@@ -182,8 +189,9 @@ class Context:
             raise RuntimeError(f"ppdl_infer_batch returned {rc}")
         out = []
         for r in res:
-            out.append((np.ctypeslib.as_array(r.dets, (NUM_DETS, DET_FIELDS)).copy(),
-                        np.ctypeslib.as_array(r.masks, (NUM_DETS, MASK_HW, MASK_HW)).copy()))
+            d = np.ctypeslib.as_array(r.dets, (NUM_DETS, DET_FIELDS))
+            m = np.ctypeslib.as_array(r.masks, (NUM_DETS, MASK_HW, MASK_HW))
+            out.append((d.copy(), m.copy()) if copy else (d, m))
         return out
 
     def infer_device(self, d_images_ptr: int, n: int, ori_hw) -> int:
@@ -219,6 +227,20 @@ class Context:
             raise RuntimeError("ppdl_profile_steps failed")
         return [(buf[i].name.decode(), STEP_KINDS.get(buf[i].kind, "other"), buf[i].ms,
                  buf[i].flops, buf[i].bytes) for i in range(k)]
+
+    def profile_timeline(self, n: int):
+        """[(end_ms, lane)] per step (the order of profile_steps): the end of
+        each step from the start of the forward, with the lanes running
+        concurrently as in the captured forward."""
+        self.lib.ppdl_profile_timeline.argtypes = [C.c_void_p, C.c_int, C.POINTER(C.c_float),
+                                                   C.POINTER(C.c_int32), C.c_int]
+        self.lib.ppdl_profile_timeline.restype = C.c_int
+        end = (C.c_float * 4096)()
+        lane = (C.c_int32 * 4096)()
+        k = self.lib.ppdl_profile_timeline(self.ctx, n, end, lane, 4096)
+        if k < 0:
+            raise RuntimeError("ppdl_profile_timeline failed")
+        return [(end[i], lane[i]) for i in range(k)]
 
     def dump_raw(self, pfx: str) -> int:
         return self.lib.ppdl_dump_raw(self.ctx, pfx.encode())
