@@ -47,28 +47,31 @@ __device__ __forceinline__ float warp_sum32(float v) {
     return v;
 }
 
-// q, k, v, o: token-major [B][T][ld] with head h at columns h*32 .. h*32+31.
+// q, k: token-major [B][T][ldqk] (page stride bsqk), v, o: [B][T][ldvo]
+// (page stride bsvo), head h at columns h*32 .. h*32+31 of each.
 // Shared memory: Q [32][36] | two K/V tiles [64][36] | scores [32][ldS], ldS
 // a multiple of 4.  Rows of 36 floats keep the 16-byte loads of a quarter
 // warp on distinct banks.  The K and V tiles stream through the two buffers
 // with cp.async, the next tile landing while the current one is used.
 __global__ void __launch_bounds__(kThreads, 2)
 attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
-            float *__restrict__ o, int T, int ld, long long bs, float scale, int ldS) {
+            float *__restrict__ o, int T, int ldqk, long long bsqk, int ldvo, long long bsvo,
+            float scale, int ldS) {
     extern __shared__ float sm[];
     float *Qs = sm;                 // [kBQ][kLD]
     float *Tb = Qs + kBQ * kLD;     // [2][kKT][kLD]
     float *Ss = Tb + 2 * kKT * kLD; // [kBQ][ldS]
     const int q0 = blockIdx.x * kBQ, h = blockIdx.y, b = blockIdx.z;
     const int t = threadIdx.x, lane = t & 31, wq = t >> 5;  // wq: query group of 4
-    const long long base = (long long)b * bs + h * kHeadDim;
+    const long long base_qk = (long long)b * bsqk + h * kHeadDim;
+    const long long base_vo = (long long)b * bsvo + h * kHeadDim;
 
     for (int i = t; i < kBQ * kHeadDim; i += kThreads) {
         const int r = i >> 5, d = i & 31;
-        Qs[r * kLD + d] = q0 + r < T ? q[base + (long long)(q0 + r) * ld + d] : 0.0f;
+        Qs[r * kLD + d] = q0 + r < T ? q[base_qk + (long long)(q0 + r) * ldqk + d] : 0.0f;
     }
     // tile j of K or V into buffer (j & 1); rows past T are zero-filled
-    auto load_tile = [&](const float *src, int j) {
+    auto load_tile = [&](const float *src, int j, int ld, long long base) {
         float *dst = Tb + (j & 1) * kKT * kLD;
         for (int i = t; i < kKT * kHeadDim / 4; i += kThreads) {
             const int r = i >> 3, c4 = i & 7, row = j * kKT + r;
@@ -80,11 +83,11 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
     };
     const int nt = (T + kKT - 1) / kKT;
     // ---- scores: thread -> queries 4wq..4wq+3, keys lane and lane+32 of a tile
-    load_tile(k, 0);
+    load_tile(k, 0, ldqk, base_qk);
     for (int jt = 0; jt < nt; jt++) {
         const int j0 = jt * kKT;
         if (jt + 1 < nt) {
-            load_tile(k, jt + 1);
+            load_tile(k, jt + 1, ldqk, base_qk);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
@@ -120,7 +123,7 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
             }
         __syncthreads();  // the buffer is refilled two tiles later
     }
-    load_tile(v, 0);  // lands during the softmax
+    load_tile(v, 0, ldvo, base_vo);  // lands during the softmax
     // ---- row softmax: warp wq owns rows 4wq..4wq+3
 #pragma unroll 1
     for (int r = 0; r < 4; r++) {
@@ -143,7 +146,7 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
     for (int jt = 0; jt < nt; jt++) {
         const int j0 = jt * kKT;
         if (jt + 1 < nt) {
-            load_tile(v, jt + 1);
+            load_tile(v, jt + 1, ldvo, base_vo);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
@@ -174,7 +177,7 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
 #pragma unroll
     for (int r = 0; r < 4; r++) {
         const int i = q0 + wq * 4 + r;
-        if (i < T) o[base + (long long)i * ld + lane] = acc[r];
+        if (i < T) o[base_vo + (long long)i * ldvo + lane] = acc[r];
     }
 }
 
@@ -187,8 +190,13 @@ size_t attention_smem_bytes(int T) {
 }  // namespace
 
 Status launch_attention(const float *q, const float *k, const float *v, float *o, int T, int heads,
-                        int ld, long long bs, float scale, int B, cudaStream_t st) {
-    if (T <= 0 || heads <= 0 || heads > 65535 || B <= 0 || B > 65535 || ld < heads * kHeadDim)
+                        int ldqk, long long bsqk, int ldvo, long long bsvo, float scale, int B,
+                        cudaStream_t st) {
+    if (T <= 0 || heads <= 0 || heads > 65535 || B <= 0 || B > 65535 ||
+        ldqk < heads * kHeadDim || ldvo < heads * kHeadDim)
+        return ERR_SHAPE;
+    // 16-byte rows for the cp.async tiles of k and v
+    if ((((uintptr_t)k | (uintptr_t)v) & 15) || ldqk % 4 || ldvo % 4 || bsqk % 4 || bsvo % 4)
         return ERR_SHAPE;
     const size_t smem = attention_smem_bytes(T);
     if (smem > 227 * 1024) return ERR_SHAPE;
@@ -202,8 +210,8 @@ Status launch_attention(const float *q, const float *k, const float *v, float *o
         attr[dev] = true;
     }
     const int ldS = attention_lds(T);
-    attn_kernel<<<dim3((T + kBQ - 1) / kBQ, heads, B), kThreads, smem, st>>>(q, k, v, o, T, ld,
-                                                                          bs, scale, ldS);
+    attn_kernel<<<dim3((T + kBQ - 1) / kBQ, heads, B), kThreads, smem, st>>>(
+        q, k, v, o, T, ldqk, bsqk, ldvo, bsvo, scale, ldS);
     return cuda_status();
 }
 

@@ -104,16 +104,64 @@ __global__ void sigmoid_kernel(const float *__restrict__ x, float *__restrict__ 
     if (i < n) y[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x[i])));
 }
 
-// ref = sigmoid(delta + inverse_sigmoid(ref)), inverse_sigmoid per :589-594
-__global__ void refine_kernel(const float *__restrict__ delta, float *__restrict__ ref, long long n) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    float x = fminf(fmaxf(ref[i], 0.0f), 1.0f);
-    const float x1 = fminf(fmaxf(x, 1e-5f), 1.0f);
-    const float x2 = fminf(fmaxf(__fsub_rn(1.0f, x), 1e-5f), 1.0f);
-    const float inv = __fsub_rn(logf(x1), logf(x2));
-    const float z = __fadd_rn(delta[i], inv);
-    ref[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+// The decoder layer's box update and the next layer's query-position input
+// in one launch, one warp per query row (src/ppdoclayout.cpp:848-850 and
+// :827):
+//   delta = h W^T + b            (bbox_head.2: 256 -> 4)
+//   ref   = sigmoid(delta + inverse_sigmoid(ref))  (inverse_sigmoid with
+//                                 the clamps of src/ppdoclayout.cpp:589-594)
+//   qp    = relu(ref Wq^T + bq)  (qpos.0: 4 -> nq of the next layer; qp may
+//                                 be null after the last layer)
+// Each lane sums eight consecutive k of the four dot products with fmaf,
+// then the warp adds the lanes' partials pairwise.
+__global__ void box_refine_kernel(const float *__restrict__ h, const float *__restrict__ w,
+                                  const float *__restrict__ b, float *__restrict__ ref,
+                                  const float *__restrict__ wq, const float *__restrict__ bq,
+                                  float *__restrict__ qp, int rows, int nqp) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int lane = threadIdx.x & 31;
+    const float4 *hp = reinterpret_cast<const float4 *>(h + (long long)row * 256 + lane * 8);
+    const float4 h0 = hp[0], h1 = hp[1];
+    const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    float d[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float4 *wp = reinterpret_cast<const float4 *>(w + j * 256 + lane * 8);
+        const float4 w0 = wp[0], w1 = wp[1];
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float acc = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) acc = fmaf(hv[k], wv[k], acc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+        d[j] = __fadd_rn(acc, b[j]);
+    }
+    float r[4];
+    const float4 r4 = *reinterpret_cast<const float4 *>(ref + (long long)row * 4);
+    const float rin[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float x = fminf(fmaxf(rin[j], 0.0f), 1.0f);
+        const float x1 = fminf(fmaxf(x, 1e-5f), 1.0f);
+        const float x2 = fminf(fmaxf(__fsub_rn(1.0f, x), 1e-5f), 1.0f);
+        const float z = __fadd_rn(d[j], __fsub_rn(logf(x1), logf(x2)));
+        r[j] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+    }
+    __syncwarp();
+    if (lane == 0)
+        *reinterpret_cast<float4 *>(ref + (long long)row * 4) = make_float4(r[0], r[1], r[2], r[3]);
+    if (!qp) return;
+    float *q = qp + (long long)row * nqp;
+    for (int o = lane; o < nqp; o += 32) {
+        const float4 wv = *reinterpret_cast<const float4 *>(wq + o * 4);
+        float acc = 0.0f;
+        acc = fmaf(r[0], wv.x, acc);
+        acc = fmaf(r[1], wv.y, acc);
+        acc = fmaf(r[2], wv.z, acc);
+        acc = fmaf(r[3], wv.w, acc);
+        q[o] = fmaxf(__fadd_rn(acc, bq[o]), 0.0f);
+    }
 }
 
 // y[b][t][:] = x[b][t][:] * v[t]; four elements per thread (D % 4 == 0),
@@ -245,8 +293,13 @@ Status launch_sigmoid(const float *x, float *y, long long n, cudaStream_t st) {
     return cuda_status();
 }
 
-Status launch_refine(const float *delta, float *ref, long long n, cudaStream_t st) {
-    refine_kernel<<<blocks(n), 256, 0, st>>>(delta, ref, n);
+Status launch_box_refine(const float *h, const float *w, const float *b, float *ref,
+                         const float *wq, const float *bq, float *qp, int rows, int nqp,
+                         cudaStream_t st) {
+    if (rows <= 0 || (qp && nqp <= 0) ||
+        (((uintptr_t)h | (uintptr_t)w | (uintptr_t)ref | (uintptr_t)wq) & 15))
+        return ERR_SHAPE;
+    box_refine_kernel<<<cdiv(rows, 8), 256, 0, st>>>(h, w, b, ref, wq, bq, qp, rows, nqp);
     return cuda_status();
 }
 

@@ -17,11 +17,17 @@ Status launch_softmax_rows(float *x, long long rows, int L, cudaStream_t st);
 // dims over token-major [B][T][ld] tensors (page stride bs), heads x 32 <= ld;
 // o must not alias q, k or v.
 Status launch_attention(const float *q, const float *k, const float *v, float *o, int T, int heads,
-                        int ld, long long bs, float scale, int B, cudaStream_t st);
+                        int ldqk, long long bsqk, int ldvo, long long bsvo, float scale, int B,
+                        cudaStream_t st);
 Status launch_add(const float *a, const float *b, float *y, long long n, cudaStream_t st);
 Status launch_sigmoid(const float *x, float *y, long long n, cudaStream_t st);
 // ref = sigmoid(delta + inverse_sigmoid(ref))
-Status launch_refine(const float *delta, float *ref, long long n, cudaStream_t st);
+// rows of h [rows][256] -> delta = h w^T + b (w [4][256]); ref [rows][4]
+// refined in place; qp [rows][nqp] = relu(ref wq^T + bq) (wq [nqp][4]) unless
+// qp is null.  h, w, ref and wq 16-byte aligned.
+Status launch_box_refine(const float *h, const float *w, const float *b, float *ref,
+                         const float *wq, const float *bq, float *qp, int rows, int nqp,
+                         cudaStream_t st);
 // y[b][t][:] = x[b][t][:] * v[t]
 Status launch_row_scale(const float *x, const float *v, float *y, long long rows_per_page, int D,
                         int B, cudaStream_t st);

@@ -552,15 +552,54 @@ public:
     // y = act(x W^T + b) (+ res), rows of all pages folded into M
     void lin(const S &x, const S &y, const std::string &name, int act = ACT_NONE,
              const S &res = S(), int max_ctas = 0) {
-        const WT &wt = W(name + ".weight");
-        const WT &bt = W(name + ".bias");
+        lin_cat(x, y, {name}, name, act, res, max_ctas);
+    }
+
+    // Linears of one input as one GEMM: their weights stacked row-wise at
+    // init ([sum of outs][in], biases likewise), their outputs side by side
+    // in y's columns.  Each output element is the same dot product as in
+    // the separate linear.
+    void lin_cat(const S &x, const S &y, const std::vector<std::string> &names,
+                 const std::string &name, int act = ACT_NONE, const S &res = S(),
+                 int max_ctas = 0) {
+        std::vector<const WT *> ws, bs;
+        for (const auto &n : names) {
+            ws.push_back(&W(n + ".weight"));
+            bs.push_back(&W(n + ".bias"));
+        }
         if (!ok) return;
-        const int in = (int)wt.ne[0], out = (int)wt.ne[1];
+        const int in = (int)ws[0]->ne[0];
+        int out = 0;
+        for (size_t i = 0; i < ws.size(); i++) {
+            if ((int)ws[i]->ne[0] != in || bs[i]->ne[0] != ws[i]->ne[1]) {
+                fail("linear " + name + ": stacked weights disagree");
+                return;
+            }
+            out += (int)ws[i]->ne[1];
+        }
         if (in != x.D || out != y.D || x.T != y.T) {
             fail("linear " + name + ": shape mismatch");
             return;
         }
-        const float *wp = wt.p, *bp = bt.p;
+        const float *wp = ws[0]->p, *bp = bs[0]->p;
+        if (ws.size() > 1) {
+            float *wc = dalloc((long long)out * in), *bc = dalloc(out);
+            if (!ok) return;
+            long long r = 0;
+            for (size_t i = 0; i < ws.size(); i++) {
+                const long long o = ws[i]->ne[1];
+                if (cudaMemcpy(wc + r * in, ws[i]->p, sizeof(float) * o * in,
+                               cudaMemcpyDeviceToDevice) != cudaSuccess ||
+                    cudaMemcpy(bc + r, bs[i]->p, sizeof(float) * o, cudaMemcpyDeviceToDevice) !=
+                        cudaSuccess) {
+                    fail("linear " + name + ": weight stacking failed");
+                    return;
+                }
+                r += o;
+            }
+            wp = wc;
+            bp = bc;
+        }
         if (use_tc && in % 4 == 0 && ((uintptr_t)x.p & 15) == 0) {
             const Split wsp = split(wp, (long long)out * in);
             TcEpilogue e;
@@ -626,21 +665,28 @@ public:
     void mha(const S &qk_in, const S &v_in, const S &out, const std::string &pfx,
              const S &v_pre = S()) {
         const int T = qk_in.T;
-        S q = seq(T, kDM), k = seq(T, kDM), o = seq(T, kDM);
+        S qk = seq(T, 2 * kDM), o = seq(T, kDM);  // q in columns 0..255, k in 256..511
         S v = v_pre.p ? v_pre : seq(T, kDM);
-        const int e_in = mark();
-        on_lane(2);
-        after(e_in);
-        if (!v_pre.p) lin(v_in, v, pfx + ".v");
-        lin(qk_in, k, pfx + ".k");
-        const int e_kv = mark();
-        on_lane(0);
-        lin(qk_in, q, pfx + ".q");
+        int e_v = -1;
+        if (!v_pre.p) {
+            const int e_in = mark();
+            on_lane(2);
+            after(e_in);
+            lin(v_in, v, pfx + ".v");
+            e_v = mark();
+            on_lane(0);
+        } else {
+            on_lane(2);
+            e_v = mark();  // v_pre is the latest step of lane 2
+            on_lane(0);
+        }
+        lin_cat(qk_in, qk, {pfx + ".q", pfx + ".k"}, pfx + ".qk");
         // softmax(q k^T / sqrt(32)) v in one launch (scores stay on chip)
-        after(e_kv);
+        after(e_v);
         push(pfx + ".attn", PPDL_STEP_ATTENTION, 4.0 * kNH * T * T * kHD,
              4.0 * 4.0 * T * kDM, [=]() {
-            return launch_attention(q.p, k.p, v.p, o.p, T, kNH, kDM, (long long)T * kDM,
+            return launch_attention(qk.p, qk.p + kDM, v.p, o.p, T, kNH, 2 * kDM,
+                                    (long long)T * 2 * kDM, kDM, (long long)T * kDM,
                                     1.0f / sqrtf((float)kHD), nb, st);
         });
         lin(o, out, pfx + ".o");
@@ -913,8 +959,21 @@ public:
         // (from x, beside the previous layer's box head and this layer's query
         // position MLP), k beside q, and the attention weights beside the
         // sampling offsets
+        // The box head's last linear, the refinement of ref and the next
+        // layer's first query-position linear run as one launch
+        // (launch_box_refine); layer 0's query-position input comes from the
+        // encoder's boxes.
+        const WT &bw0 = W("bbox_head.0.weight"), &bw1 = W("bbox_head.1.weight");
+        const WT &bw2 = W("bbox_head.2.weight"), &bb2 = W("bbox_head.2.bias");
+        const WT &qw0 = W("qpos.0.weight"), &qb0 = W("qpos.0.bias");
+        if (!ok) return;
+        const int nqp = (int)qw0.ne[1];
+        if (bw2.ne[0] != 256 || bw2.ne[1] != 4 || qw0.ne[0] != 4 || bw0.ne[1] != bw1.ne[0])
+            fail("box head / query-position shapes");
         S x = target;
         int e_x = mark();
+        S qp1 = seq(kNQ, nqp);
+        lin(ref, qp1, "qpos.0", ACT_RELU);
         for (int i = 0; i < 6; i++) {
             const std::string dp = "dec" + std::to_string(i);
             const S value = values[i];
@@ -923,27 +982,21 @@ public:
             after(e_x);
             lin(x, v, dp + ".sa.v");
             on_lane(0);
-            S qp1 = seq(kNQ, (int)W("qpos.0.weight").ne[1]), qpos = seq(kNQ, kDM);
-            lin(ref, qp1, "qpos.0", ACT_RELU);
+            S qpos = seq(kNQ, kDM);
             lin(qp1, qpos, "qpos.1");
             S qk2 = seq(kNQ, kDM), sa = seq(kNQ, kDM), x1 = seq(kNQ, kDM);
             add(x, qpos, qk2);
             mha(qk2, x, sa, dp + ".sa", v);
             ln(x, x1, dp + ".ln1", sa);
-            S z = seq(kNQ, kDM), offs = seq(kNQ, 192), aw = seq(kNQ, 96), ca = seq(kNQ, kDM);
+            // sampling offsets (columns 0..191) and attention logits (192..287)
+            S z = seq(kNQ, kDM), sa_lg = seq(kNQ, 288), ca = seq(kNQ, kDM);
             add(x1, qpos, z);
-            const int e_z = mark();
-            on_lane(2);
-            after(e_z);
-            lin(z, aw, dp + ".ca.aw");
-            const int e_aw = mark();
-            on_lane(0);
-            lin(z, offs, dp + ".ca.so");
-            after(e_aw);
+            lin_cat(z, sa_lg, {dp + ".ca.so", dp + ".ca.aw"}, dp + ".ca.so_aw");
             after(e_vp[i]);
             push(dp + ".msda", PPDL_STEP_MSDA, 0.0,
                  4.0 * ((double)kNTok * kDM + kNQ * (192.0 + 96.0 + 4.0 + kDM)), [=]() {
-                return launch_msda(value.p, offs.p, aw.p, ref.p, ca.p, kNQ, nb, false, st);
+                return launch_msda(value.p, sa_lg.p, sa_lg.p + 192, ref.p, ca.p, kNQ, nb, false,
+                                   288, 288, st);
             });
             S cao = seq(kNQ, kDM), x2 = seq(kNQ, kDM);
             lin(ca, cao, dp + ".ca.op");
@@ -957,10 +1010,19 @@ public:
                                         "hidden3", "hidden4", "hidden5"};
             dump_seq(hn[i], x3);
             e_x = mark();
-            S delta = seq(kNQ, 4);
-            mlp3(x3, delta, "bbox_head");
-            push(dp + ".refine", PPDL_STEP_GLUE, 0.0, 12.0 * ref.bs(),
-                 [=]() { return launch_refine(delta.p, ref.p, (long long)nb * ref.bs(), st); });
+            S bh1 = seq(kNQ, (int)bw0.ne[1]), bh2 = seq(kNQ, (int)bw1.ne[1]);
+            lin(x3, bh1, "bbox_head.0", ACT_RELU);
+            lin(bh1, bh2, "bbox_head.1", ACT_RELU);
+            const S qpn = i < 5 ? seq(kNQ, nqp) : S();
+            {
+                const float *w2 = bw2.p, *b2 = bb2.p, *wq = qw0.p, *bq = qb0.p;
+                push(dp + ".box_refine", PPDL_STEP_GLUE, 2.0 * kNQ * (4 * 256 + 4.0 * nqp),
+                     4.0 * kNQ * (256 + 8 + (qpn.p ? nqp : 0)), [=]() {
+                    return launch_box_refine(bh2.p, w2, b2, ref.p, wq, bq, qpn.p, nb * kNQ, nqp,
+                                             st);
+                });
+            }
+            qp1 = qpn;
             x = x3;
         }
 

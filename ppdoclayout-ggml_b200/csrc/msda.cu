@@ -41,11 +41,11 @@ __constant__ int c_lvl_start[3] = {0, 10000, 12500};
 template <bool kCanon>
 __global__ void __launch_bounds__(kThreads)
 msda_kernel(const float *__restrict__ val,  // [B][13125][256]
-            const float *__restrict__ p1,   // offsets or locations [B*nq][192]
-            const float *__restrict__ p2,   // logits or weights    [B*nq][96]
+            const float *__restrict__ p1,   // offsets or locations [B*nq][ld1], 192 used
+            const float *__restrict__ p2,   // logits or weights    [B*nq][ld2], 96 used
             const float *__restrict__ ref,  // [B*nq][4] (in-model only)
             float *__restrict__ out,        // [B*nq][256]
-            int nq, int npairs) {
+            int nq, int npairs, int ld1, int ld2) {
     __shared__ float s_w[kPairs][12];
     __shared__ int s_idx[kPairs][kTapStride];
     __shared__ float s_tw[kPairs][kTapStride];
@@ -58,7 +58,7 @@ msda_kernel(const float *__restrict__ val,  // [B][13125][256]
         const int gp = pair0 + t;
         if (gp < npairs) {
             const int bq = gp >> 3, h = gp & 7;
-            const float *a = p2 + (size_t)bq * 96 + h * 12;
+            const float *a = p2 + (size_t)bq * ld2 + h * 12;
             if (kCanon) {
 #pragma unroll
                 for (int i = 0; i < 12; i++) s_w[t][i] = a[i];
@@ -87,8 +87,8 @@ msda_kernel(const float *__restrict__ val,  // [B][13125][256]
         if (gp >= npairs) continue;
         const int bq = gp >> 3, h = gp & 7;
         const int l = pt >> 2, p = pt & 3;
-        const float ox = p1[(size_t)bq * 192 + ((h * 3 + l) * 4 + p) * 2 + 0];
-        const float oy = p1[(size_t)bq * 192 + ((h * 3 + l) * 4 + p) * 2 + 1];
+        const float ox = p1[(size_t)bq * ld1 + ((h * 3 + l) * 4 + p) * 2 + 0];
+        const float oy = p1[(size_t)bq * ld1 + ((h * 3 + l) * 4 + p) * 2 + 1];
         float lx, ly;
         if (kCanon) {
             lx = ox;
@@ -151,15 +151,18 @@ msda_kernel(const float *__restrict__ val,  // [B][13125][256]
 }  // namespace
 
 Status launch_msda(const float *val, const float *p1, const float *p2, const float *ref,
-                   float *out, int nq, int batch, bool canon, cudaStream_t stream) {
-    if (nq <= 0 || batch <= 0) return ERR_SHAPE;
+                   float *out, int nq, int batch, bool canon, int ld1, int ld2,
+                   cudaStream_t stream) {
+    if (nq <= 0 || batch <= 0 || ld1 < 192 || ld2 < 96) return ERR_SHAPE;
     if (((uintptr_t)val | (uintptr_t)out) & 15) return ERR_SHAPE;
     const int npairs = batch * nq * kNH;
     const int grid = cdiv(npairs, kPairs);
     if (canon)
-        msda_kernel<true><<<grid, kThreads, 0, stream>>>(val, p1, p2, ref, out, nq, npairs);
+        msda_kernel<true><<<grid, kThreads, 0, stream>>>(val, p1, p2, ref, out, nq, npairs, ld1,
+                                                         ld2);
     else
-        msda_kernel<false><<<grid, kThreads, 0, stream>>>(val, p1, p2, ref, out, nq, npairs);
+        msda_kernel<false><<<grid, kThreads, 0, stream>>>(val, p1, p2, ref, out, nq, npairs, ld1,
+                                                          ld2);
     return cuda_status();
 }
 

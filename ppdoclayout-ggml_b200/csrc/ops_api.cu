@@ -168,7 +168,8 @@ PPDL_OPS_API int ppdl_op_launch(const ppdl_op_desc *d, void *stream_ptr) {
             return to_status(ppdl::launch_msda((const float *)s0.data, (const float *)d->src[1].data,
                                                (const float *)d->src[2].data,
                                                canon ? nullptr : (const float *)d->src[3].data,
-                                               (float *)dst.data, (int)nq, (int)B, canon, st));
+                                               (float *)dst.data, (int)nq, (int)B, canon, 192,
+                                               96, st));
         }
         case PPDL_OP_BIASACT: {
             // patch:719-728: dst = act(src0 + bias[plane]), plane = ne0*ne1
