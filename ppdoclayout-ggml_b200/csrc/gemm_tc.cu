@@ -703,6 +703,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int c_lo = warp >= kWarpEpi2 ? half : 0;
         const int c_hi = warp >= kWarpEpi2 ? pbn : half;
         const int ew = warp < 4 ? warp : warp - 4;  // epilogue warp 0..7
+        // ReLU / SiLU outputs apply alpha, bias and a mode-1 residual in
+        // registers before the box (measured faster there); the identity and
+        // GELU forms keep the all-in-the-box loop (the other form spills them)
+        constexpr bool kPreOps = ACT == ACT_RELU || ACT == ACT_SILU;
         const uint32_t staging = stage0 + (uint32_t)S * a.stage_bytes;
         float *staging_ptr = reinterpret_cast<float *>(stage0_ptr + (size_t)S * a.stage_bytes);
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
@@ -720,6 +724,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int m = m0 + quad * 32 + lane;
             float *C = e.C + (long long)z * e.c_bs;
             const float *R = e.res_mode ? e.res + (long long)z * e.res_bs : nullptr;
+            // (ReLU / SiLU outputs) the bias of the warp's columns c_lo + lane
+            // and c_lo + 32 + lane, loaded while the k-blocks are folded and
+            // handed to the store phase by warp shuffles
+            float bias_lo = 0.0f, bias_hi = 0.0f;
+            if (kPreOps && e.bias) {
+                const int n_lo = n0 + c_lo + lane, n_hi = n_lo + 32;
+                if (c_lo + lane < c_hi && n_lo < pN) bias_lo = __ldg(e.bias + n_lo);
+                if (c_lo + 32 + lane < c_hi && n_hi < pN) bias_hi = __ldg(e.bias + n_hi);
+            }
+            // bias of column c (c_lo <= c < c_hi, warp-uniform half c - c_lo >= 32
+            // or per-lane offsets below 32 within one half)
+            auto bias_of = [&](int c) {
+                const int o = c - c_lo;
+                return __shfl_sync(0xffffffffu, o >= 32 ? bias_hi : bias_lo, o & 31);
+            };
             for (int c = 0; c < kblocks; c++, ctr++, rp.next(), re.next()) {
                 const int p = rp.i;
                 if (!mbar_wait(bar_empty + 8 * re.i, re.ph, abort_flag)) {
@@ -763,35 +782,69 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         __syncwarp();
                     }
                     float *box = staging_ptr + (size_t)(ew * 2 + b) * (kBoxBytes / 4);
-                    // raw values first (16 stores), then alpha / bias / residual
-                    // / activation in a rolled loop over the box: a small loop
-                    // body, executed once per tile, keeps instruction fetch short
+                    if constexpr (kPreOps) {
+                        // op order per element: alpha, + bias, + residual (mode
+                        // 1), activation, + residual (mode 2).  The chunk's 16
+                        // residual loads are issued together up front; alpha,
+                        // bias and a mode-1 residual are applied in registers on
+                        // the way into the box, the activation in a rolled loop
+                        // over the box, a mode-2 residual in a last pass.
+                        float rres[16];
+                        if (e.res_mode) {
 #pragma unroll
-                    for (int j = 0; j < 16; j++) box[j * 32 + lane] = v[j];
-                    if (ops) {
-                        // four columns at a time: their bias and residual loads
-                        // are issued together, the op order per element is
-                        // alpha, + bias, + residual (mode 1), act, + residual (2)
-#pragma unroll 1
-                        for (int j0 = 0; j0 < 16; j0 += 4) {
-                            float bb[4], rr[4];
-#pragma unroll
-                            for (int u = 0; u < 4; u++) {
-                                const int n = n0 + c0 + j0 + u;
-                                const bool ok_n = n < pN;
-                                bb[u] = (e.bias && ok_n) ? __ldg(e.bias + n) : 0.0f;
-                                rr[u] = (e.res_mode && ok_n && row_ok)
-                                            ? Rrow[(long long)n * e.res_ldn] : 0.0f;
+                            for (int j = 0; j < 16; j++) {
+                                const int n = n0 + c0 + j;
+                                rres[j] =
+                                    (n < pN && row_ok) ? Rrow[(long long)n * e.res_ldn] : 0.0f;
                             }
+                        }
 #pragma unroll
-                            for (int u = 0; u < 4; u++) {
-                                float x = box[(j0 + u) * 32 + lane];
-                                if (e.alpha != 1.0f) x = x * e.alpha;
-                                if (e.bias) x = x + bb[u];
-                                if (e.res_mode == 1) x = x + rr[u];
-                                x = act_apply(x, ACT);
-                                if (e.res_mode == 2) x = x + rr[u];
-                                box[(j0 + u) * 32 + lane] = x;
+                        for (int j = 0; j < 16; j++) {
+                            float x = v[j];
+                            if (e.alpha != 1.0f) x = x * e.alpha;
+                            if (e.bias) x = x + bias_of(c0 + j);
+                            if (e.res_mode == 1) x = x + rres[j];
+                            box[j * 32 + lane] = x;
+                        }
+#pragma unroll 1
+                        for (int j = 0; j < 16; j++)
+                            box[j * 32 + lane] = act_apply(box[j * 32 + lane], ACT);
+                        if (e.res_mode == 2) {
+#pragma unroll
+                            for (int j = 0; j < 16; j++) box[j * 32 + lane] += rres[j];
+                        }
+                    } else {
+                        // raw values first (16 stores), then alpha / bias /
+                        // residual / activation in a rolled loop over the box: a
+                        // small loop body, once per tile, keeps instruction
+                        // fetch short (and the registers of the identity and
+                        // GELU forms below their limit)
+#pragma unroll
+                        for (int j = 0; j < 16; j++) box[j * 32 + lane] = v[j];
+                        if (ops) {
+                            // four columns at a time: their bias and residual
+                            // loads are issued together
+#pragma unroll 1
+                            for (int j0 = 0; j0 < 16; j0 += 4) {
+                                float bb[4], rr[4];
+#pragma unroll
+                                for (int u = 0; u < 4; u++) {
+                                    const int n = n0 + c0 + j0 + u;
+                                    const bool ok_n = n < pN;
+                                    bb[u] = (e.bias && ok_n) ? __ldg(e.bias + n) : 0.0f;
+                                    rr[u] = (e.res_mode && ok_n && row_ok)
+                                                ? Rrow[(long long)n * e.res_ldn] : 0.0f;
+                                }
+#pragma unroll
+                                for (int u = 0; u < 4; u++) {
+                                    float x = box[(j0 + u) * 32 + lane];
+                                    if (e.alpha != 1.0f) x = x * e.alpha;
+                                    if (e.bias) x = x + bb[u];
+                                    if (e.res_mode == 1) x = x + rr[u];
+                                    x = act_apply(x, ACT);
+                                    if (e.res_mode == 2) x = x + rr[u];
+                                    box[(j0 + u) * 32 + lane] = x;
+                                }
                             }
                         }
                     }
@@ -836,7 +889,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                 const int n = n0 + c0 + (idx & 15);
                                 const int mr = m0 + quad * 32 + (idx >> 4);
                                 const bool okk = n < pN && mr < pM;
-                                bb[u] = (e.bias && okk) ? __ldg(e.bias + n) : 0.0f;
+                                if constexpr (kPreOps)
+                                    bb[u] = bias_of(c0 + (idx & 15));
+                                else
+                                    bb[u] = (e.bias && okk) ? __ldg(e.bias + n) : 0.0f;
                                 rr[u] = (e.res_mode && okk)
                                             ? R[(long long)mr * e.res_ldm + (long long)n * e.res_ldn]
                                             : 0.0f;
@@ -865,20 +921,23 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     nbox++;
                     return;
                 }
-                if (!row_ok) return;
                 // any other layout (strides that TMA cannot take): the raw
                 // values go through the thread's own column of a box, then a
                 // rolled loop applies the ops and stores with the output strides
+                // (all lanes run it when the bias comes by warp shuffle)
+                if (!kPreOps && !row_ok) return;
                 float *box = staging_ptr + (size_t)(ew * 2) * (kBoxBytes / 4);
 #pragma unroll
                 for (int j = 0; j < 16; j++) box[j * 32 + lane] = v[j];
 #pragma unroll 1
                 for (int j = 0; j < 16; j++) {
                     const int n = n0 + c0 + j;
-                    if (n < pN) {
+                    float bj = 0.0f;
+                    if constexpr (kPreOps) bj = bias_of(c0 + j);
+                    if (n < pN && row_ok) {
                         float x = box[j * 32 + lane];
                         if (e.alpha != 1.0f) x = x * e.alpha;
-                        if (e.bias) x = x + __ldg(e.bias + n);
+                        if (e.bias) x = x + (kPreOps ? bj : __ldg(e.bias + n));
                         if (e.res_mode == 1) x = x + Rrow[(long long)n * e.res_ldn];
                         x = act_apply(x, ACT);
                         if (e.res_mode == 2) x = x + Rrow[(long long)n * e.res_ldn];
