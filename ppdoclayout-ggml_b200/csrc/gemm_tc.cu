@@ -703,10 +703,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int c_lo = warp >= kWarpEpi2 ? half : 0;
         const int c_hi = warp >= kWarpEpi2 ? pbn : half;
         const int ew = warp < 4 ? warp : warp - 4;  // epilogue warp 0..7
-        // ReLU / SiLU outputs apply alpha, bias and a mode-1 residual in
-        // registers before the box (measured faster there); the identity and
-        // GELU forms keep the all-in-the-box loop (the other form spills them)
-        constexpr bool kPreOps = ACT == ACT_RELU || ACT == ACT_SILU;
+        // ReLU / SiLU / identity outputs apply alpha, bias and a mode-1
+        // residual in registers before the box (measured faster); the GELU
+        // form keeps the all-in-the-box loop
+        constexpr bool kPreOps = ACT != ACT_GELU;
         const uint32_t staging = stage0 + (uint32_t)S * a.stage_bytes;
         float *staging_ptr = reinterpret_cast<float *>(stage0_ptr + (size_t)S * a.stage_bytes);
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
@@ -790,7 +790,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         // the way into the box, the activation in a rolled loop
                         // over the box, a mode-2 residual in a last pass.
                         float rres[16];
-                        if (e.res_mode) {
+                        if (e.res_mode && ACT != ACT_NONE) {
 #pragma unroll
                             for (int j = 0; j < 16; j++) {
                                 const int n = n0 + c0 + j;
@@ -798,18 +798,37 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                     (n < pN && row_ok) ? Rrow[(long long)n * e.res_ldn] : 0.0f;
                             }
                         }
+                        if constexpr (ACT == ACT_NONE) {
+                            // identity: both residual modes add after the bias
 #pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            float x = v[j];
-                            if (e.alpha != 1.0f) x = x * e.alpha;
-                            if (e.bias) x = x + bias_of(c0 + j);
-                            if (e.res_mode == 1) x = x + rres[j];
-                            box[j * 32 + lane] = x;
-                        }
+                            for (int j = 0; j < 16; j++) {
+                                float x = v[j];
+                                if (e.alpha != 1.0f) x = x * e.alpha;
+                                if (e.bias) x = x + bias_of(c0 + j);
+                                box[j * 32 + lane] = x;
+                            }
+                            if (e.res_mode) {
+#pragma unroll 4
+                                for (int j = 0; j < 16; j++) {
+                                    const int n = n0 + c0 + j;
+                                    if (n < pN && row_ok)
+                                        box[j * 32 + lane] += Rrow[(long long)n * e.res_ldn];
+                                }
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; j++) {
+                                float x = v[j];
+                                if (e.alpha != 1.0f) x = x * e.alpha;
+                                if (e.bias) x = x + bias_of(c0 + j);
+                                if (e.res_mode == 1) x = x + rres[j];
+                                box[j * 32 + lane] = x;
+                            }
 #pragma unroll 1
-                        for (int j = 0; j < 16; j++)
-                            box[j * 32 + lane] = act_apply(box[j * 32 + lane], ACT);
-                        if (e.res_mode == 2) {
+                            for (int j = 0; j < 16; j++)
+                                box[j * 32 + lane] = act_apply(box[j * 32 + lane], ACT);
+                        }
+                        if (ACT != ACT_NONE && e.res_mode == 2) {
 #pragma unroll
                             for (int j = 0; j < 16; j++) box[j * 32 + lane] += rres[j];
                         }
