@@ -28,10 +28,12 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// one warp per 256-wide row; y = LN(x (+ r)) * g + b
+// one warp per 256-wide row; y = LN(x (+ r)) * g + b, and y2 = y + q when q
+// is given (the decoder's x1 and x1 + query_pos in one pass)
 __global__ void layernorm256_kernel(const float *__restrict__ x, const float *__restrict__ r,
                                     const float *__restrict__ g, const float *__restrict__ bta,
-                                    float *__restrict__ y, long long rows) {
+                                    float *__restrict__ y, const float *__restrict__ q,
+                                    float *__restrict__ y2, long long rows) {
     const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
     const int lane = threadIdx.x & 31;
@@ -70,6 +72,12 @@ __global__ void layernorm256_kernel(const float *__restrict__ x, const float *__
         o.x = v[k].x * sc * gg.x + bb.x; o.y = v[k].y * sc * gg.y + bb.y;
         o.z = v[k].z * sc * gg.z + bb.z; o.w = v[k].w * sc * gg.w + bb.w;
         yp[lane + 32 * k] = o;
+        if (q) {
+            const float4 qq = reinterpret_cast<const float4 *>(q + row * 256)[lane + 32 * k];
+            reinterpret_cast<float4 *>(y2 + row * 256)[lane + 32 * k] =
+                make_float4(__fadd_rn(o.x, qq.x), __fadd_rn(o.y, qq.y), __fadd_rn(o.z, qq.z),
+                            __fadd_rn(o.w, qq.w));
+        }
     }
 }
 
@@ -273,8 +281,15 @@ __global__ void pp_masks_kernel(const float *__restrict__ ml, const int32_t *__r
 
 Status launch_layernorm256(const float *x, const float *r, const float *g, const float *b,
                            float *y, long long rows, cudaStream_t st) {
+    return launch_layernorm256_add(x, r, g, b, y, nullptr, nullptr, rows, st);
+}
+
+Status launch_layernorm256_add(const float *x, const float *r, const float *g, const float *b,
+                               float *y, const float *q, float *y2, long long rows,
+                               cudaStream_t st) {
     if (rows <= 0) return rows == 0 ? OK : ERR_SHAPE;
-    layernorm256_kernel<<<blocks(rows * 32), 256, 0, st>>>(x, r, g, b, y, rows);
+    if (q && !y2) return ERR_SHAPE;
+    layernorm256_kernel<<<blocks(rows * 32), 256, 0, st>>>(x, r, g, b, y, q, y2, rows);
     return cuda_status();
 }
 

@@ -10,6 +10,10 @@ namespace ppdl {
 // y = LayerNorm(x (+ r)) * g + b over rows of 256 (eps 1e-5)
 Status launch_layernorm256(const float *x, const float *r, const float *g, const float *b,
                            float *y, long long rows, cudaStream_t st);
+// the same, also writing y2 = y + q (rows of 256)
+Status launch_layernorm256_add(const float *x, const float *r, const float *g, const float *b,
+                               float *y, const float *q, float *y2, long long rows,
+                               cudaStream_t st);
 // softmax over rows of length L, in place
 Status launch_softmax_rows(float *x, long long rows, int L, cudaStream_t st);
 

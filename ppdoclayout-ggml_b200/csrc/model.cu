@@ -101,7 +101,7 @@ struct Step {
 
 constexpr int kLanes = 3;
 #ifndef PPDL_VP_CTAS
-#define PPDL_VP_CTAS 64
+#define PPDL_VP_CTAS 120
 #endif
 constexpr int kVpCtas = PPDL_VP_CTAS;  // SMs a value projection may hold (of 148)
 
@@ -635,13 +635,17 @@ public:
         });
     }
 
-    void ln(const S &x, const S &y, const std::string &name, const S &r = S()) {
+    // y = LN(x (+ r)); with q given also y2 = y + q in the same pass
+    void ln(const S &x, const S &y, const std::string &name, const S &r = S(), const S &q = S(),
+            const S &y2 = S()) {
         const WT &g = W(name + ".weight");
         const WT &b = W(name + ".bias");
         if (!ok) return;
         const float *gp = g.p, *bp = b.p;
-        push(name, PPDL_STEP_GLUE, 0.0, 4.0 * x.T * kDM * (r.p ? 3 : 2), [=]() {
-            return launch_layernorm256(x.p, r.p, gp, bp, y.p, (long long)nb * x.T, st);
+        push(name, PPDL_STEP_GLUE, 0.0, 4.0 * x.T * kDM * (2 + (r.p ? 1 : 0) + (q.p ? 2 : 0)),
+             [=]() {
+            return launch_layernorm256_add(x.p, r.p, gp, bp, y.p, q.p, y2.p, (long long)nb * x.T,
+                                           st);
         });
     }
 
@@ -987,10 +991,9 @@ public:
             S qk2 = seq(kNQ, kDM), sa = seq(kNQ, kDM), x1 = seq(kNQ, kDM);
             add(x, qpos, qk2);
             mha(qk2, x, sa, dp + ".sa", v);
-            ln(x, x1, dp + ".ln1", sa);
             // sampling offsets (columns 0..191) and attention logits (192..287)
             S z = seq(kNQ, kDM), sa_lg = seq(kNQ, 288), ca = seq(kNQ, kDM);
-            add(x1, qpos, z);
+            ln(x, x1, dp + ".ln1", sa, qpos, z);  // x1 and z = x1 + qpos
             lin_cat(z, sa_lg, {dp + ".ca.so", dp + ".ca.aw"}, dp + ".ca.so_aw");
             after(e_vp[i]);
             push(dp + ".msda", PPDL_STEP_MSDA, 0.0,
