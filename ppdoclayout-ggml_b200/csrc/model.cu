@@ -131,8 +131,11 @@ public:
     std::vector<Dump> dump_list;
 
     // Winograd / attention scratch (sized while the plan is built)
-    float *wg_dt = nullptr, *wg_yt = nullptr;
-    long long wg_dt_n = 0, wg_yt_n = 0;
+    // Two scratch sets: set 1 serves the mask-feature head, which runs on a
+    // side lane at the same time as set 0's users on lane 0.
+    float *wg_dt_s[2] = {}, *wg_yt_s[2] = {};
+    long long wg_dt_ns[2] = {}, wg_yt_ns[2] = {};
+    int scratch = 0;  // set used by the convs planned next
 
     // graph inputs / outputs
     V img;
@@ -189,16 +192,17 @@ public:
             fail("weight split failed");
             return nullptr;
         }
-        wg_dt_n = std::max(wg_dt_n, (long long)Kp * Mp * Bmax);
+        const int ss = scratch;
+        wg_dt_ns[ss] = std::max(wg_dt_ns[ss], (long long)Kp * Mp * Bmax);
         auto g = std::make_shared<TcGemm>();
         finalizers.push_back([=]() {
-            if (!tc_gemm_plan(g.get(), M, OC, Kp, Bmax, wg_dt, 1, Mp, (long long)Kp * Mp, hi, lo,
-                              1, e))
+            if (!tc_gemm_plan(g.get(), M, OC, Kp, Bmax, wg_dt_s[ss], 1, Mp, (long long)Kp * Mp,
+                              hi, lo, 1, e))
                 g->ok = false;
         });
         push(name + ".im2col", PPDL_STEP_IM2COL, 0.0,
              4.0 * ((double)x.C * x.plane() + (double)Kp * Mp), [=]() {
-            return launch_im2col(x.p, x.bs, x.plane(), wg_dt, (long long)Kp * Mp, Kc, Kp, x.H,
+            return launch_im2col(x.p, x.bs, x.plane(), wg_dt_s[ss], (long long)Kp * Mp, Kc, Kp, x.H,
                                  x.W, K, s, p, OW, M, (int)Mp, nb, st);
         });
         return g;
@@ -437,11 +441,12 @@ public:
                 fail("filter transform launch failed");
                 return;
             }
-            wg_dt_n = std::max(wg_dt_n, 36LL * IC * Tp * Bmax);
-            wg_yt_n = std::max(wg_yt_n, 36LL * OC * Tp * Bmax);
+            const int ss = scratch;
+            wg_dt_ns[ss] = std::max(wg_dt_ns[ss], 36LL * IC * Tp * Bmax);
+            wg_yt_ns[ss] = std::max(wg_yt_ns[ss], 36LL * OC * Tp * Bmax);
             push(name + ".wg_in", PPDL_STEP_WG_INPUT, 0.0,
                  4.0 * ((double)IC * x.plane() + 36.0 * IC * T), [=]() {
-                return launch_wg4_input(x.p, x.bs, wg_dt, IC, x.H, x.W, TW, TH, 1, nb, st, Tp);
+                return launch_wg4_input(x.p, x.bs, wg_dt_s[ss], IC, x.H, x.W, TW, TH, 1, nb, st, Tp);
             });
             std::shared_ptr<TcGemm> g;
             if (use_tc && IC % 4 == 0) {
@@ -453,8 +458,8 @@ public:
                 g = std::make_shared<TcGemm>();
                 finalizers.push_back([=]() {
                     TcEpilogue e;
-                    e.C = wg_yt; e.ldc_m = 1; e.ldc_n = Tp; e.c_bs = (long long)OC * Tp;
-                    if (!tc_gemm_plan(g.get(), T, OC, IC, Bmax * 36, wg_dt, 1, Tp,
+                    e.C = wg_yt_s[ss]; e.ldc_m = 1; e.ldc_n = Tp; e.c_bs = (long long)OC * Tp;
+                    if (!tc_gemm_plan(g.get(), T, OC, IC, Bmax * 36, wg_dt_s[ss], 1, Tp,
                                       (long long)IC * Tp, bhi, blo, 36, e))
                         g->ok = false;
                 });
@@ -465,13 +470,13 @@ public:
                 GemmArgs q;
                 q.M = OC; q.N = T; q.K = IC; q.batch = nb * 36;
                 q.A = {wg4, 1, OC, 36, 0, (long long)IC * OC};
-                q.B = {wg_dt, Tp, 1, 1, (long long)IC * Tp, 0};
-                q.C = wg_yt; q.ldc_m = Tp; q.ldc_n = 1; q.c_bs_hi = (long long)OC * Tp;
+                q.B = {wg_dt_s[ss], Tp, 1, 1, (long long)IC * Tp, 0};
+                q.C = wg_yt_s[ss]; q.ldc_m = Tp; q.ldc_n = 1; q.c_bs_hi = (long long)OC * Tp;
                 return launch_gemm_simt(q, st);
             });
             push(name + ".wg_out", PPDL_STEP_WG_OUTPUT, 0.0,
                  4.0 * (36.0 * OC * T + (double)OC * OH * OW * (res_mode ? 2 : 1)), [=]() {
-                return launch_wg4_output(wg_yt, bp, y.p, y.bs, res.p, res.bs, res_mode, OC, OH, OW,
+                return launch_wg4_output(wg_yt_s[ss], bp, y.p, y.bs, res.p, res.bs, res_mode, OC, OH, OW,
                                          TW, TH, act, nb, st, Tp);
             });
             return;
@@ -838,22 +843,33 @@ public:
         V f8 = tensor(256, 100, 100);
         csp(fcat1, f8, "fpn1");
         dump_chw("f8", f8);
+        const int e_f8 = mark();
         // PAN (bottom-up)
         conv(f8, pcat0.slice(0, 256), "pand0", 2, 1, ACT_SILU);
         V n16 = tensor(256, 50, 50);
         csp(pcat0, n16, "pan0");
         dump_chw("n16", n16);
+        const int e_n16 = mark();
         conv(n16, pcat1.slice(0, 256), "pand1", 2, 1, ACT_SILU);
         V n32 = tensor(256, 25, 25);
         csp(pcat1, n32, "pan1");
         dump_chw("n32", n32);
-        // mask feature head
+        // mask feature head, on lane 2 with its own scratch set: each level
+        // starts once its feature exists (f8 after the FPN, n16 and n32 along
+        // the PAN), overlapping the PAN, the decoder input, the encoder head
+        // and the top-300 selection until the encoder's mask GEMM needs it
+        const int e_n32 = mark();
+        on_lane(2);
+        after(e_f8);
+        scratch = 1;
         V hs = tensor(64, 100, 100);
         conv(f8, hs, "mh0.0", 1, 1, ACT_SILU);
         V h1 = tensor(64, 50, 50);
+        after(e_n16);
         conv(n16, h1, "mh1.0", 1, 1, ACT_SILU);
         interp(h1, hs, true, hs);  // h0 + up(h1)
         V h2 = tensor(64, 25, 25), h2i = tensor(64, 50, 50), h2b = tensor(64, 50, 50);
+        after(e_n32);
         conv(n32, h2, "mh2.0", 1, 1, ACT_SILU);
         interp(h2, h2i, true);
         conv(h2i, h2b, "mh2.2", 1, 1, ACT_SILU);
@@ -866,6 +882,9 @@ public:
         conv(ml, mb, "mout.base", 1, 1, ACT_SILU);
         conv(mb, mfeat, "mout.conv", 1, 0, ACT_NONE);
         dump_chw("mask_feat", mfeat);
+        scratch = 0;
+        const int e_mf = mark();
+        on_lane(0);
 
         // ---- decoder input, two-stage selection (:781-821)
         S source = seq(kNTok, kDM);
@@ -947,6 +966,7 @@ public:
                 return launch_gemm_simt(g, st);
             });
         };
+        after(e_mf);
         mask_gemm(mq0, encm);
         if (dumps)
             dump_list.push_back({"enc_masks", encm, {kMaskPix, kNQ, 1, 1}, "f32",
@@ -1080,8 +1100,10 @@ public:
             });
         }
         if (!ok) return;
-        wg_dt = dalloc(wg_dt_n);
-        wg_yt = dalloc(wg_yt_n);
+        for (int k = 0; k < 2; k++) {
+            wg_dt_s[k] = dalloc(wg_dt_ns[k]);
+            wg_yt_s[k] = dalloc(wg_yt_ns[k]);
+        }
         if (!ok) return;
         for (auto &f : finalizers) f();
     }
