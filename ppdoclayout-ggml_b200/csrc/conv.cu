@@ -305,10 +305,10 @@ dwconv_plane_kernel(const float *__restrict__ x, long long xbs, const float *__r
     constexpr int NV = 3 * S + K;
     const int c = blockIdx.x, b = blockIdx.y;
     const float *xp = x + (long long)b * xbs + (long long)c * H * W;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     const int HP = H + 2 * P, WP = W + 2 * P;
     const uint32_t plane_s = (uint32_t)__cvta_generic_to_shared(plane);
-    for (int r = warp; r < HP; r += 8) {
+    for (int r = warp; r < HP; r += nwarps) {
         const int iy = r - P;
         const bool row_in = (unsigned)iy < (unsigned)H;
         const float *xr = xp + (long long)iy * W;
@@ -327,7 +327,7 @@ dwconv_plane_kernel(const float *__restrict__ x, long long xbs, const float *__r
     __syncthreads();
     const int ng = (OW + 3) >> 2;  // 4-output groups per row
     float *yp = y + (long long)b * ybs + (long long)c * OH * OW;
-    for (int item = threadIdx.x; item < OH * ng; item += 256) {
+    for (int item = threadIdx.x; item < OH * ng; item += blockDim.x) {
         const int oy = item / ng, g = item - oy * ng;
         const int ox0 = 4 * g;
         float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -576,6 +576,12 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
     if (plane_bytes <= kDwPlaneSmemMax) {
         const dim3 g(C, B);
         const int sm = (int)plane_bytes;
+        // threads: the 4-output items of the plane spread over as few passes
+        // of at most 256 threads as possible, in whole warps (a 25 x 25 plane:
+        // 175 items, 192 threads), so small planes keep more blocks resident
+        const int items = OH * ((OW + 3) / 4);
+        const int passes = (items + 255) / 256;
+        const int nthr = ((items + passes - 1) / passes + 31) / 32 * 32;
         int dev = 0;
         cudaGetDevice(&dev);
 #define PPDL_DW_PLANE(KK, SS)                                                                     \
@@ -588,7 +594,7 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
                 return ERR_CUDA;                                                                 \
             if (dev < 64) attr[dev] = true;                                                      \
         }                                                                                        \
-        dwconv_plane_kernel<KK, SS><<<g, 256, sm, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW,   \
+        dwconv_plane_kernel<KK, SS><<<g, nthr, sm, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW,  \
                                                         P, act, ld);                             \
     } while (0)
         if (K == 3 && S == 1)
