@@ -140,3 +140,30 @@ def test_bad_arguments(cuda, gguf_path):
     ctx.close()
     assert L.ppdl_init(b"/nonexistent/model.gguf", 1) is None
     assert L.ppdl_init(gguf_path.encode(), 0) is None  # no CPU backend in this build
+
+
+def test_zero_copy_views_and_profiles(cuda, gguf_path, pages, gpu_out):
+    """infer_batch(copy=False) returns views of the context's pinned result
+    buffers with the same values as the copies; the per-step profile and the
+    lane timeline cover the same steps, every lane's steps end in stream
+    order, and the side lanes (value projections; k/v, mask-feature head,
+    reading-order head) are used."""
+    import torch
+    ctx = ppdl.Context(gguf_path, max_batch=2)
+    imgs = torch.from_numpy(np.stack([p[0] for p in pages])).pin_memory().numpy()
+    hw = np.array([p[1] for p in pages], np.int32)
+    views = ctx.infer_batch(imgs, hw, copy=False)
+    for (d, m), (bd, bm) in zip(views, gpu_out[0]):
+        np.testing.assert_array_equal(d, bd)
+        np.testing.assert_array_equal(m, bm)
+    steps = ctx.profile_steps(2)
+    tl = ctx.profile_timeline(2)
+    ctx.close()
+    assert len(tl) == len(steps) > 300
+    assert {lane for _, lane in tl} == {0, 1, 2}
+    assert all(np.isfinite(e) and e > 0 for e, _ in tl)
+    assert all(s[2] > 0 for s in steps)
+    last = {}
+    for e, lane in tl:
+        assert e >= last.get(lane, 0.0)
+        last[lane] = e
