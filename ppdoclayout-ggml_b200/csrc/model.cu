@@ -668,9 +668,9 @@ public:
     }
 
     // MHA, 8 heads x 32, q/k from qk_in, v from v_in (src/ppdoclayout.cpp:572-587).
-    // Called on lane 0 with qk_in and v_in written there; k and v are
-    // projected on lane 2 beside q.  A caller that projected v earlier (on
-    // lane 2) passes it as v_pre.
+    // Called on lane 0 with qk_in and v_in written there; q and k are one
+    // GEMM of stacked weights on lane 0, v is projected on lane 2 beside it.
+    // A caller that projected v earlier (on lane 2) passes it as v_pre.
     void mha(const S &qk_in, const S &v_in, const S &out, const std::string &pfx,
              const S &v_pre = S()) {
         const int T = qk_in.T;
@@ -979,10 +979,9 @@ public:
              [=]() { return launch_sigmoid(refu.p, ref.p, (long long)nb * refu.bs(), st); });
 
         // ---- decoder layers (:824-851)
-        // lane 2 takes the projections off the chain: v of the self-attention
-        // (from x, beside the previous layer's box head and this layer's query
-        // position MLP), k beside q, and the attention weights beside the
-        // sampling offsets
+        // lane 2 takes the self-attention's v projection off the chain (from
+        // x, beside the previous layer's box head and this layer's query
+        // position MLP)
         // The box head's last linear, the refinement of ref and the next
         // layer's first query-position linear run as one launch
         // (launch_box_refine); layer 0's query-position input comes from the
