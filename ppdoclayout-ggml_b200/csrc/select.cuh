@@ -7,8 +7,10 @@
 // A radix select finds the nq-th largest key: eight passes over the keys,
 // each building a 256-bin histogram of the next byte among the keys that
 // match the prefix found so far (lanes of a warp with the same bin add once),
-// and one scan of the bins from the top.  The nq keys >= it are compacted
-// and bitonic-sorted descending in a 512-entry buffer.
+// and one scan of the bins from the top; the passes stop early once every
+// key of the chosen bin is needed (the threshold is then the bin's lowest
+// possible key).  The nq keys >= it are compacted and bitonic-sorted
+// descending in a 512-entry buffer.
 #pragma once
 
 #include <cstdint>
@@ -36,13 +38,14 @@ __device__ __forceinline__ void block_select_top(const unsigned long long *keys,
                                                  unsigned long long *sel) {
     __shared__ unsigned s_hist[256];
     __shared__ unsigned long long s_prefix, s_mask;
-    __shared__ unsigned s_need, s_cnt;
+    __shared__ unsigned s_need, s_cnt, s_done;
     const int nt = blockDim.x, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         s_prefix = 0ull;
         s_mask = 0ull;
         s_need = (unsigned)nq;
         s_cnt = 0;
+        s_done = 0;
     }
     for (int shift = 56; shift >= 0; shift -= 8) {
         for (int b = threadIdx.x; b < 256; b += nt) s_hist[b] = 0;
@@ -67,10 +70,14 @@ __device__ __forceinline__ void block_select_top(const unsigned long long *keys,
             s_prefix = prefix | ((unsigned long long)b << shift);
             s_mask = mask | (255ull << shift);
             s_need = need - above;
+            // every matching key of bin b is needed: the bin's smallest
+            // possible key (lower bytes zero) already separates the nq largest
+            s_done = s_hist[b] == need - above;
         }
         __syncthreads();
+        if (s_done) break;
     }
-    const unsigned long long thr = s_prefix;  // the nq-th largest key
+    const unsigned long long thr = s_prefix;  // the nq-th largest key, or a bound just below it
     for (int q = threadIdx.x; q < n; q += nt)
         if (keys[q] >= thr) sel[atomicAdd(&s_cnt, 1u)] = keys[q];
     for (int i = nq + threadIdx.x; i < kSelectMax; i += nt) sel[i] = 0ull;
