@@ -107,6 +107,13 @@ __global__ void add_kernel(const float *__restrict__ a, const float *__restrict_
     if (i < n) y[i] = __fadd_rn(a[i], b[i]);
 }
 
+// y[i] = a[i] + b[i % nb]: b shared by every page (nb elements per page)
+__global__ void add_bcast_kernel(const float *__restrict__ a, const float *__restrict__ b,
+                                 float *__restrict__ y, long long n, long long nb) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __fadd_rn(a[i], b[i % nb]);
+}
+
 __global__ void sigmoid_kernel(const float *__restrict__ x, float *__restrict__ y, long long n) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x[i])));
@@ -300,6 +307,14 @@ Status launch_softmax_rows(float *x, long long rows, int L, cudaStream_t st) {
 
 Status launch_add(const float *a, const float *b, float *y, long long n, cudaStream_t st) {
     add_kernel<<<blocks(n), 256, 0, st>>>(a, b, y, n);
+    return cuda_status();
+}
+
+Status launch_add_bcast(const float *a, const float *b, float *y, long long n_per_page,
+                        int pages, cudaStream_t st) {
+    if (n_per_page <= 0 || pages <= 0) return ERR_SHAPE;
+    const long long n = n_per_page * pages;
+    add_bcast_kernel<<<blocks(n), 256, 0, st>>>(a, b, y, n, n_per_page);
     return cuda_status();
 }
 

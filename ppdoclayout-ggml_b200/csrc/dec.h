@@ -24,6 +24,9 @@ Status launch_attention(const float *q, const float *k, const float *v, float *o
                         int ldqk, long long bsqk, int ldvo, long long bsvo, float scale, int B,
                         cudaStream_t st);
 Status launch_add(const float *a, const float *b, float *y, long long n, cudaStream_t st);
+// y = a + b over `pages` pages of n_per_page elements, b shared by all pages
+Status launch_add_bcast(const float *a, const float *b, float *y, long long n_per_page,
+                        int pages, cudaStream_t st);
 Status launch_sigmoid(const float *x, float *y, long long n, cudaStream_t st);
 // ref = sigmoid(delta + inverse_sigmoid(ref))
 // rows of h [rows][256] -> delta = h w^T + b (w [4][256]); ref [rows][4]

@@ -816,9 +816,7 @@ public:
             S q2 = qk;
             const float *pp = pos;
             push("aifi.pos", PPDL_STEP_GLUE, 0.0, 12.0 * 625 * kDM, [=]() {  // qk = s + pos
-                for (int b = 0; b < nb; b++)
-                    TRY(launch_add(sq.p + b * sq.bs(), pp, q2.p + b * q2.bs(), sq.bs(), st));
-                return OK;
+                return launch_add_bcast(sq.p, pp, q2.p, sq.bs(), nb, st);
             });
         }
         mha(qk, sq, at, "aifi");
