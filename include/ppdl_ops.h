@@ -15,9 +15,9 @@
  * op_params[16], with op_params[12] = PPDL_MAGIC and op_params[13] = the op
  * id, exactly as the reference's graph builder tags them
  * (src/ppdoclayout.cpp:50-53).  op_params[14]/[15] carry the per-op
- * parameters with the reference's encodings (listed per id below).  The
- * ggml-side adapter that fills a ppdl_op_desc from a ggml_tensor is shown in
- * INTEGRATION.md.
+ * parameters with the reference's encodings (listed per id below).  A
+ * ggml-side adapter fills a ppdl_op_desc from a ggml_tensor by copying
+ * data, ne[0..3] and op_params[0..15] of the node and of its sources.
  *
  * Batching: the reference runs every op at batch 1.  Here the outermost ne
  * dimension that the reference leaves at 1 may hold several independent
@@ -103,8 +103,11 @@ PPDL_OPS_API int ppdl_op_launch(const ppdl_op_desc * desc, void * stream);
       otherwise     A(m, k) = A[z*a_bs + m*lda + k] (row-major).
    B: [N][K] row-major, shared by all z.  C(m, n) at C[z*c_bs + m*ldc_m + n*ldc_n].
    b_split: caller-provided device workspace of 2*N*K floats for the TF32
-   halves of B.  Requirements (TMA): A, b_split 16-byte aligned; lda, a_bs and
-   K multiples of 4.  Returns PPDL_OK / PPDL_ERR_SHAPE / PPDL_ERR_CUDA. */
+   halves of B.  Requirements (TMA): b_split 16-byte aligned, a_bs and K
+   multiples of 4; a K-major A also 16-byte aligned with lda a multiple of 4
+   (an M-major A with another lda or alignment, e.g. CHW planes of 25 x 25
+   pixels, is loaded as one TMA row per k).  Returns PPDL_OK /
+   PPDL_ERR_SHAPE / PPDL_ERR_CUDA. */
 PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float * A,
                                   int a_m_major, long long lda, long long a_bs,
                                   const float * B, float * b_split, float * C,
@@ -113,9 +116,9 @@ PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float * 
 
 /* Extension (no single counterpart: the reference's conv dispatcher,
    builder::conv at src/ppdoclayout.cpp:388-543, lowers k3-s2 and k2 convs
-   to im2col + cuBLAS SGEMM and 1x1 convs to op 3): a direct convolution on
-   the FP32-faithful tensor-core GEMM, the A tile gathered from the CHW
-   input inside the kernel (no im2col buffer).
+   to im2col + cuBLAS SGEMM, patch:845-906, and 1x1 convs to op 3): a direct
+   convolution on the FP32-faithful tensor-core GEMM with no im2col buffer —
+   the path the forward's k3-s2 / k2 convs take.
      y[z][oc][oy][ox] = act(bias[oc] + sum_{ic,kh,kw} weight[oc][ic][kh][kw]
                           * x[z][ic][oy*S + kh - P][ox*S + kw - P])
    with zero outside H x W (padding P at the top/left; the bottom/right
@@ -123,13 +126,44 @@ PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float * 
    (0, 1); the last window of each axis must start inside the input,
    (OH-1)*S - P < H).  x: pages of dense [IC][H][W] at stride x_bs;
    y: pages of [OC][OH][OW] at stride y_bs; bias may be NULL; act 0/1/2/3 =
-   none/ReLU/SiLU/GELU.  b_split: device workspace of 2*OC*round_up(IC*K*K, 4)
-   floats, 16-byte aligned.  K 1..8 with P < K; K = 1 needs S = 1, P = 0.
+   none/ReLU/SiLU/GELU.  When W and x_bs are multiples of 4, x is 16-byte
+   aligned, S is 1 or 2 (H even for 2) and K is 2..4, the A operand comes
+   from TMA windows of the input (one per kernel row and 32 channels);
+   otherwise the kernel's converter warps gather it.  b_split: device
+   workspace of ppdl_conv2d_tf32x3_workspace(IC, OC, K) floats, 16-byte
+   aligned.  K 1..8 with P < K; K = 1 needs S = 1, P = 0.
    Returns PPDL_OK / PPDL_ERR_SHAPE / PPDL_ERR_CUDA. */
 PPDL_OPS_API int ppdl_conv2d_tf32x3(const float * x, int batch, int IC, int H, int W,
                                     long long x_bs, const float * weight, const float * bias,
                                     int OC, int K, int S, int P, int OH, int OW, int act,
                                     float * b_split, float * y, long long y_bs, void * stream);
+
+/* Floats of b_split that ppdl_conv2d_tf32x3 needs for these sizes (0 for
+   non-positive sizes). */
+PPDL_OPS_API long long ppdl_conv2d_tf32x3_workspace(int IC, int OC, int K);
+
+/* Extension (replaces the node chain pad_ext -> op 10 -> op 12 -> op 11 of
+   the reference's k3-s1-p1 convs, src/ppdoclayout.cpp:430-464 and
+   patch:496-610, 778-812): one 3x3, stride-1, padding-1 convolution by
+   Winograd F(4,3) exactly as the forward runs it — filter transform with the
+   reference's G (src/ppdoclayout.cpp:313-320), input transform with the
+   padding fused, the 36-plane product on the 3xTF32 tensor-core GEMM, output
+   transform with bias and activation.
+     y[z][oc][oy][ox] = act(bias[oc] + sum_{ic,kh,kw} weight[oc][ic][kh][kw]
+                          * x[z][ic][oy + kh - 1][ox + kw - 1])
+   x: pages of dense [IC][H][W] at stride x_bs; y: pages of [OC][H][W] at
+   stride y_bs; bias may be NULL; act 0/1/2/3 = none/ReLU/SiLU/GELU.  IC a
+   multiple of 4.  work: device workspace of
+   ppdl_conv3x3_wg4_workspace(batch, IC, OC, H, W) floats, 16-byte aligned
+   (transformed filter and its TF32 halves, the 36 input and output planes).
+   Returns PPDL_OK / PPDL_ERR_SHAPE / PPDL_ERR_CUDA. */
+PPDL_OPS_API int ppdl_conv3x3_wg4_tf32x3(const float * x, int batch, int IC, int H, int W,
+                                         long long x_bs, const float * weight,
+                                         const float * bias, int OC, int act, float * work,
+                                         float * y, long long y_bs, void * stream);
+
+/* Floats of work that ppdl_conv3x3_wg4_tf32x3 needs (0 for non-positive sizes). */
+PPDL_OPS_API long long ppdl_conv3x3_wg4_workspace(int batch, int IC, int OC, int H, int W);
 
 /* Extension (the reference's depthwise conv is ggml_conv_2d_dw_direct,
    src/ppdoclayout.cpp:400-404, a ggml op rather than a tagged PPDL op):
@@ -166,6 +200,14 @@ PPDL_OPS_API int ppdl_gemm_tf32x3_static(int M, int N, int K, int batch, const f
 
 /* Human-readable text of the last error of ppdl_op_launch on this thread. */
 PPDL_OPS_API const char * ppdl_op_last_error(void);
+
+/* Extension (the reference aborts through GGML_ASSERT and has no device-side
+   error state): the tensor-core kernels bound every wait inside the kernel
+   (about 2 s); a wait that gives up leaves its output unwritten, and the
+   kernel raises a device-wide flag.  After synchronising the stream of the
+   launches in question, this returns 1 if the flag was raised since the last
+   call (and clears it), else 0.  The flag is per device (the current one). */
+PPDL_OPS_API int ppdl_op_device_error(void);
 
 #ifdef __cplusplus
 }

@@ -196,16 +196,19 @@ __global__ void wg4_filter_kernel(const float *__restrict__ w, float *__restrict
 
 // wg4 [36][IC][OC] -> hi/lo [36][OC][IC] (K-major B operand of the
 // tensor-core madd, split into TF32 halves)
-__global__ void wg4_kmajor_split_kernel(const float *__restrict__ wg4, float *__restrict__ hi,
-                                        float *__restrict__ lo, int IC, int OC) {
-    const long long n = 36LL * IC * OC;
+// hi/lo[p][oc][ic] (K-major TF32 halves) from src[p][ic][n0 + oc] (row
+// stride ld, plane stride pstride), oc < nc
+__global__ void kmajor_split_kernel(const float *__restrict__ src, float *__restrict__ hi,
+                                    float *__restrict__ lo, int planes, int IC, int ld,
+                                    long long pstride, int nc) {
+    const long long n = (long long)planes * IC * nc;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int ic = (int)(i % IC);
     const long long r = i / IC;
-    const int oc = (int)(r % OC);
-    const int p = (int)(r / OC);
-    const float v = wg4[((long long)p * IC + ic) * OC + oc];
+    const int oc = (int)(r % nc);
+    const int p = (int)(r / nc);
+    const float v = src[(long long)p * pstride + (long long)ic * ld + oc];
     uint32_t hr;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hr) : "f"(v));  // nearest TF32
     const float h = __uint_as_float(hr);
@@ -460,47 +463,6 @@ __global__ void transpose_kernel(const float *__restrict__ x, long long xbs, flo
     }
 }
 
-// ---- im2col: the M-major GEMM operand of a KS x KS, stride-S conv -----------
-// col[b][k][m] = x[b][ic][oy*S + kh - P][ox*S + kw - P] (0 outside H x W and
-// for k >= IC*KS*KS), k = (ic*KS + kh)*KS + kw (the raw weight's row order),
-// m = oy*OW + ox < M; rows have stride ldm >= M (16-byte multiples for the
-// tensor-core GEMM's TMA), the tail m in [M, ldm) is zero.  KS = 1 is a
-// channel-plane copy into padded rows.  One block row per k (grid.y).
-__global__ void __launch_bounds__(256)
-im2col_kernel(const float *__restrict__ x, long long xbs, long long plane, float *__restrict__ col,
-              long long cbs, int Kc, int H, int W, int KS, int S, int P, int OW, int M, int ldm) {
-    // each thread writes 4 consecutive m with one 16-byte store (ldm % 4 == 0)
-    const int k = blockIdx.y, b = blockIdx.z;
-    float4 *cr = reinterpret_cast<float4 *>(col + (long long)b * cbs + (long long)k * ldm);
-    const int n4 = ldm >> 2;
-    if (k >= Kc) {
-        for (int m4 = blockIdx.x * 256 + threadIdx.x; m4 < n4; m4 += gridDim.x * 256)
-            cr[m4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        return;
-    }
-    const int kk2 = KS * KS, ic = k / kk2, tap = k - ic * kk2, kh = tap / KS, kw = tap - kh * KS;
-    const float *xc = x + (long long)b * xbs + (long long)ic * plane;
-    for (int m4 = blockIdx.x * 256 + threadIdx.x; m4 < n4; m4 += gridDim.x * 256) {
-        float v[4];
-        int m = m4 * 4;
-        int oy = m / OW, ox = m - oy * OW;
-#pragma unroll
-        for (int e = 0; e < 4; e++, m++) {
-            v[e] = 0.0f;
-            if (m < M) {
-                const int iy = oy * S + kh - P, ix = ox * S + kw - P;
-                if ((unsigned)iy < (unsigned)H && (unsigned)ix < (unsigned)W)
-                    v[e] = __ldg(xc + iy * W + ix);
-            }
-            if (++ox == OW) {
-                ox = 0;
-                ++oy;
-            }
-        }
-        cr[m4] = make_float4(v[0], v[1], v[2], v[3]);
-    }
-}
-
 inline int blocks(long long n, int t = 256) { return (int)((n + t - 1) / t); }
 
 // grid of the per-page kernels: x over the channels x pixels (or tiles) of a
@@ -511,19 +473,6 @@ inline bool grid3_ok(long long pix, int ch, int b) {
 inline dim3 grid3(long long pix, int ch, int b) { return dim3(blocks(pix * ch), b); }
 
 }  // namespace
-
-Status launch_im2col(const float *x, long long xbs, long long plane, float *col, long long cbs,
-                     int Kc, int Kp, int H, int W, int KS, int S, int P, int OW, int M, int ldm,
-                     int B, cudaStream_t st) {
-    if (Kp < Kc || ldm < M || ldm % 4 || M <= 0 || B <= 0 || Kp > 65535 || B > 65535 ||
-        ((uintptr_t)col & 15) || cbs % 4)
-        return ERR_SHAPE;
-    int gx = blocks(ldm / 4);
-    if (gx > 64) gx = 64;
-    im2col_kernel<<<dim3(gx, Kp, B), 256, 0, st>>>(x, xbs, plane, col, cbs, Kc, H, W, KS, S, P,
-                                                   OW, M, ldm);
-    return cuda_status();
-}
 
 Status launch_wg4_input(const float *x, long long xbs, float *dt, int IC, int H, int W, int TW,
                         int TH, int pad, int B, cudaStream_t st, int ldt) {
@@ -553,11 +502,17 @@ Status launch_wg4_filter(const float *w, float *wg4, int IC, int OC, cudaStream_
     return cuda_status();
 }
 
+Status launch_kmajor_split(const float *src, float *hi, float *lo, int planes, int IC, int ld,
+                           long long pstride, int nc, cudaStream_t st) {
+    if (planes <= 0 || IC <= 0 || nc <= 0 || ld < nc) return ERR_SHAPE;
+    const long long n = (long long)planes * IC * nc;
+    kmajor_split_kernel<<<blocks(n), 256, 0, st>>>(src, hi, lo, planes, IC, ld, pstride, nc);
+    return cuda_status();
+}
+
 Status launch_wg4_kmajor_split(const float *wg4, float *hi, float *lo, int IC, int OC,
                                cudaStream_t st) {
-    const long long n = 36LL * IC * OC;
-    wg4_kmajor_split_kernel<<<blocks(n), 256, 0, st>>>(wg4, hi, lo, IC, OC);
-    return cuda_status();
+    return launch_kmajor_split(wg4, hi, lo, 36, IC, OC, (long long)IC * OC, OC, st);
 }
 
 Status launch_dwconv(const float *x, long long xbs, const float *w, const float *bias, float *y,

@@ -25,6 +25,11 @@ Status launch_wg4_output(const float *yt, const float *bias, float *y, long long
 Status launch_wg4_kmajor_split(const float *wg4, float *hi, float *lo, int IC, int OC,
                                cudaStream_t st);
 
+// The general form: src[p][ic][n0 + oc] (row stride ld, plane stride pstride,
+// src already offset by n0) -> hi/lo [planes][nc][IC]
+Status launch_kmajor_split(const float *src, float *hi, float *lo, int planes, int IC, int ld,
+                           long long pstride, int nc, cudaStream_t st);
+
 // w [OC][IC][3][3] -> wg4 [36][IC][OC] (G g G^T with the reference's G)
 Status launch_wg4_filter(const float *w, float *wg4, int IC, int OC, cudaStream_t st);
 
@@ -43,15 +48,6 @@ Status launch_maxpool2_pad(const float *x, long long xbs, float *y, long long yb
 Status launch_interp(const float *x, long long xbs, float *y, long long ybs, const float *base,
                      long long bbs, int C, int H, int W, int OH, int OW, bool bilinear, int B,
                      cudaStream_t st);
-
-// im2col of a KS x KS stride-S conv with top/left padding P (bottom/right
-// padding implied by OW and M = OH*OW) into col [B][Kp][ldm]:
-// col[k][m] = x[ic][oy*S+kh-P][ox*S+kw-P], k = (ic*KS+kh)*KS+kw < Kc, zero
-// rows for Kc <= k < Kp and zero tails for M <= m < ldm.  KS = 1 copies the
-// channel planes into rows of stride ldm (plane stride `plane` of x).
-Status launch_im2col(const float *x, long long xbs, long long plane, float *col, long long cbs,
-                     int Kc, int Kp, int H, int W, int KS, int S, int P, int OW, int M, int ldm,
-                     int B, cudaStream_t st);
 
 // y[c][r] = x[r][c] for an R x Cc matrix per page (row strides ldx, ldy)
 Status launch_transpose(const float *x, long long xbs, float *y, long long ybs, int R, int Cc,

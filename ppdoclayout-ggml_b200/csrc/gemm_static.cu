@@ -61,11 +61,22 @@ float *scratch_on_current_device() {
 
 }  // namespace
 
+namespace ppdl {
+// The same array for the operator hooks of ops_conv.cu (ops 3 and 12 split
+// their weights into it in chunks): hi at [0, cap), lo at [cap, 2 cap).
+// Shared with ppdl_gemm_tf32x3_static: their GPU work must not overlap.
+float *static_split_workspace(long long *cap) {
+    *cap = kStaticMaxNK;
+    return scratch_on_current_device();
+}
+}  // namespace ppdl
+
 extern "C" PPDL_OPS_API int ppdl_gemm_tf32x3_static(int M, int N, int K, int batch, const float *A,
                                                     int a_m_major, long long lda, long long a_bs,
                                                     const float *B, float *C, long long ldc_m,
                                                     long long ldc_n, long long c_bs,
                                                     void *stream) {
+    ppdl::set_op_error("");  // a PPDL_OK leaves no older message behind
     if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || !A || !B || !C) {
         ppdl::set_op_error("gemm_static: bad sizes or null pointer");
         return PPDL_ERR_SHAPE;

@@ -52,6 +52,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <mutex>
 
 #include "gemm_tc.h"
 
@@ -95,6 +96,16 @@ constexpr int kBoxN = 16;
 constexpr int kBoxBytes = 32 * kBoxN * 4;
 constexpr int kStagingBytes = 8 * 2 * kBoxBytes;  // 32 KB
 constexpr int kCtrlBytes = 2048;                 // control block + 1024-alignment slack
+// box mode: input windows in flight (a ring of their own beside the stages)
+constexpr int kMaxBoxes = 4;
+// rows mode: a k-block is 32 channel rows of kRowsBox floats (128 pixels
+// plus up to 3 floats of alignment remainder, rounded to 16 bytes), each
+// in a slot of kRowsPitch floats (640 bytes: TMA destinations stay 128-byte
+// aligned); the A region is 20 KB, so B stays 1024-byte aligned
+constexpr int kRowsBox = 132;
+constexpr int kRowsPitch = 160;
+constexpr int kRowsBytes = 32 * kRowsPitch * 4;
+static_assert(kRowsBytes % 1024 == 0 && (kRowsPitch * 4) % 128 == 0, "rows-mode layout");
 constexpr int kSmemMax = 227 * 1024;
 
 // Registers per thread: at launch (the __launch_bounds__(512, 1) maximum,
@@ -108,9 +119,11 @@ static_assert(128 * kRegsConv + 128 * kRegsMma + 256 * kRegsEpi <= kThreads * kL
 
 struct Args {
     int M, N, K, batch, planes, a_mn, bn, stages, m_tiles, n_tiles, tiles;
-    int gather, tma_c;
-    uint32_t stage_bytes, tx_bytes, idesc;
+    int gather, tma_c, box, rows, rows_offmul, rows_delta;
+    long long rows_plane;
+    uint32_t stage_bytes, tx_bytes, idesc, staging_off;
     TcGather gg;
+    TcConvBox cb;
     TcEpilogue epi;
 };
 
@@ -180,6 +193,31 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *tm,
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, uint32_t bar,
+                                            int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *tm, uint32_t bar,
+                                            int x, int y, int z, int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap *tm, uint32_t bar,
+                                            int x, int y, int z, int w, int v) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v)
+        : "memory");
+}
+
 // TMA store of a shared-memory box into the tensor (async proxy; the box
 // must be published with fence.proxy.async first).  Coordinates are never
 // negative here; parts of the box outside the tensor are not written.
@@ -189,6 +227,14 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *tm, uint32_t src
         "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
             reinterpret_cast<uint64_t>(tm)),
         "r"(src), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *tm, uint32_t src, int x, int y,
+                                             int z, int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(tm)),
+        "r"(src), "r"(x), "r"(y), "r"(z), "r"(w)
         : "memory");
 }
 __device__ __forceinline__ void bulk_commit() {
@@ -429,7 +475,50 @@ __device__ __forceinline__ void split_row_mmajor(const uint8_t *tile, int r, uin
     }
 }
 
-template <int ACT>
+// Box mode: the thread's A row (one output pixel) of k-block j of the
+// current input window: kernel column j, the window's 32 channels.
+// base = the pixel's offset in the window (row r * Wb + column cx * S +
+// alignment remainder), chs = the window's channel stride (4 * Wb floats).
+__device__ __forceinline__ void split_row_box(const float *win, int base, int chs, int j,
+                                              uint32_t col) {
+    {
+        const float *t = win + base + j;
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+            float x[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) x[u] = t[(8 * h + u) * chs];
+            split_store8(col + 8 * h, x);
+        }
+        return;
+    }
+}
+
+// Rows mode: the thread's pixel r of a k-block stored as 32 channel rows of
+// kRowsPitch floats, row j starting (j * offmul + delta) & 3 floats late
+// (the TMA row began at the 16-byte boundary below it).
+__device__ __forceinline__ void split_row_rows(const uint8_t *tile, int r, int offmul, int delta,
+                                               uint32_t col) {
+    const float *t = reinterpret_cast<const float *>(tile) + r;
+#pragma unroll
+    for (int h = 0; h < 4; h++) {
+        float x[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int j = 8 * h + u;
+            x[u] = t[j * kRowsPitch + ((j * offmul + delta) & 3)];
+        }
+        split_store8(col + 8 * h, x);
+    }
+}
+
+// A-operand modes, a template parameter so that each role keeps only the
+// state of its mode (the converter runs at its register limit)
+constexpr int kModeTile = 0;  // TMA tile of A (M- or K-major), or the gather
+constexpr int kModeBox = 1;   // implicit conv from TMA windows of the input
+constexpr int kModeRows = 2;  // M-major A as 32 per-channel TMA rows
+
+template <int ACT, int AMODE>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBhi,
                const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmC,
@@ -446,7 +535,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const uint32_t ctrl = raw;
     const uint32_t bar_full = ctrl, bar_empty = ctrl + 8 * kMaxStages,
                    bar_afull = ctrl + 16 * kMaxStages, bar_pempty = bar_afull + 8 * kAStages,
-                   bar_done = bar_pempty + 8 * kSlots;
+                   bar_done = bar_pempty + 8 * kSlots,
+                   bar_bfull = bar_done + 8, bar_bempty = bar_bfull + 8 * kMaxBoxes;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem_raw + 256);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem_raw + 260);
     const uint32_t stage0 = (raw + 512 + 1023) & ~1023u;
@@ -463,6 +553,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int j = 0; j < kAStages; j++) mbar_init(bar_afull + 8 * j, kConvThreads);
         for (int i = 0; i < kSlots; i++) mbar_init(bar_pempty + 8 * i, kEpiThreads);
         mbar_init(bar_done, kMmaWarps);
+        // box mode: bfull[b] window b landed (producer arrive + tx),
+        // bempty[b] window b read by all 128 converter threads
+        for (int b = 0; b < kMaxBoxes; b++) {
+            mbar_init(bar_bfull + 8 * b, 1);
+            mbar_init(bar_bempty + 8 * b, kConvThreads);
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -489,19 +585,50 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsMma));
         // parameters in registers (the waits below clobber memory)
         const int ptiles = a.tiles, pmt = a.m_tiles, pnt = a.n_tiles, pbn = a.bn,
-                  pamn = a.a_mn, pgather = a.gather, pplanes = a.planes;
+                  pamn = a.a_mn, pgather = a.gather,
+                  pplanes = a.planes;
         const uint32_t pstage = a.stage_bytes, ptx = a.tx_bytes, pidesc = a.idesc;
         if (warp == kWarpProducer) {
             if (lane == 0) {
-                long long it = 0;
-                Ring rs(S);
+                constexpr bool pbox = AMODE == kModeBox, prows = AMODE == kModeRows;
+                const uint32_t box0 = stage0 + (uint32_t)S * pstage;
+                long long it = 0, ib = 0;  // stages and windows issued
+                Ring rs(S), rb(a.cb.nbox);
                 bool ok = true;
                 for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
                     const int z = t / (pmt * pnt);
                     const int r = t - z * pmt * pnt;
-                    const int m0 = (r / pnt) * kBM, n0 = (r % pnt) * pbn;
+                    const int mt = r / pnt;
+                    const int m0 = mt * kBM, n0 = (r - mt * pnt) * pbn;
                     const int pz = z % pplanes;
+                    // box mode: output tile origin and the window walk
+                    // (k-block j of window (cb, kh))
+                    int oy0 = 0, ox0 = 0, j = 0, kh = 0, cbk = 0;
+                    if (pbox) {
+                        const int ty = mt / a.cb.tiles_x;
+                        oy0 = ty * 4;
+                        ox0 = (mt - ty * a.cb.tiles_x) * 32;
+                    }
                     for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
+                        const int k0 = kb * kBK;
+                        if (pbox && j == 0) {
+                            if (!mbar_wait(bar_bempty + 8 * rb.i, rb.ph ^ 1, abort_flag)) {
+                                ok = false;
+                                break;
+                            }
+                            const uint32_t bb = bar_bfull + 8 * rb.i;
+                            const uint32_t dst = box0 + (uint32_t)rb.i * a.cb.box_bytes;
+                            mbar_expect_tx(bb, a.cb.box_tx);
+                            const int x = ox0 * a.cb.S - a.cb.P - a.cb.o;
+                            const int d = kh - a.cb.P;
+                            if (a.cb.S == 1)
+                                tma_load_4d(dst, &tmA, bb, x, oy0 + d, cbk * a.cb.CB, z);
+                            else  // rows (H/2, parity): input row 2 * oy + d
+                                tma_load_5d(dst, &tmA, bb, x, oy0 + (d >> 1), d & 1,
+                                            cbk * a.cb.CB, z);
+                            rb.next();
+                            ib++;
+                        }
                         const int s = rs.i;
                         const uint32_t ph = rs.ph;
                         if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, abort_flag)) {
@@ -511,24 +638,47 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         const uint32_t st = stage0 + s * pstage;
                         const uint32_t fb = bar_full + 8 * s;
                         mbar_expect_tx(fb, ptx);
-                        const int k0 = kb * kBK;
-                        if (pgather) {
-                            // A is written by the converter warps
+                        if (pgather || pbox) {
+                            // A is written by the converter warps / comes from a window
+                        } else if (prows) {
+                            // 32 channel rows, each from the 16-byte boundary below it
+                            const long long xz = a.rows_plane;
+                            for (int jr = 0; jr < 32; jr++) {
+                                const long long xr = (long long)(k0 + jr) * xz + m0 + a.rows_delta;
+                                tma_load_2d(st + (uint32_t)(jr * kRowsPitch * 4), &tmA, fb,
+                                            (int)(xr & ~3LL), z);
+                            }
                         } else if (pamn) {
                             tma_load_3d(st, &tmA, fb, m0, k0, z);
                         } else {
                             tma_load_3d(st, &tmA, fb, k0, m0, z);
                         }
-                        tma_load_3d(st + kABytes, &tmBhi, fb, k0, n0, pz);
-                        tma_load_3d(st + kABytes + pbn * 128, &tmBlo, fb, k0, n0, pz);
+                        const uint32_t stb = st + (uint32_t)a.stage_bytes - 2u * 128u * pbn;
+                        tma_load_3d(stb, &tmBhi, fb, k0, n0, pz);
+                        tma_load_3d(stb + pbn * 128, &tmBlo, fb, k0, n0, pz);
+                        if (pbox && ++j == a.cb.kbpb) {
+                            j = 0;
+                            if (++kh == a.cb.KS) {
+                                kh = 0;
+                                ++cbk;
+                            }
+                        }
                     }
                 }
-                // drain: the last issued stages must land before the CTA may exit
+                // drain: the last issued stages and windows must land before
+                // the CTA may exit
                 const long long first = it > S ? it - S : 0;
-                for (long long j = first; j < it; j++) {
-                    const int s = (int)(j % S);
+                for (long long jj = first; jj < it; jj++) {
+                    const int s = (int)(jj % S);
                     int dummy = 0;
-                    mbar_wait(bar_full + 8 * s, (uint32_t)((j / S) & 1), (volatile int *)&dummy);
+                    mbar_wait(bar_full + 8 * s, (uint32_t)((jj / S) & 1), (volatile int *)&dummy);
+                }
+                const int nb = a.cb.nbox;
+                const long long bfirst = ib > nb ? ib - nb : 0;
+                for (long long jj = bfirst; jj < ib; jj++) {
+                    int dummy = 0;
+                    mbar_wait(bar_bfull + 8 * (int)(jj % nb), (uint32_t)((jj / nb) & 1),
+                              (volatile int *)&dummy);
                 }
             }
         } else if (warp < kWarpMma + kMmaWarps) {
@@ -561,7 +711,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         const uint32_t d = tmem_base + (uint32_t)(rp.i * kSlotCols);
                         const uint32_t ahi = tmem_base + (uint32_t)(kACol0 + ra.i * kACols);
                         const uint32_t alo = ahi + kBK;
-                        const uint32_t bhi = stage0 + rs.i * pstage + kABytes;
+                        const uint32_t bhi = stage0 + rs.i * pstage + pstage - 2u * 128u * pbn;
                         // B K-major: the K=8 step kk is 32 bytes into the swizzled
                         // row, i.e. +2 in the descriptor's start-address field
                         // (which cannot carry: shared addresses stay below 256 KB)
@@ -590,7 +740,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsConv));
         // parameters in registers (the waits below clobber memory)
         const int ptiles = a.tiles, pmt = a.m_tiles, pnt = a.n_tiles, pbn = a.bn,
-                  pamn = a.a_mn, pgather = a.gather, pplanes = a.planes;
+                  pamn = a.a_mn, pgather = a.gather,
+                  pplanes = a.planes;
         const uint32_t pstage = a.stage_bytes, ptx = a.tx_bytes, pidesc = a.idesc;
         {
             // converter: thread ct owns row ct of every A tile (TMEM lane ct,
@@ -611,6 +762,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             int it = 0, pub = 0;  // k-blocks [pub, it) issued, not yet split (gather)
             Ring rs(S), rp(S), rw(S), ra(kAStages);  // issue, split, TMEM wait, A stage
             bool ok = true;
+            // box mode: window ring, the thread's pixel offset in a window
+            // and the k-block index inside the current window
+            constexpr bool pbox = AMODE == kModeBox, prows = AMODE == kModeRows;
+            Ring rbw(a.cb.nbox);
+            const float *box0_ptr =
+                reinterpret_cast<const float *>(stage0_ptr + (size_t)S * pstage);
+            const int chs = 4 * a.cb.Wb;
+            int wbase = 0, wj = 0;
             // split the k-block at ring position rp into TMEM A stage ra
             // (lane 0 waits for the warp and the verdict is shared, so the
             // warp-collective TMEM stores always run converged)
@@ -624,7 +783,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 tc_fence_after();
                 const uint8_t *tile = stage0_ptr + (size_t)rp.i * pstage;
                 const uint32_t col = tmem_base + lane_base + (uint32_t)(kACol0 + ra.i * kACols);
-                if (pamn && !pgather)
+                if (pbox)
+                    split_row_box(box0_ptr + (size_t)rbw.i * (a.cb.box_bytes / 4), wbase, chs, wj,
+                                  col);
+                else if (prows)
+                    split_row_rows(tile, ct, a.rows_offmul, a.rows_delta, col);
+                else if (pamn && !pgather)
                     split_row_mmajor(tile, ct, col);
                 else
                     split_row_kmajor(tile, ct, col);
@@ -640,6 +804,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const int r = t - z * pmt * pnt;
                 const int m0 = (r / pnt) * kBM;
                 const float *xz = pgather ? gg.x + (long long)z * gg.x_bs : nullptr;
+                if (pbox) {
+                    // pixel (row ct / 32, column ct % 32) of the 4 x 32 tile
+                    wbase = (ct >> 5) * a.cb.Wb + (ct & 31) * a.cb.S + a.cb.o;
+                    wj = 0;
+                }
                 int oy0 = -64, ox0 = 0;
                 if (pgather && m0 + ct < a.M) {
                     const int oy = (m0 + ct) / gg.OW;
@@ -648,6 +817,27 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     ox0 = ox * gg.S - gg.P;
                 }
                 for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
+                    if (pbox) {
+                        if (wj == 0) {
+                            bool good = true;
+                            if (lane == 0) good = mbar_wait(bar_bfull + 8 * rbw.i, rbw.ph, abort_flag);
+                            if (!__shfl_sync(0xffffffffu, good ? 1 : 0, 0)) {
+                                ok = false;
+                                break;
+                            }
+                        }
+                        if (!publish(it)) {
+                            ok = false;
+                            break;
+                        }
+                        if (++wj == a.cb.kbpb) {
+                            // the thread's reads of this window are done
+                            mbar_arrive(bar_bempty + 8 * rbw.i);
+                            rbw.next();
+                            wj = 0;
+                        }
+                        continue;
+                    }
                     if (!pgather) {
                         if (!publish(it)) {
                             ok = false;
@@ -707,8 +897,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // residual in registers before the box (measured faster); the GELU
         // form keeps the all-in-the-box loop
         constexpr bool kPreOps = ACT != ACT_GELU;
-        const uint32_t staging = stage0 + (uint32_t)S * a.stage_bytes;
-        float *staging_ptr = reinterpret_cast<float *>(stage0_ptr + (size_t)S * a.stage_bytes);
+        const uint32_t staging = stage0 + a.staging_off;
+        float *staging_ptr = reinterpret_cast<float *>(stage0_ptr + a.staging_off);
+        constexpr bool pbox = AMODE == kModeBox;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         float tot[kHalfCols];
         long long ctr = 0;
@@ -720,8 +911,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
             const int z = t / (pmt * pnt);
             const int r = t - z * pmt * pnt;
-            const int m0 = (r / pnt) * kBM, n0 = (r % pnt) * pbn;
-            const int m = m0 + quad * 32 + lane;
+            const int mt = r / pnt;
+            const int m0 = mt * kBM, n0 = (r - mt * pnt) * pbn;
             float *C = e.C + (long long)z * e.c_bs;
             const float *R = e.res_mode ? e.res + (long long)z * e.res_bs : nullptr;
             // (ReLU / SiLU outputs) the bias of the warp's columns c_lo + lane
@@ -764,18 +955,33 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 mbar_arrive(bar_pempty + 8 * p);
             }
             if (!ok) break;
-            const bool row_ok = m < pM;
+            // the tile's output rows (computed after the folds, which hold
+            // the most registers): row m of the GEMM, or in box mode pixel
+            // ox0 + lane of output row oy0 + quad (the warp's 32 rows)
+            int m = m0 + quad * 32 + lane;
+            bool row_ok = m < pM;
+            int oy0 = 0, ox0 = 0;
+            if (pbox) {
+                const int ty = mt / a.cb.tiles_x;
+                oy0 = ty * 4;
+                ox0 = (mt - ty * a.cb.tiles_x) * 32;
+                const int oy = oy0 + quad, ox = ox0 + lane;
+                row_ok = oy < a.cb.OH && ox < a.cb.OW;
+                m = oy * a.cb.OW + ox;
+            }
             float *Crow = C + (long long)m * e.ldc_m;
             const float *Rrow = R ? R + (long long)m * e.res_ldm : nullptr;
             const bool ops = ACT != ACT_NONE || e.alpha != 1.0f || e.bias || e.res_mode;
             // one 16-column chunk of the register totals: staged through a
             // shared-memory box and a TMA store, or stored directly
             auto store_chunk = [&](int c0, const float (&v)[16]) {
-                if (ptma == 1) {
+                if (ptma == 1 || ptma == 3) {
                     // CHW output: the warp's 32 pixels x 16 channels go into a
                     // staging box (lane = pixel, conflict-free rows of 128 B)
                     // and out with one TMA store, which clips rows >= M and
-                    // channels >= N.  Two boxes per warp alternate.
+                    // channels >= N (box mode: a 4-D store of 32 pixels of one
+                    // output row, clipped at the row end).  Two boxes per warp
+                    // alternate.
                     const int b = nbox & 1;
                     if (nbox >= 2) {
                         if (lane == 0) bulk_wait_read_1();
@@ -872,15 +1078,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     if (lane == 0) {
                         // boxes wholly past the tensor edge are skipped; the
                         // group is committed regardless to keep the count
-                        if (m0 + quad * 32 < pM && n0 + c0 < pN)
+                        if (ptma == 3) {
+                            if (oy0 + quad < a.cb.OH && n0 + c0 < pN)
+                                tma_store_4d(&tmC, staging + (uint32_t)((ew * 2 + b) * kBoxBytes),
+                                             ox0, oy0 + quad, n0 + c0, z);
+                        } else if (m0 + quad * 32 < pM && n0 + c0 < pN) {
                             tma_store_3d(&tmC, staging + (uint32_t)((ew * 2 + b) * kBoxBytes),
                                          m0 + quad * 32, n0 + c0, z);
+                        }
                         bulk_commit();
                     }
                     nbox++;
                     return;
                 }
-                if (ptma == 2) {
+                if (!pbox && ptma == 2) {
                     // token-major output: the warp's 32 rows x 16 columns go into
                     // a row-major staging box (lane = row, four 16-byte stores)
                     // and out with one TMA store; the ops pass walks the box
@@ -1009,25 +1220,45 @@ __global__ void tf32_split_pad_kernel(const float *__restrict__ w, float *__rest
     lo[i] = v - h;
 }
 
+// Box-mode repack: hi/lo[n][k], k = (bx * kbpb * 32) + kw * CB + c with
+// bx = cb * KS + kh, from w[n][ic = cb * CB + c][kh][kw]; zero where kw >= KS
+// (window padding) or ic >= IC.
+__global__ void tf32_split_box_kernel(const float *__restrict__ w, float *__restrict__ hi,
+                                      float *__restrict__ lo, int OC, int IC, int KS, int CB,
+                                      int kbpb, int Kb) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)OC * Kb) return;
+    const int n = (int)(i / Kb), k = (int)(i - (long long)n * Kb);
+    const int per = kbpb * 32;
+    const int bx = k / per, kin = k - bx * per;
+    const int kw = kin / CB, c = kin - kw * CB;
+    const int kh = bx % KS, ic = (bx / KS) * CB + c;
+    float v = 0.0f;
+    if (kw < KS && ic < IC) v = w[(((long long)n * IC + ic) * KS + kh) * KS + kw];
+    const float h = tf32_rna(v);
+    hi[i] = h;
+    lo[i] = v - h;
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// The driver's tensor-map encoder, resolved once (a function-local static
+// initialiser runs exactly once even when several host threads make their
+// first call together).
 EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
+    static const EncodeTiledFn fn = []() -> EncodeTiledFn {
         void *p = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
                 cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)p;
-        else
-            cudaGetLastError();
-    }
+            return (EncodeTiledFn)p;
+        cudaGetLastError();
+        return nullptr;
+    }();
     return fn;
 }
 
@@ -1069,10 +1300,26 @@ Status launch_tf32_split_pad(const float *w, float *hi, float *lo, int rows, int
     return cuda_status();
 }
 
+Status launch_tf32_split_box(const float *w, float *hi, float *lo, int OC, int IC, int KS,
+                             cudaStream_t st) {
+    if (OC <= 0 || IC <= 0 || KS <= 0) return ERR_SHAPE;
+    int CB, kbpb, nbx;
+    tc_conv_box_blocks(IC, KS, &CB, &kbpb, &nbx);
+    const int Kb = nbx * kbpb * 32;
+    const long long n = (long long)OC * Kb;
+    tf32_split_box_kernel<<<(int)((n + 255) / 256), 256, 0, st>>>(w, hi, lo, OC, IC, KS, CB, kbpb,
+                                                                  Kb);
+    return cuda_status();
+}
+
 namespace {
 
-// Tile and stage sizing shared by both planners.
-bool plan_common(TcGemm *g, int M, int N, int K, int batch, int planes, const TcEpilogue &epi) {
+// Tile and stage sizing shared by the planners.  a_bytes: the A region of
+// a stage (0 when A does not pass through the stages); ring_bytes: shared
+// memory held beside the stages (box mode: the window ring); row_tiles:
+// M tiles over all pages (0 = from M and batch).
+bool plan_common(TcGemm *g, int M, int N, int K, int batch, int planes, const TcEpilogue &epi,
+                 uint32_t a_bytes = kABytes, uint32_t ring_bytes = 0, long long row_tiles = 0) {
     g->ok = false;
     if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || planes <= 0) return false;
     // N tile (multiple of 16, <= 128 so that the partial slots and the A
@@ -1081,7 +1328,7 @@ bool plan_common(TcGemm *g, int M, int N, int K, int batch, int planes, const Tc
     // A traffic and epilogue overhead in column equivalents.  A GEMM of a
     // few dozen row tiles (the decoder's 2400 rows) thus takes narrower N
     // tiles and spreads over more SMs.
-    const long long row_tiles = (long long)((M + kBM - 1) / kBM) * batch;
+    if (row_tiles <= 0) row_tiles = (long long)((M + kBM - 1) / kBM) * batch;
     const long long sms = sm_count();
     int bn = 16;
     long long best = -1;
@@ -1093,13 +1340,14 @@ bool plan_common(TcGemm *g, int M, int N, int K, int batch, int planes, const Tc
             bn = c;
         }
     }
-    const uint32_t stage_bytes = kABytes + 2 * 128 * bn;
-    int stages = (int)((kSmemMax - kCtrlBytes - kStagingBytes) / stage_bytes);
+    const uint32_t stage_bytes = a_bytes + 2 * 128 * bn;
+    const long long room = (long long)kSmemMax - kCtrlBytes - kStagingBytes - ring_bytes;
+    int stages = room > 0 ? (int)(room / stage_bytes) : 0;
     if (stages > kMaxStages) stages = kMaxStages;
     if (stages < kMinStages) return false;
     g->M = M; g->N = N; g->K = K; g->batch = batch; g->planes = planes;
     g->bn = bn; g->stages = stages;
-    g->smem = kCtrlBytes + (size_t)stages * stage_bytes + kStagingBytes;
+    g->smem = kCtrlBytes + (size_t)stages * stage_bytes + ring_bytes + kStagingBytes;
     if (g->smem < 120 * 1024) g->smem = 120 * 1024;  // one CTA per SM: TMEM is not shared
     g->m_tiles = (M + kBM - 1) / kBM;
     g->n_tiles = (N + bn - 1) / bn;
@@ -1117,6 +1365,27 @@ void encode_c(TcGemm *g) {
     if (e.c_bs < 0 || ((uintptr_t)e.C & 15) || (e.c_bs * 4) % 16 ||
         (g->batch > 1 && e.c_bs == 0))
         return;
+    if (g->box) {
+        // box mode, CHW output [N][OH][OW]: 4-D map, boxes of 32 pixels of
+        // one output row x 16 channels (output rows must be 16-byte multiples)
+        const TcConvBox &b = g->cb;
+        EncodeTiledFn fn = encode_fn();
+        if (!fn || e.ldc_m != 1 || b.OW % 4 || (e.ldc_n * 4) % 16 ||
+            e.ldc_n != (long long)b.OH * b.OW)
+            return;
+        const cuuint64_t dims[4] = {(cuuint64_t)b.OW, (cuuint64_t)b.OH, (cuuint64_t)g->N,
+                                    (cuuint64_t)g->batch};
+        const cuuint64_t strides[3] = {(cuuint64_t)b.OW * 4, (cuuint64_t)e.ldc_n * 4,
+                                       (cuuint64_t)(e.c_bs ? e.c_bs : e.ldc_n * g->N) * 4};
+        const cuuint32_t box[4] = {32, 1, kBoxN, 1};
+        const cuuint32_t es[4] = {1, 1, 1, 1};
+        if (fn(&g->tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, e.C, dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+            CUDA_SUCCESS)
+            g->tma_c = 3;
+        return;
+    }
     if (e.ldc_m == 1 && e.ldc_n > 0 && (e.ldc_n * 4) % 16 == 0) {
         // CHW: pixels contiguous, boxes of 32 pixels x 16 channels
         if (encode3d(&g->tmC, e.C, (uint64_t)g->M, (uint64_t)g->N, (uint64_t)g->batch,
@@ -1153,6 +1422,8 @@ bool tc_gemm_plan(TcGemm *g, int M, int N, int K, int batch, const float *A, int
     if (!plan_common(g, M, N, K, batch, planes, epi)) return false;
     g->a_mn = a_mn;
     g->gather = 0;
+    g->box = 0;
+    g->rows = 0;
     bool ok;
     if (a_mn)
         ok = encode3d(&g->tmA, A, (uint64_t)M, (uint64_t)K, (uint64_t)batch, (uint64_t)lda * 4,
@@ -1179,31 +1450,154 @@ bool tc_gemm_plan_gather(TcGemm *g, int M, int N, int K, int batch, const TcGath
     if (!plan_common(g, M, N, K, batch, 1, epi)) return false;
     g->a_mn = 0;  // the gathered tile is K-major
     g->gather = 1;
+    g->box = 0;
+    g->rows = 0;
     g->gg = gg;
     g->ok = encode_b(g, Bhi, Blo, (K + 3) / 4 * 4);
     if (g->ok) encode_c(g);
     return g->ok;
 }
 
+bool tc_gemm_plan_box(TcGemm *g, int N, int batch, const TcConvBox &cbin, const float *Bhi,
+                      const float *Blo, const TcEpilogue &epi) {
+    g->ok = false;
+    TcConvBox b = cbin;
+    if (!b.x || b.IC <= 0 || b.H <= 0 || b.W <= 0 || b.OH <= 0 || b.OW <= 0 || b.KS < 1 ||
+        b.KS > 4 || b.P < 0 || b.P >= b.KS || (b.S != 1 && b.S != 2))
+        return false;
+    // TMA: 16-byte aligned base, rows, planes and pages
+    if (((uintptr_t)b.x & 15) || b.W % 4 || (b.x_bs * 4) % 16 || (b.S == 2 && b.H % 2))
+        return false;
+    if ((long long)b.OH * b.OW >= (1LL << 31)) return false;
+    tc_conv_box_blocks(b.IC, b.KS, &b.CB, &b.kbpb, &b.nbx);
+    // window: columns from the 16-byte boundary at or below ox0*S - P (ox0
+    // is a multiple of 32, so the remainder o is (-P) mod 4) through the
+    // last tap of column 31
+    b.o = ((-b.P) % 4 + 4) % 4;
+    b.Wb = (b.o + 31 * b.S + b.KS + 3) / 4 * 4;
+    b.tiles_x = (b.OW + 31) / 32;
+    b.tiles_y = (b.OH + 3) / 4;
+    const uint32_t raw_bytes = (uint32_t)b.Wb * 4 * b.CB * 4;
+    b.box_tx = raw_bytes;
+    b.box_bytes = (raw_bytes + 1023) / 1024 * 1024;
+    const int K = b.nbx * b.kbpb * 32;
+    const long long row_tiles = (long long)b.tiles_x * b.tiles_y * batch;
+    // two windows in flight at least, three when they fit beside the stages
+    bool planned = false;
+    for (int nb = 3; nb >= 2 && !planned; nb--) {
+        b.nbox = nb;
+        planned = plan_common(g, b.OH * b.OW, N, K, batch, 1, epi, 0, (uint32_t)nb * b.box_bytes,
+                              row_tiles);
+    }
+    if (!planned) return false;
+    g->m_tiles = b.tiles_x * b.tiles_y;
+    g->tiles = g->m_tiles * g->n_tiles * batch;
+    g->a_mn = 1;
+    g->gather = 0;
+    g->rows = 0;
+    g->box = 1;
+    g->cb = b;
+    // the input as [B][C][H][W] (S = 1) or [B][C][2][H/2][W] with the row
+    // parity as its own axis (S = 2: a window's rows are 2*oy + d for four
+    // consecutive oy, i.e. four consecutive H/2 rows of one parity)
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t W = (cuuint64_t)b.W, H = (cuuint64_t)b.H, IC = (cuuint64_t)b.IC;
+    CUresult rc;
+    if (b.S == 1) {
+        const cuuint64_t dims[4] = {W, H, IC, (cuuint64_t)batch};
+        const cuuint64_t strides[3] = {W * 4, W * H * 4, (cuuint64_t)b.x_bs * 4};
+        const cuuint32_t box[4] = {(cuuint32_t)b.Wb, 4, (cuuint32_t)b.CB, 1};
+        const cuuint32_t es[4] = {1, 1, 1, 1};
+        rc = fn(&g->tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(b.x), dims,
+                strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        const cuuint64_t dims[5] = {W, H / 2, 2, IC, (cuuint64_t)batch};
+        const cuuint64_t strides[4] = {2 * W * 4, W * 4, W * H * 4, (cuuint64_t)b.x_bs * 4};
+        const cuuint32_t box[5] = {(cuuint32_t)b.Wb, 4, 1, (cuuint32_t)b.CB, 1};
+        const cuuint32_t es[5] = {1, 1, 1, 1, 1};
+        rc = fn(&g->tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float *>(b.x), dims,
+                strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (rc != CUDA_SUCCESS) return false;
+    g->ok = encode_b(g, Bhi, Blo, K);
+    if (g->ok) encode_c(g);
+    return g->ok;
+}
+
+bool tc_gemm_plan_rows(TcGemm *g, int M, int N, int K, int batch, const float *x, long long plane,
+                       long long x_bs, const float *Bhi, const float *Blo, const TcEpilogue &epi,
+                       int planes) {
+    g->ok = false;
+    if (!x || plane < M || K % 4 || ((uintptr_t)x & 3) || (x_bs * 4) % 16 ||
+        (batch > 1 && x_bs <= 0) ||
+        (long long)(K + 32) * plane + 4 >= (1LL << 31))
+        return false;
+    if (!plan_common(g, M, N, K, batch, planes, epi, kRowsBytes)) return false;
+    // the map starts at the 16-byte boundary at or below x; delta = the
+    // floats between them
+    const float *base = reinterpret_cast<const float *>((uintptr_t)x & ~(uintptr_t)15);
+    g->rows_delta = (int)(x - base);
+    g->rows_plane = plane;
+    g->a_mn = 1;
+    g->gather = 0;
+    g->box = 0;
+    g->rows = 1;
+    // each page as one flat row of channels * plane floats (+ the slack),
+    // loaded in boxes of kRowsPitch floats
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)((long long)K * plane + g->rows_delta),
+                                (cuuint64_t)batch};
+    // (one page: any 16-byte multiple at least the row length)
+    const cuuint64_t page_bytes =
+        x_bs > 0 ? (cuuint64_t)(x_bs * 4) : (dims[0] * 4 + 15) / 16 * 16;
+    const cuuint64_t strides[1] = {page_bytes};
+    const cuuint32_t box[2] = {kRowsBox, 1};
+    const cuuint32_t es[2] = {1, 1};
+    if (fn(&g->tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides,
+           box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    g->ok = encode_b(g, Bhi, Blo, K);
+    if (g->ok) encode_c(g);
+    return g->ok;
+}
+
 Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     if (!g.ok || g.epi.act < 0 || g.epi.act > 3) return ERR_SHAPE;
+    // per device, once: the kernels' register count is checked and their
+    // shared-memory limit raised (under a mutex: host threads may launch
+    // their first GEMMs on a device together)
+    static std::mutex mu;
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr[dev]) {
-        const void *fns[4] = {(const void *)tc_gemm_kernel<0>, (const void *)tc_gemm_kernel<1>,
-                              (const void *)tc_gemm_kernel<2>, (const void *)tc_gemm_kernel<3>};
-        for (const void *f : fns) {
-            // the setmaxnreg split needs exactly kLaunchRegs per thread at launch
-            cudaFuncAttributes fa;
-            if (cudaFuncGetAttributes(&fa, f) != cudaSuccess || fa.numRegs != kLaunchRegs ||
-                cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kSmemMax) != cudaSuccess) {
-                cudaGetLastError();
-                return ERR_CUDA;
+    if (dev < 0 || dev >= 64) return ERR_CUDA;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr[dev]) {
+            const void *fns[12] = {
+                (const void *)tc_gemm_kernel<0, kModeTile>, (const void *)tc_gemm_kernel<1, kModeTile>,
+                (const void *)tc_gemm_kernel<2, kModeTile>, (const void *)tc_gemm_kernel<3, kModeTile>,
+                (const void *)tc_gemm_kernel<0, kModeBox>,  (const void *)tc_gemm_kernel<1, kModeBox>,
+                (const void *)tc_gemm_kernel<2, kModeBox>,  (const void *)tc_gemm_kernel<3, kModeBox>,
+                (const void *)tc_gemm_kernel<0, kModeRows>, (const void *)tc_gemm_kernel<1, kModeRows>,
+                (const void *)tc_gemm_kernel<2, kModeRows>, (const void *)tc_gemm_kernel<3, kModeRows>};
+            for (const void *f : fns) {
+                // the setmaxnreg split needs exactly kLaunchRegs per thread at launch
+                cudaFuncAttributes fa;
+                if (cudaFuncGetAttributes(&fa, f) != cudaSuccess || fa.numRegs != kLaunchRegs ||
+                    cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemMax) != cudaSuccess) {
+                    cudaGetLastError();
+                    return ERR_CUDA;
+                }
             }
+            attr[dev] = true;
         }
-        attr[dev] = true;
     }
     Args a;
     a.M = g.M; a.N = g.N; a.K = g.K; a.batch = g.batch; a.planes = g.planes;
@@ -1212,8 +1606,27 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     a.gather = g.gather;
     a.tma_c = g.tma_c;
     a.gg = g.gg;
-    a.stage_bytes = kABytes + 2 * 128 * g.bn;
-    a.tx_bytes = (g.gather ? 0 : kABytes) + 2 * 128 * g.bn;
+    a.box = g.box;
+    a.cb = g.cb;
+    if (!g.box) a.cb.nbox = 1;  // the window ring is unused
+    a.rows = g.rows;
+    a.rows_plane = g.rows_plane;
+    a.rows_offmul = (int)(g.rows_plane & 3);
+    a.rows_delta = g.rows_delta;
+    const uint32_t b_bytes = 2u * 128u * (uint32_t)g.bn;
+    if (g.box) {
+        a.stage_bytes = b_bytes;
+        a.tx_bytes = b_bytes;
+    } else if (g.rows) {
+        a.stage_bytes = kRowsBytes + b_bytes;
+        a.tx_bytes = 32u * kRowsBox * 4u + b_bytes;
+    } else {
+        a.stage_bytes = kABytes + b_bytes;
+        a.tx_bytes = (g.gather ? 0 : kABytes) + b_bytes;
+    }
+    a.staging_off = (uint32_t)g.stages * a.stage_bytes +
+                    (g.box ? (uint32_t)g.cb.nbox * g.cb.box_bytes : 0u);
+    if ((size_t)kCtrlBytes + a.staging_off + kStagingBytes > g.smem) return ERR_SHAPE;
     // FP32 accumulate, TF32 A and B, both K-major (A comes from TMEM), N, M
     a.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(g.bn >> 3) << 17) |
               ((uint32_t)(kBM >> 4) << 24);
@@ -1221,22 +1634,28 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     int grid = sm_count();
     if (g.max_ctas > 0 && grid > g.max_ctas) grid = g.max_ctas;
     if (grid > g.tiles) grid = g.tiles;
-    switch (g.epi.act) {
-        case ACT_RELU:
-            tc_gemm_kernel<ACT_RELU><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo,
-                                                                     g.tmC, a);
-            break;
-        case ACT_SILU:
-            tc_gemm_kernel<ACT_SILU><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo,
-                                                                     g.tmC, a);
-            break;
-        case ACT_GELU:
-            tc_gemm_kernel<ACT_GELU><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo,
-                                                                     g.tmC, a);
-            break;
+    const int mode = g.box ? kModeBox : (g.rows ? kModeRows : kModeTile);
+    switch (mode * 4 + g.epi.act) {
+#define PPDL_TC_CASE(M_, A_)                                                                  \
+    case M_ * 4 + A_:                                                                      \
+        tc_gemm_kernel<A_, M_><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo, g.tmC, \
+                                                               a);                          \
+        break;
+        PPDL_TC_CASE(kModeTile, ACT_NONE)
+        PPDL_TC_CASE(kModeTile, ACT_RELU)
+        PPDL_TC_CASE(kModeTile, ACT_SILU)
+        PPDL_TC_CASE(kModeTile, ACT_GELU)
+        PPDL_TC_CASE(kModeBox, ACT_NONE)
+        PPDL_TC_CASE(kModeBox, ACT_RELU)
+        PPDL_TC_CASE(kModeBox, ACT_SILU)
+        PPDL_TC_CASE(kModeBox, ACT_GELU)
+        PPDL_TC_CASE(kModeRows, ACT_NONE)
+        PPDL_TC_CASE(kModeRows, ACT_RELU)
+        PPDL_TC_CASE(kModeRows, ACT_SILU)
+        PPDL_TC_CASE(kModeRows, ACT_GELU)
+#undef PPDL_TC_CASE
         default:
-            tc_gemm_kernel<ACT_NONE><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo,
-                                                                     g.tmC, a);
+            return ERR_SHAPE;
     }
     return cuda_status();
 }

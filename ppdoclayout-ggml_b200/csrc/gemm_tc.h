@@ -41,6 +41,40 @@ struct TcGather {
     int KS = 1, S = 1, P = 0, H = 0, W = 0, OW = 0;
 };
 
+// Implicit convolution fed by TMA boxes of the CHW input (no im2col, no
+// per-element gather).  The output is tiled in 4 rows x 32 columns; for
+// each kernel row kh and block of CB input channels one TMA box brings the
+// input window of the tile (32*S + KS + alignment columns, 4 rows at the
+// conv stride, CB channels; zero outside the image) into shared memory, and
+// the converter warps read the A rows of all KS kernel columns from it.
+// K order of the repacked weight (launch_tf32_split_box): box
+// bx = cb*KS + kh, inside a box k = kw*CB + c, each box padded to
+// kbpb k-blocks of 32.  Needs W % 4 == 0 (16-byte input rows), S in {1, 2}
+// and, for S = 2, an even H (rows are addressed as (H/2, parity) pairs).
+struct TcConvBox {
+    const float *x = nullptr;
+    long long x_bs = 0;   // page stride (elements)
+    int IC = 0, H = 0, W = 0, KS = 1, S = 1, P = 0, OH = 0, OW = 0;
+    // derived by the planner
+    int CB = 32, kbpb = 1, nbx = 1, Wb = 0, o = 0, tiles_x = 0, tiles_y = 0, nbox = 2;
+    uint32_t box_bytes = 0;  // window slot in shared memory (1024-byte multiple)
+    uint32_t box_tx = 0;     // bytes one window load transfers (Wb * 4 * 32 * 4)
+};
+
+// Channels per window (32: channels past IC are zero-filled by TMA) and
+// k-blocks per window (one per kernel column); the repacked weight has
+// nbx * kbpb * 32 columns, nbx = ceil(IC / 32) * KS windows.
+inline void tc_conv_box_blocks(int IC, int KS, int *CB, int *kbpb, int *nbx) {
+    *CB = 32;
+    *kbpb = KS;
+    *nbx = (IC + 31) / 32 * KS;
+}
+inline int tc_conv_box_kdim(int IC, int KS) {
+    int cb, kbpb, nbx;
+    tc_conv_box_blocks(IC, KS, &cb, &kbpb, &nbx);
+    return nbx * kbpb * 32;
+}
+
 struct TcGemm {
     CUtensorMap tmA, tmBhi, tmBlo;
     CUtensorMap tmC;     // output stored by TMA: tma_c 1 = CHW, 2 = token-major rows
@@ -49,6 +83,11 @@ struct TcGemm {
     int a_mn = 1;        // 1: A is M-major (128B-base-32B swizzle), 0: K-major
     int gather = 0;      // 1: A gathered by the converter warps (conv geometry gg)
     TcGather gg;
+    int box = 0;         // 1: implicit conv from TMA boxes of the input (geometry cb)
+    TcConvBox cb;
+    int rows = 0;        // 1: M-major A loaded as 32 channel rows per k-block (rows_plane)
+    long long rows_plane = 0;
+    int rows_delta = 0;
     int bn = 128;        // N tile
     int stages = 2;
     size_t smem = 0;
@@ -80,6 +119,28 @@ bool tc_gemm_plan_gather(TcGemm *g, int M, int N, int K, int batch, const TcGath
 bool tc_gemm_plan(TcGemm *g, int M, int N, int K, int batch, const float *A, int a_mn,
                   long long lda, long long a_bs, const float *Bhi, const float *Blo, int planes,
                   const TcEpilogue &epi);
+
+// Plan a conv in box mode (see TcConvBox): M = OH*OW per page, N = OC,
+// batch = pages, B hi/lo: the weight repacked by launch_tf32_split_box.  The
+// epilogue addresses C(m = oy*OW + ox, n = channel).  False when the
+// geometry is outside the mode (the caller then keeps another path).
+bool tc_gemm_plan_box(TcGemm *g, int N, int batch, const TcConvBox &cb, const float *Bhi,
+                      const float *Blo, const TcEpilogue &epi);
+
+// Plan a GEMM whose M-major A (a CHW activation, A(m, k) = x[z][k][m]) has
+// channel rows that TMA cannot describe as one tensor (plane stride or base
+// not 16-byte aligned, e.g. 25 x 25 planes): every k-block is loaded as 32
+// per-channel TMA rows of 132 floats starting at the 16-byte boundary below
+// the row (each in a 160-float slot, 128-byte aligned), and the converter
+// indexes past the alignment remainder.
+bool tc_gemm_plan_rows(TcGemm *g, int M, int N, int K, int batch, const float *x, long long plane,
+                       long long x_bs, const float *Bhi, const float *Blo, const TcEpilogue &epi,
+                       int planes = 1);
+
+// Repack and split a conv weight [OC][IC][KS][KS] into the box-mode K order
+// (hi/lo rows of tc_conv_box_kdim(IC, KS) floats, zero where no tap/channel).
+Status launch_tf32_split_box(const float *w, float *hi, float *lo, int OC, int IC, int KS,
+                             cudaStream_t st);
 
 Status launch_tc_gemm(const TcGemm &g, cudaStream_t st);
 

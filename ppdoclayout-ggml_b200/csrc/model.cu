@@ -10,7 +10,8 @@
 //   * every conv goes through conv() — the reference's builder::conv
 //     dispatch (src/ppdoclayout.cpp:388-543): depthwise -> direct kernel;
 //     1x1 -> GEMM writing CHW (bias + activation fused); k3-s1-p1 ->
-//     Winograd F(4,3); k3-s2 and k2 -> implicit GEMM (no im2col);
+//     Winograd F(4,3); k3-s2 and k2 -> implicit GEMM fed by TMA windows of
+//     the input (no im2col buffer);
 //   * concatenations are free: producers write straight into channel
 //     slices of the consumer's buffer (HG-block aggregation, CCFM/PAN
 //     concats), and residual adds ride in the producing epilogue;
@@ -174,37 +175,57 @@ public:
     static bool tc_shape_ok(const float *p, long long plane, long long bs, int K) {
         return ((uintptr_t)p & 15) == 0 && plane % 4 == 0 && bs % 4 == 0 && K % 4 == 0;
     }
-    // Tensor-core conv through im2col: the operand is packed into the shared A
-    // scratch as [Kp][Mp] rows (M-major, 16-byte rows; for a 1x1 conv a plane
-    // copy into padded rows), then the TMA-fed GEMM runs on it.  Used for the
-    // k3-s2 / k2 convs and for 1x1 convs whose planes break the TMA stride
-    // rule.  Returns a null plan (caller keeps the SIMT GEMM) when the
-    // packed operand cannot be described.
-    std::shared_ptr<TcGemm> plan_conv_im2col(const V &x, int K, int s, int p, int OC, int OH,
-                                             int OW, const float *wp, const TcEpilogue &e,
-                                             const std::string &name) {
-        const int Kc = x.C * K * K, Kp = (Kc + 3) / 4 * 4, M = OH * OW;
-        const long long Mp = (M + 3) / 4 * 4;
-        if (Kp > 65535 || !ok) return nullptr;
-        float *hi = dalloc((long long)OC * Kp), *lo = dalloc((long long)OC * Kp);
+    // Tensor-core conv of a k3-s2 / k2 kernel read straight from the CHW
+    // input (implicit GEMM, no im2col buffer): TMA windows of the input
+    // (box mode) when its rows are 16-byte multiples, else the converter
+    // warps' gather.  Returns a null plan when neither applies (the caller
+    // keeps the SIMT GEMM).
+    std::shared_ptr<TcGemm> plan_conv_implicit(const V &x, int K, int s, int p, int OC, int OH,
+                                               int OW, const float *wp, const TcEpilogue &e) {
         if (!ok) return nullptr;
+        auto g = std::make_shared<TcGemm>();
+        TcConvBox cb;
+        cb.x = x.p; cb.x_bs = x.bs;
+        cb.IC = x.C; cb.H = x.H; cb.W = x.W; cb.KS = K; cb.S = s; cb.P = p;
+        cb.OH = OH; cb.OW = OW;
+        const int Kb = tc_conv_box_kdim(x.C, K);
+        float *hi = dalloc((long long)OC * Kb), *lo = dalloc((long long)OC * Kb);
+        if (!ok) return nullptr;
+        if (tc_gemm_plan_box(g.get(), OC, Bmax, cb, hi, lo, e)) {
+            if (launch_tf32_split_box(wp, hi, lo, OC, x.C, K, st) != OK) {
+                fail("weight split failed");
+                return nullptr;
+            }
+            return g;
+        }
+        // gather: B = the raw weight rows [OC][IC*K*K] padded to 16 bytes
+        const int Kc = x.C * K * K, Kp = (Kc + 3) / 4 * 4;
+        if ((long long)Kp > Kb) {
+            hi = dalloc((long long)OC * Kp);
+            lo = dalloc((long long)OC * Kp);
+            if (!ok) return nullptr;
+        }
+        TcGather gg;
+        gg.x = x.p; gg.x_bs = x.bs; gg.plane = x.plane();
+        gg.KS = K; gg.S = s; gg.P = p; gg.H = x.H; gg.W = x.W; gg.OW = OW;
+        if (!tc_gemm_plan_gather(g.get(), OH * OW, OC, Kc, Bmax, gg, hi, lo, e)) return nullptr;
         if (launch_tf32_split_pad(wp, hi, lo, OC, Kc, Kp, st) != OK) {
             fail("weight split failed");
             return nullptr;
         }
-        const int ss = scratch;
-        wg_dt_ns[ss] = std::max(wg_dt_ns[ss], (long long)Kp * Mp * Bmax);
+        return g;
+    }
+    // Tensor-core 1x1 conv on planes that TMA cannot take as one tensor
+    // (H*W not a multiple of 4, e.g. 25 x 25): A is loaded as per-channel
+    // TMA rows (rows mode).  Null plan when even that does not apply.
+    std::shared_ptr<TcGemm> plan_conv1x1_rows(const V &x, int OC, const float *wp,
+                                              const TcEpilogue &e) {
+        if (!ok || x.C % 4) return nullptr;
+        const Split wsp = split(wp, (long long)OC * x.C);
         auto g = std::make_shared<TcGemm>();
-        finalizers.push_back([=]() {
-            if (!tc_gemm_plan(g.get(), M, OC, Kp, Bmax, wg_dt_s[ss], 1, Mp, (long long)Kp * Mp,
-                              hi, lo, 1, e))
-                g->ok = false;
-        });
-        push(name + ".im2col", PPDL_STEP_IM2COL, 0.0,
-             4.0 * ((double)x.C * x.plane() + (double)Kp * Mp), [=]() {
-            return launch_im2col(x.p, x.bs, x.plane(), wg_dt_s[ss], (long long)Kp * Mp, Kc, Kp, x.H,
-                                 x.W, K, s, p, OW, M, (int)Mp, nb, st);
-        });
+        if (!ok || !tc_gemm_plan_rows(g.get(), (int)x.plane(), OC, x.C, Bmax, x.p, x.plane(), x.bs,
+                                      wsp.hi, wsp.lo, e))
+            return nullptr;
         return g;
     }
     // conv epilogue writing a CHW view
@@ -405,12 +426,11 @@ public:
                     return;
                 }
             } else if (use_tc) {
-                auto g = plan_conv_im2col(x, 1, 1, 0, OC, OH, OW, wp,
-                                          chw_epilogue(y, bp, act, res, res_mode), name);
+                auto g = plan_conv1x1_rows(x, OC, wp, chw_epilogue(y, bp, act, res, res_mode));
                 if (g) {
                     push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * OH * OW * IC,
                          4.0 * ((double)IC * x.plane() + (double)OC * OH * OW),
-                         [=]() { return g->ok ? run_tc(g, 0) : ERR_SHAPE; });
+                         [=]() { return run_tc(g, 0); });
                     return;
                 }
             }
@@ -481,14 +501,14 @@ public:
             });
             return;
         }
-        // k3-s2 / k2: implicit GEMM
+        // k3-s2 / k2: implicit GEMM on the CHW input (no im2col buffer)
         if (use_tc) {
-            auto g = plan_conv_im2col(x, K, s, p, OC, OH, OW, wp,
-                                      chw_epilogue(y, bp, act, res, res_mode), name);
+            auto g = plan_conv_implicit(x, K, s, p, OC, OH, OW, wp,
+                                        chw_epilogue(y, bp, act, res, res_mode));
             if (g) {
                 push(name, PPDL_STEP_GEMM_IMPLICIT, 2.0 * OC * OH * OW * IC * K * K,
                      4.0 * ((double)IC * x.plane() + (double)OC * OH * OW),
-                     [=]() { return g->ok ? run_tc(g, 0) : ERR_SHAPE; });
+                     [=]() { return run_tc(g, 0); });
                 return;
             }
         }
@@ -534,11 +554,10 @@ public:
                 return;
             }
         } else if (use_tc) {
-            auto g = plan_conv_im2col(x, 1, 1, 0, OC, x.H, x.W, wp, e, name);
+            auto g = plan_conv1x1_rows(x, OC, wp, e);
             if (g) {
                 push(name, PPDL_STEP_GEMM_1X1, 2.0 * OC * x.plane() * IC,
-                     4.0 * ((double)IC + OC) * x.plane(),
-                     [=]() { return g->ok ? run_tc(g, 0) : ERR_SHAPE; });
+                     4.0 * ((double)IC + OC) * x.plane(), [=]() { return run_tc(g, 0); });
                 return;
             }
         }

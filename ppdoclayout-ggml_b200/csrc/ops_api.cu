@@ -67,6 +67,8 @@ PPDL_OPS_API int ppdl_op_supported(const ppdl_op_desc *d) {
 
 PPDL_OPS_API const char *ppdl_op_last_error(void) { return g_err; }
 
+PPDL_OPS_API int ppdl_op_device_error(void) { return ppdl::tc_error_fetch_and_clear() ? 1 : 0; }
+
 PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float *A, int a_m_major,
                                   long long lda, long long a_bs, const float *B, float *b_split,
                                   float *C, long long ldc_m, long long ldc_n, long long c_bs,
@@ -81,9 +83,12 @@ PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float *A
     ppdl::TcEpilogue e;
     e.C = C; e.ldc_m = ldc_m; e.ldc_n = ldc_n; e.c_bs = c_bs;
     ppdl::TcGemm g;
-    if (!ppdl::tc_gemm_plan(&g, M, N, K, batch, A, a_m_major ? 1 : 0, lda, a_bs, hi, lo, 1, e))
-        return fail(PPDL_ERR_SHAPE, "gemm: operands violate the TMA rules (16-byte alignment, "
-                                    "strides and K multiples of 4)");
+    // an M-major A whose channel rows TMA cannot take as one tensor (lda or
+    // the base not 16-byte aligned, e.g. 25 x 25 planes) is loaded row by row
+    if (!ppdl::tc_gemm_plan(&g, M, N, K, batch, A, a_m_major ? 1 : 0, lda, a_bs, hi, lo, 1, e) &&
+        !(a_m_major && ppdl::tc_gemm_plan_rows(&g, M, N, K, batch, A, lda, a_bs, hi, lo, e)))
+        return fail(PPDL_ERR_SHAPE, "gemm: operands violate the TMA rules (16-byte aligned "
+                                    "b_split and a_bs, K a multiple of 4; K-major A also lda)");
     return to_status(ppdl::launch_tc_gemm(g, st));
 }
 
@@ -101,6 +106,12 @@ PPDL_OPS_API int ppdl_depthwise_conv2d(const float *x, int batch, int C, int H, 
                                          batch, (cudaStream_t)stream));
 }
 
+PPDL_OPS_API long long ppdl_conv2d_tf32x3_workspace(int IC, int OC, int K) {
+    if (IC <= 0 || OC <= 0 || K <= 0) return 0;
+    const long long kp = (IC * K * K + 3) / 4 * 4, kb = ppdl::tc_conv_box_kdim(IC, K);
+    return 2LL * OC * (kp > kb ? kp : kb);
+}
+
 PPDL_OPS_API int ppdl_conv2d_tf32x3(const float *x, int batch, int IC, int H, int W,
                                     long long x_bs, const float *weight, const float *bias,
                                     int OC, int K, int S, int P, int OH, int OW, int act,
@@ -114,22 +125,85 @@ PPDL_OPS_API int ppdl_conv2d_tf32x3(const float *x, int batch, int IC, int H, in
     if ((long long)(OH - 1) * S - P >= H || (long long)(OW - 1) * S - P >= W ||
         (long long)OH * OW >= (1LL << 31))
         return fail(PPDL_ERR_SHAPE, "conv2d: output %dx%d larger than the input allows", OH, OW);
-    const int Kc = IC * K * K, Kp = (Kc + 3) / 4 * 4;
     cudaStream_t st = (cudaStream_t)stream;
-    float *hi = b_split, *lo = b_split + (long long)OC * Kp;
     ppdl::TcEpilogue e;
     e.C = y; e.ldc_m = 1; e.ldc_n = (long long)OH * OW; e.c_bs = y_bs;
     e.bias = bias; e.act = act;
+    ppdl::TcGemm g;
+    // the forward's path: TMA windows of the input when its rows are 16-byte
+    // multiples (K > 1), else the converter warps' gather
+    if (K > 1) {
+        ppdl::TcConvBox cb;
+        cb.x = x; cb.x_bs = x_bs;
+        cb.IC = IC; cb.H = H; cb.W = W; cb.KS = K; cb.S = S; cb.P = P; cb.OH = OH; cb.OW = OW;
+        const int Kb = ppdl::tc_conv_box_kdim(IC, K);
+        float *hi = b_split, *lo = b_split + (long long)OC * Kb;
+        if (ppdl::tc_gemm_plan_box(&g, OC, batch, cb, hi, lo, e)) {
+            const ppdl::Status s = ppdl::launch_tf32_split_box(weight, hi, lo, OC, IC, K, st);
+            if (s != ppdl::OK) return to_status(s);
+            return to_status(ppdl::launch_tc_gemm(g, st));
+        }
+    }
+    const int Kc = IC * K * K, Kp = (Kc + 3) / 4 * 4;
+    float *hi = b_split, *lo = b_split + (long long)OC * Kp;
     ppdl::TcGather gg;
     gg.x = x; gg.x_bs = x_bs; gg.plane = (long long)H * W;
     gg.KS = K; gg.S = S; gg.P = P; gg.H = H; gg.W = W; gg.OW = OW;
-    ppdl::TcGemm g;
     if (!ppdl::tc_gemm_plan_gather(&g, OH * OW, OC, Kc, batch, gg, hi, lo, e))
         return fail(PPDL_ERR_SHAPE, "conv2d: geometry outside the gather (K 1..8, P < K, "
                                     "1x1 only with S=1 P=0) or misaligned b_split");
     const ppdl::Status s = ppdl::launch_tf32_split_pad(weight, hi, lo, OC, Kc, Kp, st);
     if (s != ppdl::OK) return to_status(s);
     return to_status(ppdl::launch_tc_gemm(g, st));
+}
+
+namespace {
+// Winograd F(4,3) conv workspace, in floats, each part a multiple of 4:
+// wg4 [36][IC][OC], hi / lo [36][OC][IC], dt [B*36][IC][Tp], yt [B*36][OC][Tp]
+struct Wg4Parts {
+    long long wg4, split, dt, yt;
+};
+Wg4Parts wg4_parts(int batch, int IC, int OC, int H, int W) {
+    const long long T = (long long)((W + 3) / 4) * ((H + 3) / 4), Tp = (T + 3) / 4 * 4;
+    return {36LL * IC * OC, 36LL * IC * OC, 36LL * batch * IC * Tp, 36LL * batch * OC * Tp};
+}
+}  // namespace
+
+PPDL_OPS_API long long ppdl_conv3x3_wg4_workspace(int batch, int IC, int OC, int H, int W) {
+    if (batch <= 0 || IC <= 0 || OC <= 0 || H <= 0 || W <= 0) return 0;
+    const Wg4Parts q = wg4_parts(batch, IC, OC, H, W);
+    return q.wg4 + 2 * q.split + q.dt + q.yt;
+}
+
+PPDL_OPS_API int ppdl_conv3x3_wg4_tf32x3(const float *x, int batch, int IC, int H, int W,
+                                         long long x_bs, const float *weight, const float *bias,
+                                         int OC, int act, float *work, float *y, long long y_bs,
+                                         void *stream) {
+    g_err[0] = 0;
+    if (!x || !weight || !work || !y || batch <= 0 || IC <= 0 || OC <= 0 || H <= 0 || W <= 0 ||
+        act < 0 || act > 3)
+        return fail(PPDL_ERR_SHAPE, "conv3x3: bad sizes, activation or null pointer");
+    if (IC % 4 || ((uintptr_t)work & 15))
+        return fail(PPDL_ERR_SHAPE, "conv3x3: IC must be a multiple of 4 and the workspace "
+                                    "16-byte aligned");
+    cudaStream_t st = (cudaStream_t)stream;
+    const int TW = (W + 3) / 4, TH = (H + 3) / 4, T = TW * TH, Tp = (T + 3) / 4 * 4;
+    const Wg4Parts q = wg4_parts(batch, IC, OC, H, W);
+    float *wg4 = work, *hi = wg4 + q.wg4, *lo = hi + q.split, *dt = lo + q.split, *yt = dt + q.dt;
+    ppdl::TcEpilogue e;
+    e.C = yt; e.ldc_m = 1; e.ldc_n = Tp; e.c_bs = (long long)OC * Tp;
+    ppdl::TcGemm g;
+    if (!ppdl::tc_gemm_plan(&g, T, OC, IC, batch * 36, dt, 1, Tp, (long long)IC * Tp, hi, lo, 36,
+                            e))
+        return fail(PPDL_ERR_SHAPE, "conv3x3: the plane GEMM cannot be planned");
+    ppdl::Status s = ppdl::launch_wg4_filter(weight, wg4, IC, OC, st);
+    if (s == ppdl::OK) s = ppdl::launch_wg4_kmajor_split(wg4, hi, lo, IC, OC, st);
+    if (s == ppdl::OK) s = ppdl::launch_wg4_input(x, x_bs, dt, IC, H, W, TW, TH, 1, batch, st, Tp);
+    if (s == ppdl::OK) s = ppdl::launch_tc_gemm(g, st);
+    if (s == ppdl::OK)
+        s = ppdl::launch_wg4_output(yt, bias, y, y_bs, nullptr, 0, 0, OC, H, W, TW, TH, act,
+                                    batch, st, Tp);
+    return to_status(s);
 }
 
 PPDL_OPS_API int ppdl_op_launch(const ppdl_op_desc *d, void *stream_ptr) {

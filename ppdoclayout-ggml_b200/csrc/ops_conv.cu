@@ -9,13 +9,25 @@
 //   op 12 36-plane madd with ".wg4" (36, IC, OC)
 //   op 11 output transform + bias + act
 // The ggml ne[3] (ne[2] for the plane tensors' page count) carries pages.
+//
+// Ops 3 and 12 run on the 3xTF32 tensor-core GEMM.  A hook sees only its
+// node's tensors and cannot allocate, so the TF32 halves of the weight go to
+// the library's static split array (the one ppdl_gemm_tf32x3_static uses,
+// 2^21 weights per half) in chunks of output channels (op 3) or Winograd
+// planes (op 12), each chunk split and multiplied in stream order; calls
+// whose GPU work overlaps on one device race on that array.  A GEMM whose
+// operands TMA cannot describe (IC not a multiple of 4) keeps the SIMT
+// FFMA GEMM.
 #include <cstdio>
 
 #include "conv.h"
 #include "gemm.h"
+#include "gemm_tc.h"
 #include "ops_internal.h"
 
 namespace ppdl {
+
+float *static_split_workspace(long long *cap);
 
 namespace {
 
@@ -28,6 +40,69 @@ int code(Status s) {
         case ERR_SHAPE: return PPDL_ERR_SHAPE;
         default: return PPDL_ERR_CUDA;
     }
+}
+
+// C[z](m, n) for n in [0, N) as chunks of output columns whose split
+// weights fit the static array; w points at the weight with element
+// (plane p, k, n) at w[p * pstride + k * ldw + n] (the ggml ".wr"/".wg4"
+// layouts), A: M-major, one z per (page, plane).  Returns false (nothing
+// launched) when the shapes cannot use the tensor cores.
+bool tc_chunked(const float *A, int M, int K, long long lda, long long a_bs, int planes, int pages,
+                const float *w, long long ldw, long long pstride, int N, float *C,
+                long long ldc_n, long long c_bs, cudaStream_t st, Status *out) {
+    long long cap = 0;
+    float *ws = static_split_workspace(&cap);
+    if (!ws || K % 4) return false;
+    float *hi = ws, *lo = ws + cap;
+    // chunk: all output columns of as many planes as fit, else the columns
+    // of one plane in multiples of 16
+    const long long per_plane = (long long)N * K;
+    int pc = (int)(cap / per_plane);
+    int nc = N;
+    if (pc < 1) {
+        pc = 1;
+        nc = (int)(cap / K) / 16 * 16;
+        if (nc < 16) return false;
+    }
+    if (pc > planes) pc = planes;
+    // plan every chunk before launching anything
+    struct Chunk { int p0, np, n0, nn, b; };
+    const int n_pchunks = (planes + pc - 1) / pc, n_nchunks = (N + nc - 1) / nc;
+    for (int pi = 0; pi < n_pchunks; pi++)
+        for (int ni = 0; ni < n_nchunks; ni++) {
+            const int p0 = pi * pc, np = planes - p0 < pc ? planes - p0 : pc;
+            const int n0 = ni * nc, nn = N - n0 < nc ? N - n0 : nc;
+            // one split of the chunk's weights, then one GEMM per page (the
+            // planes of a page are consecutive z)
+            if (launch_kmajor_split(w + (long long)p0 * pstride + n0, hi, lo, np, K, (int)ldw,
+                                    pstride, nn, st) != OK) {
+                *out = ERR_CUDA;
+                return true;
+            }
+            for (int b = 0; b < pages; b++) {
+                const long long z0 = (long long)b * planes + p0;
+                TcEpilogue e;
+                e.C = C + z0 * c_bs + (long long)n0 * ldc_n;
+                e.ldc_m = 1; e.ldc_n = ldc_n; e.c_bs = c_bs;
+                TcGemm g;
+                const float *Az = A + z0 * a_bs;
+                if (!tc_gemm_plan(&g, M, nn, K, np, Az, 1, lda, a_bs, hi, lo, np, e) &&
+                    !tc_gemm_plan_rows(&g, M, nn, K, np, Az, lda, a_bs, hi, lo, e, np)) {
+                    // only the first chunk can fail (same strides for all):
+                    // nothing has been multiplied yet
+                    if (pi == 0 && ni == 0 && b == 0) return false;
+                    *out = ERR_SHAPE;
+                    return true;
+                }
+                const Status s = launch_tc_gemm(g, st);
+                if (s != OK) {
+                    *out = s;
+                    return true;
+                }
+            }
+        }
+    *out = OK;
+    return true;
 }
 
 }  // namespace
@@ -59,6 +134,16 @@ bool ops_ext_launch(const ppdl_op_desc *d, cudaStream_t st, int *status, char *e
             if (dst.ne[0] != IW || dst.ne[1] != IH || dst.ne[3] != B || s1.ne[0] != OC ||
                 s1.ne[1] != IC || nel(s1) != OC * IC)
                 return bad("op 3: x / .wr / dst shapes disagree");
+            {
+                // tensor cores: A = x (pixels x channels, M-major), B(oc, ic) = wr[ic][oc]
+                Status ts = OK;
+                if (tc_chunked((const float *)s0.data, (int)(IW * IH), (int)IC, IW * IH,
+                               IW * IH * IC, 1, (int)B, (const float *)s1.data, OC, 0, (int)OC,
+                               (float *)dst.data, IW * IH, IW * IH * OC, st, &ts)) {
+                    *status = code(ts);
+                    return true;
+                }
+            }
             GemmArgs g;  // dst[oc][p] = sum_ic wr[ic][oc] x[ic][p]
             g.M = (int)OC; g.N = (int)(IW * IH); g.K = (int)IC; g.batch = (int)B;
             g.A = {(const float *)s1.data, 1, OC};
@@ -108,6 +193,17 @@ bool ops_ext_launch(const ppdl_op_desc *d, cudaStream_t st, int *status, char *e
             if (s0.ne[0] != T || s0.ne[2] != 36 || s0.ne[3] != B || dst.ne[2] != 36 ||
                 s1.ne[0] != OC || s1.ne[1] != IC || s1.ne[2] != 36)
                 return bad("op 12: dt / .wg4 / yt shapes disagree");
+            {
+                // tensor cores, per plane p: A(t, ic) = dt[b][p][ic][t],
+                // B(oc, ic) = wg4[p][ic][oc], yt[b][p][oc][t]
+                Status ts = OK;
+                if (tc_chunked((const float *)s0.data, (int)T, (int)IC, T, IC * T, 36, (int)B,
+                               (const float *)s1.data, OC, IC * OC, (int)OC, (float *)dst.data, T,
+                               OC * T, st, &ts)) {
+                    *status = code(ts);
+                    return true;
+                }
+            }
             GemmArgs g;
             g.M = (int)OC; g.N = (int)T; g.K = (int)IC; g.batch = (int)(B * 36);
             g.A = {(const float *)s1.data, 1, OC, 36, 0, IC * OC};

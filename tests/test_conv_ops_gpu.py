@@ -4,7 +4,10 @@
 The oracle's direct conv accumulates in double, so it is an
 algorithm-independent reference for the GEMM, implicit-GEMM and Winograd
 paths; the Winograd stages are additionally compared stage by stage with the
-oracle's restatement of the reference transforms.  Gate: the hot path's
+oracle's restatement of the reference transforms.  Ops 3 and 12 run on the
+3xTF32 tensor-core GEMM (weights split into the library's static array in
+chunks; cases below exceed one chunk), op 12 with IC not a multiple of 4
+on the SIMT GEMM.  Gate: the hot path's
 per-op FP32 relative error, max|diff| / max|ref| <= 1e-5.
 """
 import numpy as np
@@ -34,7 +37,9 @@ def _wr(w):
 
 
 @pytest.mark.parametrize("B,IC,OC,H,W", [(1, 48, 64, 25, 25), (2, 37, 19, 13, 11),
-                                          (1, 512, 256, 50, 50)])
+                                          (1, 512, 256, 50, 50),
+                                          # 3.1M weights > the 2^21 split array: N chunks
+                                          (2, 2048, 1536, 13, 13)])
 def test_op3_conv1x1(cuda, orc, B, IC, OC, H, W):
     rng = np.random.default_rng(B * 1000 + IC)
     x = rng.standard_normal((B, IC, H, W), dtype=np.float32)
@@ -101,7 +106,9 @@ def test_winograd_known_answer_f43(cuda, orc):
 
 
 @pytest.mark.parametrize("H,W,IC,OC,act", [(25, 25, 64, 64, 2), (50, 50, 48, 48, 1),
-                                           (13, 11, 7, 5, 0), (100, 100, 128, 96, 1)])
+                                           (13, 11, 7, 5, 0), (100, 100, 128, 96, 1),
+                                           # 36 x 256 x 256 > the 2^21 split array: plane chunks
+                                           (25, 25, 256, 256, 1)])
 def test_winograd_stages_vs_oracle(cuda, orc, H, W, IC, OC, act):
     rng = np.random.default_rng(H * W + IC)
     B = 2

@@ -107,9 +107,16 @@ def test_tc_gemm_rejects_unaligned_strides(cuda):
     B = torch.zeros(32 * 64, device=cuda)
     ws = torch.zeros(2 * 32 * 64, device=cuda)
     Cc = torch.zeros(625 * 32, device=cuda)
-    # lda = 625 floats is not a 16-byte multiple: no TMA descriptor, clear error
-    st = L.ppdl_gemm_tf32x3(625, 32, 64, 1, A.data_ptr(), 1, 625, 625 * 64, B.data_ptr(),
-                            ws.data_ptr(), Cc.data_ptr(), 1, 625, 0,
+    # a K-major A with lda = 66 floats (not a 16-byte multiple): no TMA
+    # descriptor and no row-wise form for this layout, so a clear error (an
+    # M-major A with lda = 625 is loaded row by row and accepted)
+    st = L.ppdl_gemm_tf32x3(64, 32, 64, 1, A.data_ptr(), 0, 66, 66 * 64, B.data_ptr(),
+                            ws.data_ptr(), Cc.data_ptr(), 32, 1, 0,
                             torch.cuda.current_stream().cuda_stream)
     assert st == ppdl.PPDL_ERR_SHAPE
     assert "TMA" in ppdl.last_error()
+    # K not a multiple of 4: rejected for both layouts
+    st = L.ppdl_gemm_tf32x3(625, 32, 63, 1, A.data_ptr(), 1, 625, 625 * 64, B.data_ptr(),
+                            ws.data_ptr(), Cc.data_ptr(), 1, 625, 0,
+                            torch.cuda.current_stream().cuda_stream)
+    assert st == ppdl.PPDL_ERR_SHAPE

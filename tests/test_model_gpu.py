@@ -88,11 +88,8 @@ def test_raw_outputs_page0(gpu_out, ref_out):
     assert np.abs(od - r["order"]).max() / max(np.abs(r["order"]).max(), 1) < 1e-4
 
 
-@pytest.mark.parametrize("page", [0, 1])
-def test_dets_and_masks(gpu_out, ref_out, pages, page):
-    outs, _ = gpu_out
-    dets, masks = outs[page]
-    r = ref_out[page]
+def _check_page(dets, masks, r):
+    """The end-to-end gates of one page against the oracle's result r."""
     rd, rm = r["dets"], r["masks"].reshape(300, 200, 200)
     scores = rd[:, 1]
     n_checked = 0
@@ -102,7 +99,6 @@ def test_dets_and_masks(gpu_out, ref_out, pages, page):
         n_checked += 1
         assert dets[i, 0] == rd[i, 0], f"label row {i}"
         assert abs(dets[i, 1] - rd[i, 1]) < 1e-4, f"score row {i}"
-        h, w = pages[page][1]
         # box diff in pixels of the original image
         assert np.abs(dets[i, 2:6] - rd[i, 2:6]).max() <= 0.01, f"box row {i}"
         a, b = masks[i] != 0, rm[i] != 0
@@ -114,6 +110,33 @@ def test_dets_and_masks(gpu_out, ref_out, pages, page):
     assert n_checked >= 30, n_checked
     # the whole score column regardless of margins
     assert np.abs(dets[:, 1] - rd[:, 1]).max() < 1e-4
+
+
+@pytest.mark.parametrize("page", [0, 1])
+def test_dets_and_masks(gpu_out, ref_out, pages, page):
+    outs, _ = gpu_out
+    dets, masks = outs[page]
+    _check_page(dets, masks, ref_out[page])
+
+
+def test_batch8_bench_pages_graph_replay(cuda, gguf_path, ref_model):
+    """The benchmarked configuration: a context of capacity 8 (as bench.py's
+    forward workload), the 8 pages bench.py times on rank 0 (seeds
+    1000..1007, 800 x 800), run twice — the first call eager, the second a
+    replay of the captured CUDA graph — and every page of the replay held
+    to the end-to-end gates; eager and replay agree bit for bit."""
+    B = 8
+    ctx = ppdl.Context(gguf_path, max_batch=B)
+    imgs = np.stack([synth.synth_page(1000 + i) for i in range(B)])
+    hw = np.full((B, 2), 800, np.int32)
+    eager = ctx.infer_batch(imgs, hw)
+    replay = ctx.infer_batch(imgs, hw)
+    ctx.close()
+    for i in range(B):
+        np.testing.assert_array_equal(eager[i][0], replay[i][0])
+        np.testing.assert_array_equal(eager[i][1], replay[i][1])
+        r = ref_model.forward(imgs[i], 800, 800)
+        _check_page(replay[i][0], replay[i][1], r)
 
 
 def test_single_page_api_matches_batch(cuda, gguf_path, pages, gpu_out):

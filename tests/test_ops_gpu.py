@@ -69,6 +69,21 @@ def test_msdeform_canonical_config1(cuda, orc):
     np.testing.assert_allclose(got, exp, rtol=0, atol=1e-6)
 
 
+def test_msdeform_canonical_config1_b32(cuda, orc):
+    """Config 1 at the benchmarked size, B = 32 pages (bench.py's msda
+    workload recipe: value N(0,1), loc U[0,1], weights softmax(N(0,1)))."""
+    rng = np.random.default_rng(32)
+    B, nq = 32, 300
+    val = rng.standard_normal((B, 13125, 8, 32), dtype=np.float32)
+    loc = rng.uniform(0, 1, (B, nq, 8, 3, 4, 2)).astype(np.float32)
+    lg = rng.standard_normal((B, nq, 8, 12)).astype(np.float32)
+    w = np.exp(lg - lg.max(-1, keepdims=True))
+    w = (w / w.sum(-1, keepdims=True)).astype(np.float32)
+    got = _msda(cuda, val, loc.reshape(B, nq, 192), w.reshape(B, nq, 96), None, B, nq, canon=True)
+    exp = orc.msdeform_canon(val, loc, w)
+    np.testing.assert_allclose(got, exp, rtol=0, atol=1e-6)
+
+
 def test_mask_box_vs_golden(cuda, golden_dir):
     g = np.load(f"{golden_dir}/mask_box_s21.npz")
     ml = cases.mask_box_inputs(21)

@@ -5,11 +5,12 @@ only sees its own tensors; ggml's allocator owns all other device memory).
 Its split-weight workspace is a static device array of the library, shared
 by every call and keeping the last call's contents, so the test makes two
 calls in a row with different shapes and data and checks each result
-against ppdl_gemm_tf32x3 (caller-provided workspace) under the GEMM tests'
-gate, max|diff| / max|ref| <= 1e-5 (the two paths run the same arithmetic,
-so they agree far more closely).  This file is collected last so that a run
-stopping at the first failure has run every other test; it also passes on
-its own in a fresh process.
+against ppdl_gemm_tf32x3 (caller-provided workspace) and against a float64
+matmul of the same operands, both under the GEMM tests' gate,
+max|diff| / max|ref| <= 1e-5 (the two library paths run the same
+arithmetic, so they agree far more closely).  This file is collected last
+so that a run stopping at the first failure has run every other test; it
+also passes on its own in a fresh process.
 """
 import ctypes as C
 
@@ -33,6 +34,7 @@ def _lib():
     L.ppdl_gemm_tf32x3.restype = C.c_int
     L.ppdl_gemm_tf32x3_static.argtypes = common + tail
     L.ppdl_gemm_tf32x3_static.restype = C.c_int
+    L.ppdl_op_device_error.restype = C.c_int
     return L
 
 
@@ -61,10 +63,20 @@ def _run_pair(L, cuda, M, N, K, batch, a_m_major, seed):
                                    B.data_ptr(), got.data_ptr(), ldc_m, ldc_n, M * N, stream)
     assert st == ppdl.PPDL_OK, ppdl.last_error()
     torch.cuda.synchronize()
+    assert L.ppdl_op_device_error() == 0
     want, got = want.cpu().numpy(), got.cpu().numpy()
     assert np.isfinite(got).all()
     err = np.abs(got - want).max() / np.abs(want).max()
     assert err <= RTOL, err
+    # float64 product of the same operands: A(m, k) per the layout, B [N][K]
+    Ad = A.cpu().double()[:, :, :(M if a_m_major else K)]
+    Am = Ad.transpose(1, 2) if a_m_major else Ad           # [batch][M][K]
+    ref = Am @ B.cpu().double().T                          # [batch][M][N]
+    if a_m_major:
+        ref = ref.transpose(1, 2)                          # [batch][N][M]
+    ref = ref.numpy()
+    err64 = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err64 <= RTOL, err64
     return err
 
 
