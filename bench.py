@@ -432,14 +432,15 @@ def run_forward(args, world, rank, local, pg):
     st = torch.cuda.ExternalStream(ctx.stream_ptr(), device=dev)
     if args.capture_once:
         torch.cuda.synchronize(dev)
-        if ctx.infer_device(d_img.data_ptr(), B, hw) != 0 or ctx.sync() != 0:
+        if ctx.infer_device_bits(d_img.data_ptr(), B, hw) != 0 or ctx.sync() != 0:
             raise RuntimeError("forward failed")
         return None
 
     def step():
-        rc = ctx.infer_device(d_img.data_ptr(), B, hw)
+        # the forward with its own mask output (packed, 1 bit per pixel)
+        rc = ctx.infer_device_bits(d_img.data_ptr(), B, hw)
         if rc != 0:
-            raise RuntimeError(f"ppdl_infer_device returned {rc}")
+            raise RuntimeError(f"ppdl_infer_device_bits returned {rc}")
 
     for _ in range(args.warmup):
         step()
@@ -509,25 +510,48 @@ def run_forward(args, world, rank, local, pg):
         roof["algorithmic_bytes_per_launch"] = round(
             sum(s[4] for s in gsteps) * B / max(1, len(gsteps)))
 
-    # ---- e2e: ppdl_infer_batch with the pages in pinned host memory; the
-    # dets and int32 masks come back into the context's pinned buffers and
-    # are read there (views, no extra host copy)
+    # ---- e2e (headline): the pipelined public API, ppdl_submit_batch /
+    # ppdl_wait_batch, with the pages in pinned host memory and the dets and
+    # packed masks read back into the context's pinned result slots; two
+    # batches in flight, so one batch's copies overlap the next one's
+    # forward.  Timed by the host clock from a synchronised start to the
+    # last wait (which returns once that batch's results are in host memory).
     h_pages = torch.from_numpy(pages).pin_memory().numpy()
+    e2e_steps = max(3, K)
+    for _ in range(2):
+        ctx.wait(ctx.submit(h_pages, hw), B, copy=False)
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    w0 = time.perf_counter()
+    pending = []
+    for _ in range(e2e_steps):
+        pending.append(ctx.submit(h_pages, hw))
+        if len(pending) == 2:
+            ctx.wait(pending.pop(0), B, copy=False)
+    for t in pending:
+        ctx.wait(t, B, copy=False)
+    e2e_ms = (time.perf_counter() - w0) * 1e3
+    barrier(pg)
+    e2e_ms = max_over_ranks(pg, e2e_ms)
+    e2e_val = B * e2e_steps * world / (e2e_ms / 1e3)
+    h2d = B * 3 * 800 * 800 * 4 + B * 8
+    d2h = B * 300 * 7 * 4 + B * 300 * 1250 * 4
+
+    # ---- e2e in the reference's result format: ppdl_infer_batch (one batch
+    # at a time, int32 masks of 48 MB per page read back into pinned buffers)
     ctx.infer_batch(h_pages, hw, copy=False)
     barrier(pg)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e2e_steps = max(3, min(K, 5))
+    i32_steps = max(3, min(K, 5))
     e0.record(st)
-    for _ in range(e2e_steps):
-        res = ctx.infer_batch(h_pages, hw, copy=False)
+    for _ in range(i32_steps):
+        ctx.infer_batch(h_pages, hw, copy=False)
     e1.record(st)
     torch.cuda.synchronize(dev)
     barrier(pg)
-    e2e_ms = max_over_ranks(pg, e0.elapsed_time(e1))
-    e2e_val = B * e2e_steps * world / (e2e_ms / 1e3)
-    h2d = B * 3 * 800 * 800 * 4 + B * 8
-    d2h = B * 300 * 7 * 4 + B * 300 * 40000 * 4
+    i32_ms = max_over_ranks(pg, e0.elapsed_time(e1))
+    i32_val = B * i32_steps * world / (i32_ms / 1e3)
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -555,9 +579,15 @@ def run_forward(args, world, rank, local, pg):
         "profile_ms_per_step": round(prof_ms, 3),
         "roofline": roof,
         "e2e": {"value": round(e2e_val, 2), "unit": "pages/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h,
-                "path": "ppdl_infer_batch (pinned host images in, dets + int32 masks out "
-                        "into pinned host buffers)"},
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "path": "ppdl_submit_batch / ppdl_wait_batch (pinned host pages in, dets + "
+                        "packed masks out into pinned host buffers, two batches in flight; "
+                        "host clock)"},
+        "e2e_int32_masks": {"value": round(i32_val, 2), "unit": "pages/s",
+                            "h2d_bytes_per_step": h2d,
+                            "d2h_bytes_per_step": B * 300 * 7 * 4 + B * 300 * 40000 * 4,
+                            "path": "ppdl_infer_batch (one batch at a time, dets + int32 masks "
+                                    "of the reference's format)"},
         "gpu_launches": len(steps) * K,
         "clocks": clk,
     }

@@ -85,6 +85,52 @@ PPDL_API int ppdl_device_outputs(ppdl_ctx * ctx, const float ** d_dets,
 /* extension: waits for the ctx stream; returns 2 if the GPU work failed. */
 PPDL_API int ppdl_sync(ppdl_ctx * ctx);
 
+/* extension: as ppdl_infer_device, but the masks stay packed (the forward's
+   own mask output, 1 bit per pixel, see ppdl_result_bits); they are read with
+   ppdl_device_mask_bits after ppdl_sync.  ppdl_device_outputs' int32 masks
+   are not refreshed by this call. */
+PPDL_API int ppdl_infer_device_bits(ppdl_ctx * ctx, const float * d_images, int n,
+                                    const int32_t * ori_hw);
+
+/* extension: device pointer of the packed masks of the last forward,
+   [n][300][1250] 32-bit words (layout as ppdl_result_bits.mask_bits). */
+PPDL_API int ppdl_device_mask_bits(ppdl_ctx * ctx, const uint32_t ** d_bits);
+
+/* extension (no counterpart in the reference, whose result masks are
+   300 x 200 x 200 int32 per page, src/ppdoclayout.cpp:985-990): one page's
+   result with the masks packed 1 bit per pixel — 1.5 MB instead of 48 MB.
+   Pixel p = y * 200 + x of detection i is bit (p & 31) of
+   mask_bits[i * 1250 + (p >> 5)]; ppdl_expand_mask_bits restores the int32
+   form.  dets and infer_ms as in ppdl_result. */
+typedef struct {
+    const float *    dets;       /* 300 x 7, score-descending */
+    int32_t          num_dets;   /* 300 */
+    const uint32_t * mask_bits;  /* 300 x 1250 words */
+    double           infer_ms;   /* device time of the forward */
+} ppdl_result_bits;
+
+/* extension: pipelined batches.  Enqueues n pages (host memory; pinned
+   memory lets the copy overlap the previous batch's forward) and returns at
+   once with *ticket.  The copy in, the forward and the copy out of the
+   results (dets + packed masks) run on three streams, so up to two batches
+   are in flight: batch t's copies overlap batch t-1's forward.  The pages
+   must stay unchanged until ppdl_wait_batch(ticket) returns.  Results of
+   ticket t live in ctx-owned pinned buffers until ticket t + 2 is submitted
+   (a submission waits for ticket t - 2's copy-out first).  The first call
+   allocates the pipeline's buffers (two device staging copies of the pages
+   and outputs, two pinned result slots).  Returns 0, 1 (bad args), 2
+   (failure). */
+PPDL_API int ppdl_submit_batch(ppdl_ctx * ctx, const float * images_chw, int n,
+                               const int32_t * ori_hw, int64_t * ticket);
+
+/* extension: waits for the batch of ticket and fills results[n] (n of that
+   submission).  Returns 0, 1 (unknown or overwritten ticket), 2 (failure). */
+PPDL_API int ppdl_wait_batch(ppdl_ctx * ctx, int64_t ticket, ppdl_result_bits * results);
+
+/* extension: host expansion of packed masks into the reference's int32
+   format: masks[i * 40000 + p] = bit p of detection i, for n_dets rows. */
+PPDL_API void ppdl_expand_mask_bits(const uint32_t * mask_bits, int32_t * masks, int n_dets);
+
 /* extension: the CUDA stream (cudaStream_t) the ctx enqueues on, for callers
    that time or order their own work against it. */
 PPDL_API void * ppdl_stream(ppdl_ctx * ctx);

@@ -17,6 +17,7 @@ constexpr int kNLvl = 3;
 constexpr int kNPts = 4;
 constexpr int kMaskHW = 200;
 constexpr int kMaskPix = kMaskHW * kMaskHW;
+constexpr int kMaskWords = kMaskPix / 32;  // packed mask: 1250 32-bit words
 constexpr int kNTok = 13125;
 
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_SILU = 2, ACT_GELU = 3 };

@@ -463,6 +463,27 @@ __global__ void transpose_kernel(const float *__restrict__ x, long long xbs, flo
     }
 }
 
+// ---- rows padded to 16-byte multiples ---------------------------------------
+// y[b][c][h][w] = x[b][c][h][w] for w < W, 0 for W <= w < Wp (Wp % 4 == 0):
+// the input of a tensor-core conv whose rows TMA cannot address otherwise.
+// Each thread writes four floats with one 16-byte store.
+__global__ void pad_rows_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
+                                long long ybs, int C, int H, int W, int Wp) {
+    const int q = Wp >> 2;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long n = (long long)C * H * q;
+    if (i >= n) return;
+    const int b = blockIdx.y;
+    const long long row = i / q;  // c * H + h
+    const int w0 = (int)(i - row * q) * 4;
+    const float *xr = x + (long long)b * xbs + row * W;
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) v[e] = w0 + e < W ? __ldg(xr + w0 + e) : 0.0f;
+    reinterpret_cast<float4 *>(y + (long long)b * ybs + row * Wp)[w0 >> 2] =
+        make_float4(v[0], v[1], v[2], v[3]);
+}
+
 inline int blocks(long long n, int t = 256) { return (int)((n + t - 1) / t); }
 
 // grid of the per-page kernels: x over the channels x pixels (or tiles) of a
@@ -473,6 +494,16 @@ inline bool grid3_ok(long long pix, int ch, int b) {
 inline dim3 grid3(long long pix, int ch, int b) { return dim3(blocks(pix * ch), b); }
 
 }  // namespace
+
+Status launch_pad_rows(const float *x, long long xbs, float *y, long long ybs, int C, int H,
+                       int W, int Wp, int B, cudaStream_t st) {
+    if (C <= 0 || H <= 0 || W <= 0 || Wp < W || Wp % 4 || B <= 0 || B > 65535 ||
+        ((uintptr_t)y & 15) || ybs % 4)
+        return ERR_SHAPE;
+    const long long n = (long long)C * H * (Wp / 4);
+    pad_rows_kernel<<<dim3(blocks(n), B), 256, 0, st>>>(x, xbs, y, ybs, C, H, W, Wp);
+    return cuda_status();
+}
 
 Status launch_wg4_input(const float *x, long long xbs, float *dt, int IC, int H, int W, int TW,
                         int TH, int pad, int B, cudaStream_t st, int ldt) {

@@ -49,6 +49,12 @@ Status launch_interp(const float *x, long long xbs, float *y, long long ybs, con
                      long long bbs, int C, int H, int W, int OH, int OW, bool bilinear, int B,
                      cudaStream_t st);
 
+// rows of the C x H x W pages copied into rows of Wp floats (Wp % 4 == 0,
+// zero past W): the input of a tensor-core conv whose rows are not 16-byte
+// multiples
+Status launch_pad_rows(const float *x, long long xbs, float *y, long long ybs, int C, int H,
+                       int W, int Wp, int B, cudaStream_t st);
+
 // y[c][r] = x[r][c] for an R x Cc matrix per page (row strides ldx, ldy)
 Status launch_transpose(const float *x, long long xbs, float *y, long long ybs, int R, int Cc,
                         long long ldx, long long ldy, int B, cudaStream_t st);

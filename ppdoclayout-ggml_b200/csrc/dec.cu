@@ -284,7 +284,48 @@ __global__ void pp_masks_kernel(const float *__restrict__ ml, const int32_t *__r
     dst[i] = make_int4(v.x > 0.0f, v.y > 0.0f, v.z > 0.0f, v.w > 0.0f);
 }
 
+// Packed masks: word w of detection row r holds pixels 32w .. 32w + 31 of
+// the thresholded mask of the query selected for that row (bit i = pixel
+// 32w + i, logit > 0 — the reference's threshold, src/ppdoclayout.cpp:985-990).
+// A warp reads 32 consecutive logits (one 128-byte line) per word and
+// ballots them.
+__global__ void pp_mask_bits_kernel(const float *__restrict__ ml, const int32_t *__restrict__ sel,
+                                    uint32_t *__restrict__ bits) {
+    const int r = blockIdx.y, b = blockIdx.z;
+    const int q = sel[b * kNQ + r] / kNC;
+    const float *src = ml + ((long long)b * kNQ + q) * kMaskPix;
+    uint32_t *dst = bits + ((long long)b * kNQ + r) * kMaskWords;
+    const int lane = threadIdx.x & 31;
+    const int w0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    for (int w = w0; w < kMaskWords; w += gridDim.x * (blockDim.x >> 5)) {
+        const uint32_t word = __ballot_sync(0xffffffffu, __ldg(src + w * 32 + lane) > 0.0f);
+        if (lane == 0) dst[w] = word;
+    }
+}
+
+// int32 masks (the reference's result format) from packed masks: each
+// thread expands one word into 32 ints (eight 16-byte stores).
+__global__ void unpack_mask_bits_kernel(const uint32_t *__restrict__ bits,
+                                        int32_t *__restrict__ masks, long long words) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= words) return;
+    const uint32_t w = __ldg(bits + i);
+    int4 *dst = reinterpret_cast<int4 *>(masks + i * 32);
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+        dst[j] = make_int4((w >> (4 * j)) & 1, (w >> (4 * j + 1)) & 1, (w >> (4 * j + 2)) & 1,
+                           (w >> (4 * j + 3)) & 1);
+}
+
 }  // namespace
+
+Status launch_unpack_mask_bits(const uint32_t *bits, int32_t *masks, long long rows,
+                               cudaStream_t st) {
+    if (rows <= 0) return rows == 0 ? OK : ERR_SHAPE;
+    const long long words = rows * kMaskWords;
+    unpack_mask_bits_kernel<<<blocks(words), 256, 0, st>>>(bits, masks, words);
+    return cuda_status();
+}
 
 Status launch_layernorm256(const float *x, const float *r, const float *g, const float *b,
                            float *y, long long rows, cudaStream_t st) {
@@ -353,7 +394,8 @@ Status launch_gather_rows(const float *x, const int32_t *idx, float *y, int rows
 
 Status launch_postprocess(const float *logits, const float *boxes, const float *order,
                           const float *mask_logits, const int32_t *ori_hw, int32_t *rank,
-                          float *dets, int32_t *sel, int32_t *masks, int B, cudaStream_t st) {
+                          float *dets, int32_t *sel, int32_t *masks, uint32_t *mask_bits, int B,
+                          cudaStream_t st) {
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -369,6 +411,11 @@ Status launch_postprocess(const float *logits, const float *boxes, const float *
     if (masks) {
         dim3 grid((unsigned)cdiv(kMaskPix / 4, 256), kNQ, (unsigned)B);
         pp_masks_kernel<<<grid, 256, 0, st>>>(mask_logits, sel, masks);
+    }
+    if (mask_bits) {
+        // 1250 words per row: 5 blocks of 8 warps, each warp ~31 words
+        dim3 grid(5u, kNQ, (unsigned)B);
+        pp_mask_bits_kernel<<<grid, 256, 0, st>>>(mask_logits, sel, mask_bits);
     }
     return cuda_status();
 }

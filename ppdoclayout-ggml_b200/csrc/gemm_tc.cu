@@ -98,14 +98,17 @@ constexpr int kStagingBytes = 8 * 2 * kBoxBytes;  // 32 KB
 constexpr int kCtrlBytes = 2048;                 // control block + 1024-alignment slack
 // box mode: input windows in flight (a ring of their own beside the stages)
 constexpr int kMaxBoxes = 4;
-// rows mode: a k-block is 32 channel rows of kRowsBox floats (128 pixels
-// plus up to 3 floats of alignment remainder, rounded to 16 bytes), each
-// in a slot of kRowsPitch floats (640 bytes: TMA destinations stay 128-byte
-// aligned); the A region is 20 KB, so B stays 1024-byte aligned
+// rows mode: channel rows c and c + 4 of a CHW tensor lie 4 * plane floats
+// apart, a 16-byte multiple for any plane, so the tensor is viewed as
+// [pages][C / 4][4 * plane] and a k-block (32 channels) is four TMA boxes,
+// one per q = c % 4, each 8 rows (channels q, q + 4, ..., q + 28) of
+// kRowsBox floats: 128 pixels plus up to 3 floats of alignment remainder,
+// rounded to 16 bytes.  A box is 4224 bytes (128-byte aligned boxes); the A
+// region is rounded to 17 KB so that B stays 1024-byte aligned.
 constexpr int kRowsBox = 132;
-constexpr int kRowsPitch = 160;
-constexpr int kRowsBytes = 32 * kRowsPitch * 4;
-static_assert(kRowsBytes % 1024 == 0 && (kRowsPitch * 4) % 128 == 0, "rows-mode layout");
+constexpr int kRowsQBytes = 8 * kRowsBox * 4;
+constexpr int kRowsBytes = (4 * kRowsQBytes + 1023) / 1024 * 1024;
+static_assert(kRowsQBytes % 128 == 0 && kRowsBytes % 1024 == 0, "rows-mode layout");
 constexpr int kSmemMax = 227 * 1024;
 
 // Registers per thread: at launch (the __launch_bounds__(512, 1) maximum,
@@ -476,12 +479,31 @@ __device__ __forceinline__ void split_row_mmajor(const uint8_t *tile, int r, uin
 }
 
 // Box mode: the thread's A row (one output pixel) of k-block j of the
-// current input window: kernel column j, the window's 32 channels.
-// base = the pixel's offset in the window (row r * Wb + column cx * S +
-// alignment remainder), chs = the window's channel stride (4 * Wb floats).
-__device__ __forceinline__ void split_row_box(const float *win, int base, int chs, int j,
-                                              uint32_t col) {
-    {
+// current input window.  base = the pixel's offset in the window (row
+// r * Wb + column cx * S + alignment remainder), chs = the window's channel
+// stride (4 * Wb floats).  With 32 channels per window (lcb = 5) k-block j
+// is kernel column j; with CB = 4, 8 or 16 channels (lcb = 2..4) the one
+// k-block of the window holds all KS kernel columns, k = kw * CB + c, and
+// k >= KS * CB (zero weight columns) reads column 0, which holds finite data.
+template <int LCB>
+__device__ __forceinline__ void split_row_box_small(const float *win, int base, int chs, int KS,
+                                                    uint32_t col) {
+#pragma unroll
+    for (int h = 0; h < 4; h++) {
+        float x[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            constexpr int kCB = 1 << LCB;
+            const int k = 8 * h + u, kw = k >> LCB, c = k & (kCB - 1);
+            x[u] = kw < KS ? win[base + c * chs + kw] : win[base];
+        }
+        split_store8(col + 8 * h, x);
+    }
+}
+
+__device__ __forceinline__ void split_row_box(const float *win, int base, int chs, int j, int lcb,
+                                              int KS, uint32_t col) {
+    if (lcb == 5) {
         const float *t = win + base + j;
 #pragma unroll
         for (int h = 0; h < 4; h++) {
@@ -490,23 +512,32 @@ __device__ __forceinline__ void split_row_box(const float *win, int base, int ch
             for (int u = 0; u < 8; u++) x[u] = t[(8 * h + u) * chs];
             split_store8(col + 8 * h, x);
         }
-        return;
+    } else if (lcb == 4) {
+        split_row_box_small<4>(win, base, chs, KS, col);
+    } else if (lcb == 3) {
+        split_row_box_small<3>(win, base, chs, KS, col);
+    } else {
+        split_row_box_small<2>(win, base, chs, KS, col);
     }
 }
 
-// Rows mode: the thread's pixel r of a k-block stored as 32 channel rows of
-// kRowsPitch floats, row j starting (j * offmul + delta) & 3 floats late
-// (the TMA row began at the 16-byte boundary below it).
+// Rows mode: the thread's pixel r of a k-block stored as four boxes (q =
+// channel % 4) of 8 rows of kRowsBox floats, the rows of box q starting
+// (q * offmul + delta) & 3 floats late (the box began at the 16-byte
+// boundary below them).
 __device__ __forceinline__ void split_row_rows(const uint8_t *tile, int r, int offmul, int delta,
                                                uint32_t col) {
     const float *t = reinterpret_cast<const float *>(tile) + r;
+    int off[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) off[q] = q * (kRowsQBytes / 4) + ((q * offmul + delta) & 3);
 #pragma unroll
     for (int h = 0; h < 4; h++) {
         float x[8];
 #pragma unroll
         for (int u = 0; u < 8; u++) {
-            const int j = 8 * h + u;
-            x[u] = t[j * kRowsPitch + ((j * offmul + delta) & 3)];
+            const int j = 8 * h + u;  // channel k0 + j: box j % 4, row j / 4
+            x[u] = t[off[j & 3] + (j >> 2) * kRowsBox];
         }
         split_store8(col + 8 * h, x);
     }
@@ -589,8 +620,58 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                   pplanes = a.planes;
         const uint32_t pstage = a.stage_bytes, ptx = a.tx_bytes, pidesc = a.idesc;
         if (warp == kWarpProducer) {
-            if (lane == 0) {
-                constexpr bool pbox = AMODE == kModeBox, prows = AMODE == kModeRows;
+            if constexpr (AMODE == kModeRows) {
+                // rows mode, the whole warp: lane 0 waits for the stage and
+                // arms its barrier, then lanes 0-3 issue the four boxes of
+                // the k-block (each from the 16-byte boundary below its rows)
+                // and lane 0 the B loads
+                long long it = 0;
+                Ring rs(S);
+                bool ok = true;
+                const long long rplane = a.rows_plane;
+                const int rdelta = a.rows_delta;
+                for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
+                    const int z = t / (pmt * pnt);
+                    const int r = t - z * pmt * pnt;
+                    const int mt = r / pnt;
+                    const int m0 = mt * kBM, n0 = (r - mt * pnt) * pbn;
+                    const int pz = z % pplanes;
+                    for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
+                        const int s = rs.i;
+                        bool good = true;
+                        if (lane == 0) {
+                            good = mbar_wait(bar_empty + 8 * s, rs.ph ^ 1, abort_flag);
+                            if (good) mbar_expect_tx(bar_full + 8 * s, ptx);
+                        }
+                        if (!__shfl_sync(0xffffffffu, good ? 1 : 0, 0)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t st = stage0 + s * pstage;
+                        const uint32_t fb = bar_full + 8 * s;
+                        const int k0 = kb * kBK;
+                        if (lane < 4) {
+                            const long long xr = (long long)lane * rplane + m0 + rdelta;
+                            tma_load_3d(st + (uint32_t)(lane * kRowsQBytes), &tmA, fb,
+                                        (int)(xr & ~3LL), k0 >> 2, z);
+                        }
+                        if (lane == 0) {
+                            const uint32_t stb = st + pstage - 2u * 128u * pbn;
+                            tma_load_3d(stb, &tmBhi, fb, k0, n0, pz);
+                            tma_load_3d(stb + pbn * 128, &tmBlo, fb, k0, n0, pz);
+                        }
+                    }
+                }
+                if (lane == 0) {
+                    const long long first = it > S ? it - S : 0;
+                    for (long long jj = first; jj < it; jj++) {
+                        int dummy = 0;
+                        mbar_wait(bar_full + 8 * (int)(jj % S), (uint32_t)((jj / S) & 1),
+                                  (volatile int *)&dummy);
+                    }
+                }
+            } else if (lane == 0) {
+                constexpr bool pbox = AMODE == kModeBox;
                 const uint32_t box0 = stage0 + (uint32_t)S * pstage;
                 long long it = 0, ib = 0;  // stages and windows issued
                 Ring rs(S), rb(a.cb.nbox);
@@ -640,14 +721,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         mbar_expect_tx(fb, ptx);
                         if (pgather || pbox) {
                             // A is written by the converter warps / comes from a window
-                        } else if (prows) {
-                            // 32 channel rows, each from the 16-byte boundary below it
-                            const long long xz = a.rows_plane;
-                            for (int jr = 0; jr < 32; jr++) {
-                                const long long xr = (long long)(k0 + jr) * xz + m0 + a.rows_delta;
-                                tma_load_2d(st + (uint32_t)(jr * kRowsPitch * 4), &tmA, fb,
-                                            (int)(xr & ~3LL), z);
-                            }
                         } else if (pamn) {
                             tma_load_3d(st, &tmA, fb, m0, k0, z);
                         } else {
@@ -785,7 +858,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const uint32_t col = tmem_base + lane_base + (uint32_t)(kACol0 + ra.i * kACols);
                 if (pbox)
                     split_row_box(box0_ptr + (size_t)rbw.i * (a.cb.box_bytes / 4), wbase, chs, wj,
-                                  col);
+                                  a.cb.lcb, a.cb.KS, col);
                 else if (prows)
                     split_row_rows(tile, ct, a.rows_offmul, a.rows_delta, col);
                 else if (pamn && !pgather)
@@ -1470,6 +1543,8 @@ bool tc_gemm_plan_box(TcGemm *g, int N, int batch, const TcConvBox &cbin, const 
         return false;
     if ((long long)b.OH * b.OW >= (1LL << 31)) return false;
     tc_conv_box_blocks(b.IC, b.KS, &b.CB, &b.kbpb, &b.nbx);
+    b.lcb = 2;
+    while ((1 << b.lcb) < b.CB) b.lcb++;
     // window: columns from the 16-byte boundary at or below ox0*S - P (ox0
     // is a multiple of 32, so the remainder o is (-P) mod 4) through the
     // last tap of column 31
@@ -1477,7 +1552,7 @@ bool tc_gemm_plan_box(TcGemm *g, int N, int batch, const TcConvBox &cbin, const 
     b.Wb = (b.o + 31 * b.S + b.KS + 3) / 4 * 4;
     b.tiles_x = (b.OW + 31) / 32;
     b.tiles_y = (b.OH + 3) / 4;
-    const uint32_t raw_bytes = (uint32_t)b.Wb * 4 * b.CB * 4;
+    const uint32_t raw_bytes = (uint32_t)b.Wb * 4 * (uint32_t)b.CB * 4;
     b.box_tx = raw_bytes;
     b.box_bytes = (raw_bytes + 1023) / 1024 * 1024;
     const int K = b.nbx * b.kbpb * 32;
@@ -1532,8 +1607,7 @@ bool tc_gemm_plan_rows(TcGemm *g, int M, int N, int K, int batch, const float *x
                        int planes) {
     g->ok = false;
     if (!x || plane < M || K % 4 || ((uintptr_t)x & 3) || (x_bs * 4) % 16 ||
-        (batch > 1 && x_bs <= 0) ||
-        (long long)(K + 32) * plane + 4 >= (1LL << 31))
+        (batch > 1 && x_bs <= 0) || 4 * plane + 4 >= (1LL << 31))
         return false;
     if (!plan_common(g, M, N, K, batch, planes, epi, kRowsBytes)) return false;
     // the map starts at the 16-byte boundary at or below x; delta = the
@@ -1545,19 +1619,19 @@ bool tc_gemm_plan_rows(TcGemm *g, int M, int N, int K, int batch, const float *x
     g->gather = 0;
     g->box = 0;
     g->rows = 1;
-    // each page as one flat row of channels * plane floats (+ the slack),
-    // loaded in boxes of kRowsPitch floats
+    // each page as [K / 4][4 * plane (+ the slack)]: row q of group g is
+    // channel 4g + q; boxes of kRowsBox floats x 8 groups
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)((long long)K * plane + g->rows_delta),
+    const cuuint64_t dims[3] = {(cuuint64_t)(4 * plane + g->rows_delta), (cuuint64_t)(K / 4),
                                 (cuuint64_t)batch};
-    // (one page: any 16-byte multiple at least the row length)
+    // (one page: any 16-byte multiple at least the page's length)
     const cuuint64_t page_bytes =
-        x_bs > 0 ? (cuuint64_t)(x_bs * 4) : (dims[0] * 4 + 15) / 16 * 16;
-    const cuuint64_t strides[1] = {page_bytes};
-    const cuuint32_t box[2] = {kRowsBox, 1};
-    const cuuint32_t es[2] = {1, 1};
-    if (fn(&g->tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides,
+        x_bs > 0 ? (cuuint64_t)(x_bs * 4) : (cuuint64_t)(K * plane * 4 + 15) / 16 * 16;
+    const cuuint64_t strides[2] = {(cuuint64_t)(16 * plane), page_bytes};
+    const cuuint32_t box[3] = {kRowsBox, 8, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    if (fn(&g->tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides,
            box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
@@ -1619,7 +1693,7 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
         a.tx_bytes = b_bytes;
     } else if (g.rows) {
         a.stage_bytes = kRowsBytes + b_bytes;
-        a.tx_bytes = 32u * kRowsBox * 4u + b_bytes;
+        a.tx_bytes = 4u * kRowsQBytes + b_bytes;
     } else {
         a.stage_bytes = kABytes + b_bytes;
         a.tx_bytes = (g.gather ? 0 : kABytes) + b_bytes;

@@ -56,18 +56,23 @@ struct TcConvBox {
     long long x_bs = 0;   // page stride (elements)
     int IC = 0, H = 0, W = 0, KS = 1, S = 1, P = 0, OH = 0, OW = 0;
     // derived by the planner
-    int CB = 32, kbpb = 1, nbx = 1, Wb = 0, o = 0, tiles_x = 0, tiles_y = 0, nbox = 2;
+    int CB = 32, lcb = 5, kbpb = 1, nbx = 1, Wb = 0, o = 0, tiles_x = 0, tiles_y = 0, nbox = 2;
     uint32_t box_bytes = 0;  // window slot in shared memory (1024-byte multiple)
     uint32_t box_tx = 0;     // bytes one window load transfers (Wb * 4 * 32 * 4)
 };
 
-// Channels per window (32: channels past IC are zero-filled by TMA) and
-// k-blocks per window (one per kernel column); the repacked weight has
-// nbx * kbpb * 32 columns, nbx = ceil(IC / 32) * KS windows.
+// Channels per window and k-blocks per window.  CB = the power of two >= IC
+// (at least 4) when all KS kernel columns of CB channels fit one k-block of
+// 32 (then k = kw * CB + c inside the window's single k-block), else 32
+// (one k-block per kernel column); channels past IC are zero-filled by TMA.
+// The repacked weight has nbx * kbpb * 32 columns, nbx = ceil(IC / CB) * KS.
 inline void tc_conv_box_blocks(int IC, int KS, int *CB, int *kbpb, int *nbx) {
-    *CB = 32;
-    *kbpb = KS;
-    *nbx = (IC + 31) / 32 * KS;
+    int cb = 4;
+    while (cb < IC && cb < 32) cb *= 2;
+    if (KS * cb > 32) cb = 32;
+    *CB = cb;
+    *kbpb = cb == 32 ? KS : 1;
+    *nbx = (IC + cb - 1) / cb * KS;
 }
 inline int tc_conv_box_kdim(int IC, int KS) {
     int cb, kbpb, nbx;

@@ -145,6 +145,7 @@ public:
     float *mask_logits = nullptr;
     float *dets = nullptr;
     int32_t *sel = nullptr, *rank = nullptr, *masks = nullptr;
+    uint32_t *mask_bits = nullptr;  // packed masks [B][300][1250], made by the forward
     int32_t *enc_topk = nullptr;  // encoder top-300 token indices (query order)
 
     ~Model() {
@@ -181,13 +182,29 @@ public:
     // warps' gather.  Returns a null plan when neither applies (the caller
     // keeps the SIMT GEMM).
     std::shared_ptr<TcGemm> plan_conv_implicit(const V &x, int K, int s, int p, int OC, int OH,
-                                               int OW, const float *wp, const TcEpilogue &e) {
+                                               int OW, const float *wp, const TcEpilogue &e,
+                                               const std::string &name) {
         if (!ok) return nullptr;
         auto g = std::make_shared<TcGemm>();
         TcConvBox cb;
         cb.x = x.p; cb.x_bs = x.bs;
         cb.IC = x.C; cb.H = x.H; cb.W = x.W; cb.KS = K; cb.S = s; cb.P = p;
         cb.OH = OH; cb.OW = OW;
+        if (x.W % 4) {
+            // rows that are not 16-byte multiples (a 50-wide input): the
+            // windows come from a copy with rows padded to Wp = W rounded up
+            // to 4 (zeros past W, which the conv reads as its padding)
+            const int Wp = (x.W + 3) / 4 * 4;
+            const long long pbs = (long long)x.C * x.H * Wp;
+            float *xp = dalloc(pbs * Bmax);
+            if (!ok) return nullptr;
+            const V xv = x;
+            push(name + ".pad_rows", PPDL_STEP_GLUE, 0.0,
+                 4.0 * ((double)x.C * x.plane() + (double)pbs), [=]() {
+                return launch_pad_rows(xv.p, xv.bs, xp, pbs, xv.C, xv.H, xv.W, Wp, nb, st);
+            });
+            cb.x = xp; cb.x_bs = pbs; cb.W = Wp;
+        }
         const int Kb = tc_conv_box_kdim(x.C, K);
         float *hi = dalloc((long long)OC * Kb), *lo = dalloc((long long)OC * Kb);
         if (!ok) return nullptr;
@@ -504,7 +521,7 @@ public:
         // k3-s2 / k2: implicit GEMM on the CHW input (no im2col buffer)
         if (use_tc) {
             auto g = plan_conv_implicit(x, K, s, p, OC, OH, OW, wp,
-                                        chw_epilogue(y, bp, act, res, res_mode));
+                                        chw_epilogue(y, bp, act, res, res_mode), name);
             if (g) {
                 push(name, PPDL_STEP_GEMM_IMPLICIT, 2.0 * OC * OH * OW * IC * K * K,
                      4.0 * ((double)IC * x.plane() + (double)OC * OH * OW),
@@ -1105,14 +1122,22 @@ public:
         if (cudaMalloc(&masks, sizeof(int32_t) * (size_t)kNQ * kMaskPix * Bmax) != cudaSuccess)
             fail("cudaMalloc");
         allocs.push_back(masks);
+        if (cudaMalloc(&mask_bits, sizeof(uint32_t) * (size_t)kNQ * kMaskWords * Bmax) !=
+            cudaSuccess)
+            fail("cudaMalloc");
+        allocs.push_back(mask_bits);
         {
+            // the forward's mask output is packed (1 bit per pixel); the
+            // int32 form of the reference's result is expanded from it only
+            // for the calls that return it (expand_masks)
             const S lg = logits, bx = boxes, od = order;
             const float *mlp = mask_logits;
+            uint32_t *mb = mask_bits;
             after(e_order);
             push("postprocess", PPDL_STEP_POSTPROCESS, 0.0,
-                 4.0 * ((double)kNQ * kNQ + 2.0 * kNQ * kMaskPix), [=]() {
-                return launch_postprocess(lg.p, bx.p, od.p, mlp, ori_hw, rank, dets, sel, masks, nb,
-                                          st);
+                 4.0 * ((double)kNQ * kNQ + kNQ * kMaskPix) + 4.0 * kNQ * kMaskWords, [=]() {
+                return launch_postprocess(lg.p, bx.p, od.p, mlp, ori_hw, rank, dets, sel, nullptr,
+                                          mb, nb, st);
             });
         }
         if (!ok) return;
@@ -1234,6 +1259,12 @@ public:
         return s;
     }
 
+    // int32 masks of the last n pages from the packed ones (the reference's
+    // result format, 48 MB per page)
+    Status expand_masks(int n) {
+        return launch_unpack_mask_bits(mask_bits, masks, (long long)n * kNQ, st);
+    }
+
     // Runs the plan for n pages: eagerly the first time (sets kernel
     // attributes), then from a captured CUDA graph per batch size.
     Status run(int n) {
@@ -1263,6 +1294,25 @@ public:
 }  // namespace ppdl
 
 // ============================================================ C ABI ========
+// Two-deep pipeline of ppdl_submit_batch / ppdl_wait_batch: slot s = ticket
+// % 2 owns a device staging buffer for the pages (filled on the copy-in
+// stream, copied into the forward's input on the compute stream), device
+// and pinned host copies of the dets and packed masks (copied out on the
+// copy-out stream), and the events that order the three streams.
+struct PpdlPipe {
+    bool ready = false;
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    float *d_in[2] = {}, *d_dets[2] = {};
+    int32_t *d_hw[2] = {};
+    uint32_t *d_bits[2] = {};
+    float *h_dets[2] = {};
+    uint32_t *h_bits[2] = {};
+    cudaEvent_t in_ready[2] = {}, in_free[2] = {}, out_ready[2] = {}, out_done[2] = {},
+                t0[2] = {}, t1[2] = {};
+    long long ticket_of[2] = {-1, -1}, next = 0;
+    int n_of[2] = {0, 0};
+};
+
 struct ppdl_ctx {
     std::unique_ptr<ppdl::Model> m;
     float *h_dets = nullptr;
@@ -1270,13 +1320,35 @@ struct ppdl_ctx {
     bool computed = false;
     int last_n = 0;
     cudaEvent_t e0 = nullptr, e1 = nullptr;
+    PpdlPipe pipe;
 };
 
 namespace {
 
+void pipe_release(PpdlPipe &p) {
+    if (p.h2d) cudaStreamSynchronize(p.h2d);
+    if (p.d2h) cudaStreamSynchronize(p.d2h);
+    for (int s = 0; s < 2; s++) {
+        if (p.d_in[s]) cudaFree(p.d_in[s]);
+        if (p.d_dets[s]) cudaFree(p.d_dets[s]);
+        if (p.d_hw[s]) cudaFree(p.d_hw[s]);
+        if (p.d_bits[s]) cudaFree(p.d_bits[s]);
+        if (p.h_dets[s]) cudaFreeHost(p.h_dets[s]);
+        if (p.h_bits[s]) cudaFreeHost(p.h_bits[s]);
+        for (cudaEvent_t e : {p.in_ready[s], p.in_free[s], p.out_ready[s], p.out_done[s], p.t0[s],
+                              p.t1[s]})
+            if (e) cudaEventDestroy(e);
+    }
+    if (p.h2d) cudaStreamDestroy(p.h2d);
+    if (p.d2h) cudaStreamDestroy(p.d2h);
+    p = PpdlPipe();
+}
+
 void ctx_release(ppdl_ctx *c) {
     if (!c) return;
     if (c->m) cudaSetDevice(c->m->dev);
+    if (c->m) cudaStreamSynchronize(c->m->st);
+    pipe_release(c->pipe);
     if (c->h_dets) cudaFreeHost(c->h_dets);
     if (c->h_masks) cudaFreeHost(c->h_masks);
     if (c->e0) cudaEventDestroy(c->e0);
@@ -1293,7 +1365,8 @@ bool write_file(const std::string &path, const void *src, size_t n) {
     return wr == n;
 }
 
-int enqueue(ppdl_ctx *c, const float *images, bool images_on_device, int n, const int32_t *ori_hw) {
+int enqueue(ppdl_ctx *c, const float *images, bool images_on_device, int n, const int32_t *ori_hw,
+            bool int32_masks = true) {
     ppdl::Model &m = *c->m;
     cudaSetDevice(m.dev);
     const size_t img_bytes = (size_t)3 * ppdl::kImg * ppdl::kImg * sizeof(float);
@@ -1310,6 +1383,7 @@ int enqueue(ppdl_ctx *c, const float *images, bool images_on_device, int n, cons
         return 2;
     }
     cudaEventRecord(c->e1, m.st);
+    if (int32_masks && m.expand_masks(n) != ppdl::OK) return 2;
     c->last_n = n;
     return 0;
 }
@@ -1431,6 +1505,155 @@ PPDL_API int ppdl_sync(ppdl_ctx *c) {
     cudaSetDevice(c->m->dev);
     if (cudaStreamSynchronize(c->m->st) != cudaSuccess) return 2;
     return ppdl::tc_error_fetch_and_clear() ? 2 : 0;
+}
+
+PPDL_API int ppdl_infer_device_bits(ppdl_ctx *c, const float *d_images, int n,
+                                   const int32_t *ori_hw) {
+    if (!c || !d_images || !ori_hw || n < 1 || n > c->m->Bmax) return 1;
+    for (int i = 0; i < n; i++)
+        if (ori_hw[2 * i] <= 0 || ori_hw[2 * i + 1] <= 0) return 1;
+    const int rc = enqueue(c, d_images, true, n, ori_hw, false);
+    if (!rc) c->computed = true;
+    return rc;
+}
+
+PPDL_API int ppdl_device_mask_bits(ppdl_ctx *c, const uint32_t **d_bits) {
+    if (!c || !c->computed || !d_bits) return 1;
+    *d_bits = c->m->mask_bits;
+    return 0;
+}
+
+namespace {
+
+bool pipe_setup(ppdl_ctx *c) {
+    PpdlPipe &p = c->pipe;
+    if (p.ready) return true;
+    const int B = c->m->Bmax;
+    const size_t img = (size_t)3 * ppdl::kImg * ppdl::kImg * sizeof(float) * B;
+    const size_t dets = sizeof(float) * ppdl::kNQ * 7 * B;
+    const size_t bits = sizeof(uint32_t) * (size_t)ppdl::kNQ * ppdl::kMaskWords * B;
+    bool ok = cudaStreamCreateWithFlags(&p.h2d, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&p.d2h, cudaStreamNonBlocking) == cudaSuccess;
+    for (int s = 0; s < 2 && ok; s++) {
+        ok = cudaMalloc(&p.d_in[s], img) == cudaSuccess &&
+             cudaMalloc(&p.d_hw[s], sizeof(int32_t) * 2 * B) == cudaSuccess &&
+             cudaMalloc(&p.d_dets[s], dets) == cudaSuccess &&
+             cudaMalloc(&p.d_bits[s], bits) == cudaSuccess &&
+             cudaHostAlloc(&p.h_dets[s], dets, 0) == cudaSuccess &&
+             cudaHostAlloc(&p.h_bits[s], bits, 0) == cudaSuccess;
+        for (cudaEvent_t *e : {&p.in_ready[s], &p.in_free[s], &p.out_ready[s], &p.out_done[s]})
+            ok = ok && cudaEventCreateWithFlags(e, cudaEventDisableTiming) == cudaSuccess;
+        ok = ok && cudaEventCreate(&p.t0[s]) == cudaSuccess && cudaEventCreate(&p.t1[s]) == cudaSuccess;
+    }
+    if (!ok) {
+        cudaGetLastError();
+        pipe_release(p);
+        fprintf(stderr, "ppdl: pipeline buffer allocation failed\n");
+        return false;
+    }
+    p.ready = true;
+    return true;
+}
+
+}  // namespace
+
+PPDL_API int ppdl_submit_batch(ppdl_ctx *c, const float *images, int n, const int32_t *ori_hw,
+                               int64_t *ticket) {
+    if (!c || !images || !ori_hw || !ticket || n < 1 || n > c->m->Bmax) return 1;
+    for (int i = 0; i < n; i++)
+        if (ori_hw[2 * i] <= 0 || ori_hw[2 * i + 1] <= 0) return 1;
+    ppdl::Model &m = *c->m;
+    cudaSetDevice(m.dev);
+    if (!pipe_setup(c)) return 2;
+    PpdlPipe &p = c->pipe;
+    const long long t = p.next;
+    const int s = (int)(t & 1);
+    // the slot's previous batch (ticket t - 2) must have left its host
+    // buffers: results of ticket t stay valid until ticket t + 2 is submitted
+    if (p.ticket_of[s] >= 0 && cudaEventSynchronize(p.out_done[s]) != cudaSuccess) return 2;
+    const size_t img_bytes = (size_t)3 * ppdl::kImg * ppdl::kImg * sizeof(float) * n;
+    // copy-in stream: pages into the slot's staging buffer once the forward
+    // of ticket t - 2 has taken them (in_free)
+    bool ok = (p.ticket_of[s] < 0 || cudaStreamWaitEvent(p.h2d, p.in_free[s], 0) == cudaSuccess) &&
+              cudaMemcpyAsync(p.d_in[s], images, img_bytes, cudaMemcpyHostToDevice, p.h2d) ==
+                  cudaSuccess &&
+              cudaMemcpyAsync(p.d_hw[s], ori_hw, sizeof(int32_t) * 2 * n, cudaMemcpyHostToDevice,
+                              p.h2d) == cudaSuccess &&
+              cudaEventRecord(p.in_ready[s], p.h2d) == cudaSuccess;
+    // compute stream: staging -> the forward's input, the forward (its
+    // CUDA graph), dets + packed masks -> the slot's device output copy
+    ok = ok && cudaStreamWaitEvent(m.st, p.in_ready[s], 0) == cudaSuccess &&
+         cudaMemcpyAsync(m.img.p, p.d_in[s], img_bytes, cudaMemcpyDeviceToDevice, m.st) ==
+             cudaSuccess &&
+         cudaMemcpyAsync(m.ori_hw, p.d_hw[s], sizeof(int32_t) * 2 * n, cudaMemcpyDeviceToDevice,
+                         m.st) == cudaSuccess &&
+         cudaEventRecord(p.in_free[s], m.st) == cudaSuccess &&
+         cudaEventRecord(p.t0[s], m.st) == cudaSuccess;
+    if (!ok) return 2;
+    m.nb = n;
+    if (m.run(n) != ppdl::OK) {
+        fprintf(stderr, "ppdl: forward launch failed: %s\n", cudaGetErrorString(cudaGetLastError()));
+        return 2;
+    }
+    const size_t dets_bytes = sizeof(float) * ppdl::kNQ * 7 * n;
+    const size_t bits_bytes = sizeof(uint32_t) * (size_t)ppdl::kNQ * ppdl::kMaskWords * n;
+    ok = cudaEventRecord(p.t1[s], m.st) == cudaSuccess &&
+         cudaMemcpyAsync(p.d_dets[s], m.dets, dets_bytes, cudaMemcpyDeviceToDevice, m.st) ==
+             cudaSuccess &&
+         cudaMemcpyAsync(p.d_bits[s], m.mask_bits, bits_bytes, cudaMemcpyDeviceToDevice, m.st) ==
+             cudaSuccess &&
+         cudaEventRecord(p.out_ready[s], m.st) == cudaSuccess &&
+         // copy-out stream: the slot's outputs to its pinned host buffers
+         cudaStreamWaitEvent(p.d2h, p.out_ready[s], 0) == cudaSuccess &&
+         cudaMemcpyAsync(p.h_dets[s], p.d_dets[s], dets_bytes, cudaMemcpyDeviceToHost, p.d2h) ==
+             cudaSuccess &&
+         cudaMemcpyAsync(p.h_bits[s], p.d_bits[s], bits_bytes, cudaMemcpyDeviceToHost, p.d2h) ==
+             cudaSuccess &&
+         cudaEventRecord(p.out_done[s], p.d2h) == cudaSuccess;
+    if (!ok) return 2;
+    p.ticket_of[s] = t;
+    p.n_of[s] = n;
+    p.next = t + 1;
+    *ticket = t;
+    c->computed = true;
+    c->last_n = n;
+    return 0;
+}
+
+PPDL_API int ppdl_wait_batch(ppdl_ctx *c, int64_t ticket, ppdl_result_bits *res) {
+    if (!c || !res || ticket < 0 || !c->pipe.ready) return 1;
+    PpdlPipe &p = c->pipe;
+    const int s = (int)(ticket & 1);
+    if (p.ticket_of[s] != ticket) return 1;  // never submitted, or already overwritten
+    cudaSetDevice(c->m->dev);
+    if (cudaEventSynchronize(p.out_done[s]) != cudaSuccess) {
+        fprintf(stderr, "ppdl: pipelined batch failed: %s\n",
+                cudaGetErrorString(cudaGetLastError()));
+        return 2;
+    }
+    if (ppdl::tc_error_fetch_and_clear()) {
+        fprintf(stderr, "ppdl: tensor-core GEMM gave up waiting (device error flag set)\n");
+        return 2;
+    }
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, p.t0[s], p.t1[s]);
+    for (int i = 0; i < p.n_of[s]; i++) {
+        res[i].dets = p.h_dets[s] + (size_t)i * ppdl::kNQ * 7;
+        res[i].num_dets = ppdl::kNQ;
+        res[i].mask_bits = p.h_bits[s] + (size_t)i * ppdl::kNQ * ppdl::kMaskWords;
+        res[i].infer_ms = ms;
+    }
+    return 0;
+}
+
+PPDL_API void ppdl_expand_mask_bits(const uint32_t *bits, int32_t *masks, int n_dets) {
+    if (!bits || !masks || n_dets <= 0) return;
+    const long long words = (long long)n_dets * ppdl::kMaskWords;
+    for (long long w = 0; w < words; w++) {
+        const uint32_t v = bits[w];
+        int32_t *o = masks + w * 32;
+        for (int i = 0; i < 32; i++) o[i] = (int32_t)((v >> i) & 1u);
+    }
 }
 
 PPDL_API int ppdl_dump(ppdl_ctx *c, const char *dir) {

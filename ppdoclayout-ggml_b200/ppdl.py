@@ -45,6 +45,25 @@ class Result(C.Structure):
                 ("masks", C.POINTER(C.c_int32)), ("infer_ms", C.c_double)]
 
 
+class ResultBits(C.Structure):
+    """ppdl_result_bits: masks packed 1 bit per pixel (300 x 1250 words)."""
+    _fields_ = [("dets", C.POINTER(C.c_float)), ("num_dets", C.c_int32),
+                ("mask_bits", C.POINTER(C.c_uint32)), ("infer_ms", C.c_double)]
+
+
+MASK_WORDS = 1250
+
+
+def unpack_mask_bits(bits):
+    """[..., 1250] uint32 words -> [..., 200, 200] uint8 masks (bit p & 31 of
+    word p >> 5 is pixel p), the numpy form of ppdl_expand_mask_bits."""
+    import numpy as np
+    b = np.ascontiguousarray(bits, dtype=np.uint32)
+    u8 = b.view(np.uint8).reshape(b.shape[:-1] + (MASK_WORDS * 4,))
+    px = np.unpackbits(u8, axis=-1, bitorder="little")
+    return px.reshape(b.shape[:-1] + (MASK_HW, MASK_HW))
+
+
 _lib = None
 
 
@@ -210,6 +229,64 @@ class Context:
 
     def sync(self) -> int:
         return self.lib.ppdl_sync(self.ctx)
+
+    def infer_device_bits(self, d_images_ptr: int, n: int, ori_hw) -> int:
+        """ppdl_infer_device with the masks left packed (no int32 expansion)."""
+        import numpy as np
+        L = self.lib
+        L.ppdl_infer_device_bits.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+        L.ppdl_infer_device_bits.restype = C.c_int
+        hw = np.ascontiguousarray(ori_hw, dtype=np.int32).reshape(-1, 2)
+        self._hw = hw
+        return L.ppdl_infer_device_bits(self.ctx, C.c_void_p(d_images_ptr), n, hw.ctypes.data)
+
+    def device_mask_bits(self) -> int:
+        L = self.lib
+        L.ppdl_device_mask_bits.argtypes = [C.c_void_p, C.POINTER(C.c_void_p)]
+        L.ppdl_device_mask_bits.restype = C.c_int
+        p = C.c_void_p()
+        if L.ppdl_device_mask_bits(self.ctx, C.byref(p)) != 0:
+            raise RuntimeError("no device outputs")
+        return p.value
+
+    def submit(self, images, ori_hw) -> int:
+        """ppdl_submit_batch: enqueue n pages [n,3,800,800] (keep them alive
+        and unchanged until wait() of the returned ticket; pinned memory lets
+        the copy overlap the previous batch's forward)."""
+        import numpy as np
+        L = self.lib
+        L.ppdl_submit_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                        C.POINTER(C.c_int64)]
+        L.ppdl_submit_batch.restype = C.c_int
+        if not (isinstance(images, np.ndarray) and images.dtype == np.float32 and
+                images.flags.c_contiguous):
+            raise ValueError("submit() needs a C-contiguous float32 array that stays alive")
+        hw = np.ascontiguousarray(ori_hw, dtype=np.int32).reshape(-1, 2)
+        t = C.c_int64()
+        rc = L.ppdl_submit_batch(self.ctx, images.ctypes.data, images.shape[0], hw.ctypes.data,
+                                 C.byref(t))
+        if rc != 0:
+            raise RuntimeError(f"ppdl_submit_batch returned {rc}")
+        return t.value
+
+    def wait(self, ticket: int, n: int, copy=True):
+        """ppdl_wait_batch: [(dets [300,7], mask_bits [300,1250] uint32)] of
+        the n pages of ticket.  copy=False returns views of the context's
+        pinned result slot, valid until ticket + 2 is submitted."""
+        import numpy as np
+        L = self.lib
+        L.ppdl_wait_batch.argtypes = [C.c_void_p, C.c_int64, C.POINTER(ResultBits)]
+        L.ppdl_wait_batch.restype = C.c_int
+        res = (ResultBits * n)()
+        rc = L.ppdl_wait_batch(self.ctx, ticket, res)
+        if rc != 0:
+            raise RuntimeError(f"ppdl_wait_batch returned {rc}")
+        out = []
+        for r in res:
+            d = np.ctypeslib.as_array(r.dets, (NUM_DETS, DET_FIELDS))
+            b = np.ctypeslib.as_array(r.mask_bits, (NUM_DETS, MASK_WORDS))
+            out.append((d.copy(), b.copy()) if copy else (d, b))
+        return out
 
     def stream_ptr(self) -> int:
         self.lib.ppdl_stream.argtypes = [C.c_void_p]

@@ -101,6 +101,8 @@ def _run(L, cuda, B, IC, H, W, OC, K, S, P, act, OH=None, OW=None, seed=0, ref_o
     (1, 40, 36, 36, 48, 3, 2, 1, 0, None, None),    # channel tail 40 = 32 + 8, OW 18
     (2, 32, 64, 96, 64, 3, 1, 1, 1, None, None),    # k3-s1 window (P = 1, 4 rows)
     (3, 64, 132, 128, 40, 2, 1, 0, 2, 132, 128),    # row tiles past H, 3 pages
+    (2, 8, 36, 36, 24, 3, 2, 1, 1, None, None),     # 8-channel windows, 3 columns per k-block
+    (1, 12, 44, 44, 20, 2, 1, 0, 2, 44, 44),        # 16-channel windows (12 real)
 ])
 def test_conv2d_gather_matches_float64(cuda, case):
     B, IC, H, W, OC, K, S, P, act, OH, OW = case

@@ -88,8 +88,10 @@ def test_raw_outputs_page0(gpu_out, ref_out):
     assert np.abs(od - r["order"]).max() / max(np.abs(r["order"]).max(), 1) < 1e-4
 
 
-def _check_page(dets, masks, r):
-    """The end-to-end gates of one page against the oracle's result r."""
+def _check_page(dets, masks, r, min_checked=30):
+    """The end-to-end gates of one page against the oracle's result r;
+    returns the number of rows held to the per-row gates (rows whose score
+    margins to both neighbours exceed 1e-4 — a property of the page)."""
     rd, rm = r["dets"], r["masks"].reshape(300, 200, 200)
     scores = rd[:, 1]
     n_checked = 0
@@ -107,9 +109,10 @@ def _check_page(dets, masks, r):
         assert iou >= 0.99, f"mask IoU row {i}: {iou}"
         if rd[i, 1] >= 0.3:
             assert dets[i, 6] == rd[i, 6], f"reading order row {i}"
-    assert n_checked >= 30, n_checked
+    assert n_checked >= min_checked, n_checked
     # the whole score column regardless of margins
     assert np.abs(dets[:, 1] - rd[:, 1]).max() < 1e-4
+    return n_checked
 
 
 @pytest.mark.parametrize("page", [0, 1])
@@ -124,7 +127,10 @@ def test_batch8_bench_pages_graph_replay(cuda, gguf_path, ref_model):
     forward workload), the 8 pages bench.py times on rank 0 (seeds
     1000..1007, 800 x 800), run twice — the first call eager, the second a
     replay of the captured CUDA graph — and every page of the replay held
-    to the end-to-end gates; eager and replay agree bit for bit."""
+    to the end-to-end gates; eager and replay agree bit for bit.  Random
+    weights leave some pages with many near-tied scores, so the rows with
+    clear margins are counted over the batch (at least 5 per page, 120 in
+    all) rather than 30 per page."""
     B = 8
     ctx = ppdl.Context(gguf_path, max_batch=B)
     imgs = np.stack([synth.synth_page(1000 + i) for i in range(B)])
@@ -132,11 +138,50 @@ def test_batch8_bench_pages_graph_replay(cuda, gguf_path, ref_model):
     eager = ctx.infer_batch(imgs, hw)
     replay = ctx.infer_batch(imgs, hw)
     ctx.close()
+    total = 0
     for i in range(B):
         np.testing.assert_array_equal(eager[i][0], replay[i][0])
         np.testing.assert_array_equal(eager[i][1], replay[i][1])
         r = ref_model.forward(imgs[i], 800, 800)
-        _check_page(replay[i][0], replay[i][1], r)
+        total += _check_page(replay[i][0], replay[i][1], r, min_checked=5)
+    assert total >= 120, total
+
+
+def test_pipelined_batches_with_packed_masks(cuda, gguf_path, pages, gpu_out):
+    """ppdl_submit_batch / ppdl_wait_batch: three batches in a row from
+    pinned host memory, two in flight; every result equals ppdl_infer_batch's
+    (dets bit for bit, masks after unpacking the bits, also through the C
+    expansion ppdl_expand_mask_bits); a ticket two submissions old is
+    reported as overwritten."""
+    import ctypes as C
+    import torch
+    ctx = ppdl.Context(gguf_path, max_batch=2)
+    base = np.stack([p[0] for p in pages])
+    hw = np.array([p[1] for p in pages], np.int32)
+    order = [[0, 1], [1, 0], [0, 1]]
+    bufs = [torch.from_numpy(np.ascontiguousarray(base[o])).pin_memory().numpy() for o in order]
+    hws = [np.ascontiguousarray(hw[o]) for o in order]
+    t0 = ctx.submit(bufs[0], hws[0])
+    t1 = ctx.submit(bufs[1], hws[1])
+    r0 = ctx.wait(t0, 2)
+    t2 = ctx.submit(bufs[2], hws[2])
+    r1 = ctx.wait(t1, 2)
+    r2 = ctx.wait(t2, 2)
+    with pytest.raises(RuntimeError):
+        ctx.wait(t0, 2)  # slot reused by t2
+    want = gpu_out[0]
+    for o, r in zip(order, (r0, r1, r2)):
+        for k, page in enumerate(o):
+            dets, bits = r[k]
+            np.testing.assert_array_equal(dets, want[page][0])
+            np.testing.assert_array_equal(ppdl.unpack_mask_bits(bits), want[page][1] != 0)
+    L = ppdl.lib()
+    L.ppdl_expand_mask_bits.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+    bits = np.ascontiguousarray(r2[0][1])
+    m32 = np.empty((300, 200, 200), np.int32)
+    L.ppdl_expand_mask_bits(bits.ctypes.data, m32.ctypes.data, 300)
+    np.testing.assert_array_equal(m32, want[0][1])
+    ctx.close()
 
 
 def test_single_page_api_matches_batch(cuda, gguf_path, pages, gpu_out):
