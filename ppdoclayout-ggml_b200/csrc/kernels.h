@@ -14,12 +14,14 @@ namespace ppdl {
 // ---- decoder / selection ops ------------------------------------------------
 // MSDeformAttn.  In-model: p1 = offsets [B*nq][192], p2 = logits [B*nq][96],
 // ref [B*nq][4].  Canonical: p1 = locations, p2 = softmax weights, ref unused.
-// val [B][13125][256], out [B*nq][256].  Rows of p1 / p2 lie ld1 / ld2
-// floats apart (192 / 96 when dense; the model's fused projection writes
-// both into one [B*nq][288] buffer).
+// val [B][13125][ldv] (256 channels used), out [B*nq][256].  Rows of p1 /
+// p2 lie ld1 / ld2 floats apart (192 / 96 when dense; the model's fused
+// projection writes both into one [B*nq][288] buffer); value rows ldv
+// floats apart (256 when dense; the six decoder layers' projections share
+// one [B][13125][1536] buffer).
 Status launch_msda(const float *val, const float *p1, const float *p2, const float *ref,
                    float *out, int nq, int batch, bool canon, int ld1, int ld2,
-                   cudaStream_t stream);
+                   cudaStream_t stream, int ldv = 256);
 
 // mask logits [rows][40000] -> [rows][4]
 Status launch_mask_box(const float *ml, float *out, int rows, cudaStream_t stream);

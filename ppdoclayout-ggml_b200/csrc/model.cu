@@ -926,21 +926,20 @@ public:
         conv1x1_tok(n16, source, 10000, "dec_in1");
         conv1x1_tok(n32, source, 12500, "dec_in2");
         dump_seq("source", source);
-        // the six layers' value projections of `source` (:836) on lane 1,
-        // beside the encoder head and the decoder chain, each on at most
-        // kVpCtas SMs so that the chain keeps the rest
-        S values[6];
-        int e_vp[6];
+        // the six layers' value projections of `source` (:836) as one GEMM
+        // of stacked weights, 13125*B x 1536 x 256, on lane 1 beside the
+        // encoder head, on at most kVpCtas SMs so that the chain keeps the
+        // rest; layer i's MSDA reads columns 256i .. 256i + 255 of each row
+        S values_all = seq(kNTok, 6 * kDM);
+        int e_vp_all;
         {
             const int e_src = mark();
             on_lane(1);
             after(e_src);
-            for (int i = 0; i < 6; i++) {
-                values[i] = seq(kNTok, kDM);
-                lin(source, values[i], "dec" + std::to_string(i) + ".ca.vp", ACT_NONE, S(),
-                    kVpCtas);
-                e_vp[i] = mark();
-            }
+            std::vector<std::string> vps;
+            for (int i = 0; i < 6; i++) vps.push_back("dec" + std::to_string(i) + ".ca.vp");
+            lin_cat(source, values_all, vps, "dec.ca.vp", ACT_NONE, S(), kVpCtas);
+            e_vp_all = mark();
             on_lane(0);
         }
         S memory = seq(kNTok, kDM), eo = seq(kNTok, kDM), om = seq(kNTok, kDM);
@@ -1033,7 +1032,7 @@ public:
         lin(ref, qp1, "qpos.0", ACT_RELU);
         for (int i = 0; i < 6; i++) {
             const std::string dp = "dec" + std::to_string(i);
-            const S value = values[i];
+            const float *value_p = values_all.p + (long long)i * kDM;
             S v = seq(kNQ, kDM);
             on_lane(2);
             after(e_x);
@@ -1048,11 +1047,11 @@ public:
             S z = seq(kNQ, kDM), sa_lg = seq(kNQ, 288), ca = seq(kNQ, kDM);
             ln(x, x1, dp + ".ln1", sa, qpos, z);  // x1 and z = x1 + qpos
             lin_cat(z, sa_lg, {dp + ".ca.so", dp + ".ca.aw"}, dp + ".ca.so_aw");
-            after(e_vp[i]);
+            if (i == 0) after(e_vp_all);
             push(dp + ".msda", PPDL_STEP_MSDA, 0.0,
                  4.0 * ((double)kNTok * kDM + kNQ * (192.0 + 96.0 + 4.0 + kDM)), [=]() {
-                return launch_msda(value.p, sa_lg.p, sa_lg.p + 192, ref.p, ca.p, kNQ, nb, false,
-                                   288, 288, st);
+                return launch_msda(value_p, sa_lg.p, sa_lg.p + 192, ref.p, ca.p, kNQ, nb, false,
+                                   288, 288, st, 6 * kDM);
             });
             S cao = seq(kNQ, kDM), x2 = seq(kNQ, kDM);
             lin(ca, cao, dp + ".ca.op");

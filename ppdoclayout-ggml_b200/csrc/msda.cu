@@ -15,11 +15,18 @@
 //            once instead of once per channel lane;
 //   phase 2  eight lanes own one pair, each lane one float4 of the head's
 //            32 channels, so one warp instruction fetches four whole
-//            128-byte rows (4 pairs) with 16-byte loads; each lane then
+//            128-byte rows (4 pairs) with 16-byte loads.  Per level a lane
+//            issues all 16 tap loads (4 points x 4 corners) before it
+//            accumulates them, so 16 rows per lane are in flight; taps
+//            outside the map or with zero weight point at the head's row 0
+//            with weight 0 (no branch around the loads), and adding
+//            0 * (finite value) leaves the sum unchanged.  Each lane
 //            accumulates its four channels over the 48 taps in the
 //            reference's l -> p -> corner order with separate multiply and
 //            add, which keeps the result bit-identical to the reference CPU
 //            op whenever expf agrees.
+// The value rows may be strided (ldv floats per token: the six decoder
+// layers' projections share one [B][13125][6 * 256] buffer).
 // The canonical (PyTorch MSDeformAttn) form takes locations and
 // post-softmax weights directly and shares phase 2.
 #include "common.cuh"
@@ -38,14 +45,16 @@ __constant__ int c_lvl_w[3] = {100, 50, 25};
 __constant__ int c_lvl_h[3] = {100, 50, 25};
 __constant__ int c_lvl_start[3] = {0, 10000, 12500};
 
+// (at most 5 blocks per SM: ptxas then keeps the 16 loads of a level in
+// registers at once; with no register cap it trades them for occupancy)
 template <bool kCanon>
-__global__ void __launch_bounds__(kThreads)
-msda_kernel(const float *__restrict__ val,  // [B][13125][256]
+__global__ void __launch_bounds__(kThreads, 5)
+msda_kernel(const float *__restrict__ val,  // [B][13125][ldv], 256 used
             const float *__restrict__ p1,   // offsets or locations [B*nq][ld1], 192 used
             const float *__restrict__ p2,   // logits or weights    [B*nq][ld2], 96 used
             const float *__restrict__ ref,  // [B*nq][4] (in-model only)
             float *__restrict__ out,        // [B*nq][256]
-            int nq, int npairs, int ld1, int ld2) {
+            int nq, int npairs, int ld1, int ld2, int ldv) {
     __shared__ float s_w[kPairs][12];
     __shared__ int s_idx[kPairs][kTapStride];
     __shared__ float s_tw[kPairs][kTapStride];
@@ -117,8 +126,9 @@ msda_kernel(const float *__restrict__ val,  // [B][13125][256]
         for (int k = 0; k < 4; k++) {
             const int xx = x0 + (k & 1), yy = y0 + (k >> 1);
             const bool ok = xx >= 0 && xx < W && yy >= 0 && yy < H && cw[k] != 0.0f;
-            s_idx[lp][pt * 4 + k] = ok ? st + yy * W + xx : -1;
-            s_tw[lp][pt * 4 + k] = __fmul_rn(wt, cw[k]);
+            // a skipped tap reads row 0 with weight 0
+            s_idx[lp][pt * 4 + k] = ok ? st + yy * W + xx : 0;
+            s_tw[lp][pt * 4 + k] = ok ? __fmul_rn(wt, cw[k]) : 0.0f;
         }
     }
     __syncthreads();
@@ -131,18 +141,21 @@ msda_kernel(const float *__restrict__ val,  // [B][13125][256]
     if (gp >= npairs) return;
     const int bq = gp >> 3, h = gp & 7;
     const int b = bq / nq;
-    const float *vb = val + (size_t)b * kNTok * kDM + h * kHD + c4;
+    const float *vb = val + (size_t)b * kNTok * ldv + h * kHD + c4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 12
-    for (int i = 0; i < kTaps; i++) {
-        const int idx = s_idx[lp][i];
-        if (idx >= 0) {
-            const float ww = s_tw[lp][i];
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(vb + (size_t)idx * kDM));
-            acc.x = __fadd_rn(acc.x, __fmul_rn(ww, v.x));
-            acc.y = __fadd_rn(acc.y, __fmul_rn(ww, v.y));
-            acc.z = __fadd_rn(acc.z, __fmul_rn(ww, v.z));
-            acc.w = __fadd_rn(acc.w, __fmul_rn(ww, v.w));
+#pragma unroll
+    for (int l = 0; l < 3; l++) {
+        float4 v[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            v[i] = __ldg(reinterpret_cast<const float4 *>(vb + (size_t)s_idx[lp][l * 16 + i] * ldv));
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const float ww = s_tw[lp][l * 16 + i];
+            acc.x = __fadd_rn(acc.x, __fmul_rn(ww, v[i].x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(ww, v[i].y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(ww, v[i].z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(ww, v[i].w));
         }
     }
     *reinterpret_cast<float4 *>(out + (size_t)bq * kDM + h * kHD + c4) = acc;
@@ -152,17 +165,17 @@ msda_kernel(const float *__restrict__ val,  // [B][13125][256]
 
 Status launch_msda(const float *val, const float *p1, const float *p2, const float *ref,
                    float *out, int nq, int batch, bool canon, int ld1, int ld2,
-                   cudaStream_t stream) {
-    if (nq <= 0 || batch <= 0 || ld1 < 192 || ld2 < 96) return ERR_SHAPE;
+                   cudaStream_t stream, int ldv) {
+    if (nq <= 0 || batch <= 0 || ld1 < 192 || ld2 < 96 || ldv < kDM || ldv % 4) return ERR_SHAPE;
     if (((uintptr_t)val | (uintptr_t)out) & 15) return ERR_SHAPE;
     const int npairs = batch * nq * kNH;
     const int grid = cdiv(npairs, kPairs);
     if (canon)
         msda_kernel<true><<<grid, kThreads, 0, stream>>>(val, p1, p2, ref, out, nq, npairs, ld1,
-                                                         ld2);
+                                                         ld2, ldv);
     else
         msda_kernel<false><<<grid, kThreads, 0, stream>>>(val, p1, p2, ref, out, nq, npairs, ld1,
-                                                          ld2);
+                                                          ld2, ldv);
     return cuda_status();
 }
 
