@@ -591,10 +591,247 @@ def run_forward(args, world, rank, local, pg):
         "gpu_launches": len(steps) * K,
         "clocks": clk,
     }
+    ctx.close()
+    if rank == 0 and world == 1 and not args.no_sweeps:
+        # the metric's other two clauses, measured after the timed region:
+        # MSDeformAttn HBM GB/s (config 1, B = 32) and conv TFLOPS (config 2)
+        line.update(kernel_sweeps(dev, hbm, tc))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_forward(gguf, budget_s=args.cpu_seconds)
-    ctx.close()
+        if not args.no_sweeps:
+            line["reference_gpu_bar"] = reference_gpu_bar(dev, hbm)
     return line
+
+
+# --------------------------------------------- per-kernel sweeps (configs 1, 2)
+L2_FLUSH_BYTES = 256 << 20  # written between timed launches (L2 is 126 MB)
+
+
+def _time_launches(fn, dev, iters=10, warmup=3, flush=True):
+    """Mean device time (ms) of fn() over iters launches, CUDA events on the
+    current stream around each launch, L2 flushed in between (untimed)."""
+    import torch
+    buf = torch.empty(L2_FLUSH_BYTES // 4, device=dev) if flush else None
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    st = torch.cuda.current_stream(dev)
+    tot = 0.0
+    for _ in range(iters):
+        if buf is not None:
+            buf.fill_(1.0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        fn()
+        b.record(st)
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    return tot / iters
+
+
+CONFIG2 = [
+    # (kind, IC, H, OC): config 2 of the baseline, NCHW, B in {1, 8}
+    ("3x3-s1", 128, 200, 128), ("3x3-s1", 256, 100, 256), ("3x3-s1", 512, 50, 512),
+    ("3x3-s1", 1024, 25, 1024),
+    ("1x1", 512, 100, 256), ("1x1", 1024, 50, 256), ("1x1", 2048, 25, 256),
+    ("3x3-s2", 128, 200, 256), ("3x3-s2", 512, 100, 512),
+]
+
+
+def _bind_conv_entries(L):
+    import ctypes as C
+    L.ppdl_conv3x3_wg4_workspace.argtypes = [C.c_int] * 5
+    L.ppdl_conv3x3_wg4_workspace.restype = C.c_longlong
+    L.ppdl_conv3x3_wg4_prepare.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    L.ppdl_conv3x3_wg4_run.argtypes = (
+        [C.c_void_p] + [C.c_int] * 4 + [C.c_longlong, C.c_void_p, C.c_int, C.c_int,
+                                        C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p])
+    L.ppdl_tf32_split.argtypes = [C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]
+    L.ppdl_gemm_tf32x3_presplit.argtypes = ([C.c_int] * 4 + [C.c_void_p, C.c_int, C.c_longlong,
+                                            C.c_longlong, C.c_void_p, C.c_void_p]
+                                            + [C.c_longlong] * 3 + [C.c_void_p])
+    L.ppdl_conv2d_tf32x3.argtypes = (
+        [C.c_void_p] + [C.c_int] * 4 + [C.c_longlong, C.c_void_p, C.c_void_p]
+        + [C.c_int] * 7 + [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p])
+    L.ppdl_conv2d_tf32x3_workspace.argtypes = [C.c_int] * 3
+    L.ppdl_conv2d_tf32x3_workspace.restype = C.c_longlong
+
+
+def _conv_case(L, g, dev, kind, IC, H, OC, Bc, stream, with_bar=False):
+    """One config-2 conv: (launch closure, direct FLOPs, executed GEMM
+    FLOPs[, cuBLAS FP32 SGEMM closure on the GEMM the reference runs])."""
+    import torch
+    import ppdl
+    K = 1 if kind == "1x1" else 3
+    S = 2 if kind == "3x3-s2" else 1
+    OH = (H + 2 * (K // 2) - K) // S + 1
+    x = torch.randn((Bc, IC, H, H), generator=g, device=dev)
+    wt = torch.randn((OC, IC, K, K), generator=g, device=dev) * (2.0 / (IC * K * K)) ** 0.5
+    bias = torch.randn((OC,), generator=g, device=dev) * 0.1
+    y = torch.empty((Bc, OC, OH, OH), device=dev)
+    direct = 2.0 * Bc * OH * OH * OC * IC * K * K
+    bar = None
+    if kind == "3x3-s1":
+        # filter transform once (as at model load), then the conv
+        work = torch.empty(L.ppdl_conv3x3_wg4_workspace(Bc, IC, OC, H, H), device=dev)
+        ppdl.check(L.ppdl_conv3x3_wg4_prepare(wt.data_ptr(), IC, OC, work.data_ptr(), stream()))
+
+        def f():
+            ppdl.check(L.ppdl_conv3x3_wg4_run(x.data_ptr(), Bc, IC, H, H, IC * H * H,
+                                              bias.data_ptr(), OC, 1, work.data_ptr(),
+                                              y.data_ptr(), OC * H * H, stream()))
+        T = ((H + 3) // 4) ** 2
+        executed = 2.0 * 36 * Bc * T * IC * OC
+        if with_bar:
+            # the reference's op 12: 36 strided-batched SGEMMs per page
+            ga = torch.randn((Bc * 36, T, IC), generator=g, device=dev)
+            gb = torch.randn((IC, OC), generator=g, device=dev)
+            bar = lambda: torch.matmul(ga, gb)  # noqa: E731
+    elif kind == "1x1":
+        M = H * H
+        ws = torch.empty(2 * OC * IC, device=dev)
+        ppdl.check(L.ppdl_tf32_split(wt.data_ptr(), OC * IC, ws.data_ptr(), stream()))
+
+        def f():
+            ppdl.check(L.ppdl_gemm_tf32x3_presplit(M, OC, IC, Bc, x.data_ptr(), 1, M, IC * M,
+                                                   ws.data_ptr(), y.data_ptr(), 1, M, OC * M,
+                                                   stream()))
+        executed = direct
+        if with_bar:
+            w2, x2 = wt.view(OC, IC), x.view(Bc, IC, M)
+            bar = lambda: torch.matmul(w2, x2)  # noqa: E731
+    else:
+        ws = torch.empty(L.ppdl_conv2d_tf32x3_workspace(IC, OC, 3), device=dev)
+
+        def f():
+            ppdl.check(L.ppdl_conv2d_tf32x3(x.data_ptr(), Bc, IC, H, H, IC * H * H, wt.data_ptr(),
+                                            bias.data_ptr(), OC, 3, 2, 1, OH, OH, 1,
+                                            ws.data_ptr(), y.data_ptr(), OC * OH * OH, stream()))
+        executed = direct
+        if with_bar:
+            # the reference's im2col + mul_mat: the GEMM alone
+            ga = torch.randn((Bc, OH * OH, IC * 9), generator=g, device=dev)
+            gb = torch.randn((IC * 9, OC), generator=g, device=dev)
+            bar = lambda: torch.matmul(ga, gb)  # noqa: E731
+    if with_bar:
+        return f, direct, executed, bar
+    return f, direct, executed
+
+
+def kernel_sweeps(dev, hbm, tc):
+    """Config 1 (MSDeformAttn alone, canonical form, B = 32) and config 2
+    (the conv sweep at B = 1 and 8) through this build's C ABI entry points
+    — the kernels the forward runs — with cuBLAS FP32 SGEMM (TF32 off, the
+    reference's GEMM mode, patches/ggml-ppdl.patch:14-16, 650-665, 787-802)
+    timed on each conv's GEMM beside it as the same-box bar."""
+    import ctypes as C
+    import torch
+    import ppdl
+    L = ppdl.lib()
+    stream = lambda: torch.cuda.current_stream(dev).cuda_stream  # noqa: E731
+    out = {}
+    # ---- config 1
+    B = MSDA_B
+    val, loc, w = msda_inputs_torch(B, 4321, dev)
+    o = torch.empty((B, NQ, 256), device=dev)
+    desc = ppdl.make_desc(ppdl.OP_MSDEF, o, [val, loc, w], params=[1],
+                          dst_ne=[256, NQ, B], src_ne=[[256, NTOK, B], [192, NQ, B], [96, NQ, B]])
+    alg, _ = msda_algorithmic_bytes(loc, w)
+    ms = _time_launches(lambda: ppdl.check(L.ppdl_op_launch(C.byref(desc), C.c_void_p(stream()))),
+                        dev)
+    out["config1_msda"] = {"pages": B, "ms": round(ms, 5), "gbs": round(alg / ms / 1e6, 1),
+                           "frac_of_hbm": round(alg / ms / 1e6 / hbm, 4),
+                           "algorithmic_bytes": alg, "l2": "flushed between launches"}
+    del val, loc, w, o
+    # ---- config 2
+    _bind_conv_entries(L)
+    tf32_was = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    rows = []
+    g = torch.Generator(device=dev).manual_seed(99)
+    try:
+        for kind, IC, H, OC in CONFIG2:
+            for Bc in (1, 8):
+                f, direct, executed, bar = _conv_case(L, g, dev, kind, IC, H, OC, Bc, stream,
+                                                      with_bar=True)
+                ms = _time_launches(f, dev)
+                ms_bar = _time_launches(bar, dev)
+                rows.append({"conv": f"{kind} {H}x{H}x{IC}->{OC}", "pages": Bc,
+                             "ms": round(ms, 4), "tflops_direct": round(direct / ms / 1e9, 2),
+                             "tflops_executed": round(executed / ms / 1e9, 2),
+                             "frac_of_3xtf32": round(executed / ms / 1e9 / tc, 4),
+                             "sgemm_gemm_only_ms": round(ms_bar, 4),
+                             "speedup_vs_sgemm": round(ms_bar / ms, 2)})
+                del f, bar
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32_was
+    out["config2_conv"] = rows
+    out["config2_note"] = ("ms: this build's conv with its weights prepared beforehand as at model "
+                           "load (Winograd: input transform + 36-plane GEMM + output transform; "
+                           "1x1: the GEMM; k3-s2: windowed implicit GEMM, its weight split "
+                           "included) with bias + ReLU; sgemm_gemm_only_ms: "
+                           "cuBLAS FP32 SGEMM, TF32 off, on the GEMM the reference runs for that "
+                           "conv (its transforms / im2col not counted); L2 flushed between "
+                           "launches")
+    return out
+
+
+def reference_gpu_bar(dev, hbm):
+    """The reference's own CUDA kernels for MSDeformAttn and mask->box
+    (compiled for sm_100a from its ggml patch into oracle/_ref/, one launch
+    per page as the reference runs them) timed beside this build's kernels
+    on the same inputs: config 1 at B = 32 (in-model form with reference
+    boxes (0, 0, 8, 8), so the sampling locations are the config's) and
+    mask->box over 8 pages of 300 masks."""
+    import ctypes as C
+    import torch
+    import ppdl
+    so = os.path.join(ROOT, "oracle", "_ref", "librefkern.so")
+    if not os.path.exists(so):
+        return {"unavailable": "oracle/_ref/librefkern.so not built (needs the reference "
+                               "checkout at build time)"}
+    R = C.CDLL(so)
+    R.refkern_msdeform.argtypes = [C.c_void_p] * 5 + [C.c_int, C.c_int, C.c_void_p]
+    R.refkern_mask_box.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+    L = ppdl.lib()
+    st = lambda: C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)  # noqa: E731
+    B = MSDA_B
+    g = torch.Generator(device=dev).manual_seed(4321)
+    val = torch.randn((B, NTOK, 256), generator=g, device=dev)
+    off = torch.rand((B, NQ, 192), generator=g, device=dev)
+    lg = torch.randn((B, NQ, 96), generator=g, device=dev)
+    ref = torch.tensor([0.0, 0.0, 8.0, 8.0], device=dev).repeat(B, NQ, 1).contiguous()
+    o1 = torch.empty((B, NQ, 256), device=dev)
+    o2 = torch.empty((B, NQ, 256), device=dev)
+    desc = ppdl.make_desc(ppdl.OP_MSDEF, o1, [val, off, lg, ref], params=[0],
+                          dst_ne=[256, NQ, B],
+                          src_ne=[[256, NTOK, B], [192, NQ, B], [96, NQ, B], [4, NQ, B]])
+    ours = _time_launches(lambda: ppdl.check(L.ppdl_op_launch(C.byref(desc), st())), dev)
+    theirs = _time_launches(lambda: R.refkern_msdeform(val.data_ptr(), off.data_ptr(),
+                                                       lg.data_ptr(), ref.data_ptr(),
+                                                       o2.data_ptr(), NQ, B, st()), dev)
+    torch.cuda.synchronize(dev)
+    msda_diff = float((o1 - o2).abs().max())
+    rows = 8 * NQ
+    ml = torch.randn((rows, 40000), generator=g, device=dev) - 1.5
+    b1 = torch.empty((rows, 4), device=dev)
+    b2 = torch.empty((rows, 4), device=dev)
+    mdesc = ppdl.make_desc(ppdl.OP_MASKBOX, b1, [ml], dst_ne=[4, rows], src_ne=[[40000, rows]])
+    ours_mb = _time_launches(lambda: ppdl.check(L.ppdl_op_launch(C.byref(mdesc), st())), dev)
+    theirs_mb = _time_launches(lambda: R.refkern_mask_box(ml.data_ptr(), b2.data_ptr(), rows,
+                                                          st()), dev)
+    torch.cuda.synchronize(dev)
+    mb_bytes = rows * 40000 * 4
+    return {
+        "kind": "reference CUDA kernels (patches/ggml-ppdl.patch:212-312) compiled for sm_100a",
+        "msda_config1_b32": {"ours_ms": round(ours, 5), "reference_ms": round(theirs, 5),
+                             "speedup": round(theirs / ours, 2), "max_abs_diff": msda_diff},
+        "mask_box_8_pages": {"ours_ms": round(ours_mb, 5), "reference_ms": round(theirs_mb, 5),
+                             "ours_gbs": round(mb_bytes / ours_mb / 1e6, 1),
+                             "reference_gbs": round(mb_bytes / theirs_mb / 1e6, 1),
+                             "speedup": round(theirs_mb / ours_mb, 2),
+                             "max_abs_diff": float((b1 - b2).abs().max())},
+    }
 
 
 def cpu_baseline_forward(gguf, budget_s=10.0, sample_pages=None):
@@ -622,9 +859,10 @@ def cpu_baseline_forward(gguf, budget_s=10.0, sample_pages=None):
 def run_reference(args, world, rank):
     if rank != 0:
         return None
-    if args.workload == "gemm":
-        return {"impl": "reference", "unavailable": "the gemm workload is a kernel-level "
-                "measurement of this build only; the reference arm times the forward"}
+    if args.workload in ("gemm", "conv"):
+        return {"impl": "reference", "unavailable": f"the {args.workload} workload is a kernel-level "
+                "measurement of this build only (its same-box bar, cuBLAS FP32 SGEMM, is part of "
+                "the forward workload's config2_conv); the reference arm times the forward"}
     if args.workload == "forward":
         import synth
         gguf = synth.cached_gguf(0)
@@ -746,17 +984,73 @@ def run_gemm(args, world, rank, local, pg):
     }
 
 
+def run_conv(args, world, rank, local, pg):
+    """Config 2 of the baseline, one conv shape: the forward's conv path
+    through the C ABI (Winograd F(4,3) for 3x3-s1, the 3xTF32 GEMM for 1x1,
+    the windowed implicit GEMM for 3x3-s2), weights prepared beforehand as at
+    model load (the k3-s2 entry splits its weights in the call), bias + ReLU.
+    `value` is conv TFLOP/s on the direct-conv FLOPs 2*B*OH*OW*OC*IC*K^2;
+    the L2 is flushed between launches."""
+    import ctypes as C
+    import torch
+    import ppdl
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    kind, IC, H, OC, Bc = (args.conv.split(",") if args.conv else ("3x3-s1", 256, 100, 256, 8))
+    IC, H, OC, Bc = int(IC), int(H), int(OC), int(Bc)
+    if kind not in ("3x3-s1", "1x1", "3x3-s2"):
+        raise SystemExit(f"--conv kind must be 3x3-s1, 1x1 or 3x3-s2, not {kind}")
+    hbm, bf16, peak_kind = _peaks()
+    tc = bf16 / 6.0
+    L = ppdl.lib()
+    _bind_conv_entries(L)
+    stream = lambda: torch.cuda.current_stream(dev).cuda_stream  # noqa: E731
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    f, direct, executed = _conv_case(L, g, dev, kind, IC, H, OC, Bc, stream)
+    for _ in range(args.warmup):
+        f()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    barrier(pg)
+    clocks.start()
+    ms = _time_launches(f, dev, iters=args.steps, warmup=0)
+    barrier(pg)
+    clk = clocks.stop()
+    ms = max_over_ranks(pg, ms)
+    per_gpu = direct / ms / 1e9
+    return {
+        "metric": METRIC, "value": round(per_gpu * world, 2), "unit": "conv TFLOP/s (direct FLOPs)",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: activations N(0,1), Kaiming weights, bias N(0,0.1), ReLU",
+        "config": {"workload": f"config 2: {kind} conv {H}x{H}x{IC}->{OC}, {Bc} pages",
+                   "l2": "flushed between launches", "parallelism": f"dp{world} (no collective)"},
+        "roofline": {"bound": "tensor", "achieved": round(executed / ms / 1e9, 2),
+                     "peak": round(tc, 1), "unit": "TFLOP/s",
+                     "frac": round(executed / ms / 1e9 / tc, 4),
+                     "peak_kind": f"{peak_kind} bf16 dense burst / 6 (3xTF32)",
+                     "flops": "executed GEMM FLOPs (Winograd: 2*36*T*IC*OC per page)"},
+        "gpu_launches": args.steps * (3 if kind == "3x3-s1" else (2 if kind == "3x3-s2" else 1)),
+        "clocks": clk,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="forward", choices=["forward", "msda", "gemm"])
+    ap.add_argument("--workload", default="forward", choices=["forward", "msda", "gemm", "conv"])
+    ap.add_argument("--conv", default="",
+                    help="conv workload: kind,IC,H,OC,pages with kind 3x3-s1, 1x1 or 3x3-s2 "
+                         "(default 3x3-s1,256,100,256,8)")
     ap.add_argument("--gemm", default="",
                     help="gemm workload shape M,N,K,pages (default 40000,256,1024,8)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweeps", action="store_true",
+                    help="forward workload: skip the config-1 / config-2 kernel sweeps")
     ap.add_argument("--pages", type=int, default=0,
                     help="pages per GPU per step of the forward workload (default 8, config 3); "
                          "smaller values are for profiler captures")
@@ -774,6 +1068,8 @@ def main():
             line = run_forward(args, world, rank, local, pg)
         elif args.workload == "gemm":
             line = run_gemm(args, world, rank, local, pg)
+        elif args.workload == "conv":
+            line = run_conv(args, world, rank, local, pg)
         else:
             line = run_msda(args, world, rank, local, pg)
         if rank == 0 and line is not None:

@@ -165,6 +165,29 @@ PPDL_OPS_API int ppdl_conv3x3_wg4_tf32x3(const float * x, int batch, int IC, int
 /* Floats of work that ppdl_conv3x3_wg4_tf32x3 needs (0 for non-positive sizes). */
 PPDL_OPS_API long long ppdl_conv3x3_wg4_workspace(int batch, int IC, int OC, int H, int W);
 
+/* ppdl_conv3x3_wg4_tf32x3 in two parts, for weights used many times (the
+   reference transforms its filters once at load, repack_convs at
+   src/ppdoclayout.cpp:251-346): _prepare writes the transformed filter and
+   its TF32 halves into the head of work; _run then convolves with them
+   (same arguments minus weight).  work as for ppdl_conv3x3_wg4_tf32x3, with
+   batch, H and W of the largest _run. */
+PPDL_OPS_API int ppdl_conv3x3_wg4_prepare(const float * weight, int IC, int OC, float * work,
+                                          void * stream);
+PPDL_OPS_API int ppdl_conv3x3_wg4_run(const float * x, int batch, int IC, int H, int W,
+                                      long long x_bs, const float * bias, int OC, int act,
+                                      float * work, float * y, long long y_bs, void * stream);
+
+/* ppdl_gemm_tf32x3 in two parts, for a B used many times: ppdl_tf32_split
+   writes the TF32 halves of the n floats of B into b_split (2n floats: hi,
+   then lo); ppdl_gemm_tf32x3_presplit multiplies with them (arguments as
+   ppdl_gemm_tf32x3, b_split read only). */
+PPDL_OPS_API int ppdl_tf32_split(const float * B, long long n, float * b_split, void * stream);
+PPDL_OPS_API int ppdl_gemm_tf32x3_presplit(int M, int N, int K, int batch, const float * A,
+                                           int a_m_major, long long lda, long long a_bs,
+                                           const float * b_split, float * C,
+                                           long long ldc_m, long long ldc_n, long long c_bs,
+                                           void * stream);
+
 /* Extension (the reference's depthwise conv is ggml_conv_2d_dw_direct,
    src/ppdoclayout.cpp:400-404, a ggml op rather than a tagged PPDL op):
    the depthwise conv of the backbone's downsampling and light blocks.

@@ -438,15 +438,24 @@ __device__ __forceinline__ void gather_issue(const TcGather &g, int K, const flo
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// 3xTF32 split of 8 values into TMEM: hi = x rounded to the nearest TF32
-// (cvt.rna), lo = x - hi (exact in FP32, either sign, so the tensor core's
-// truncation of lo carries no bias); hi goes to columns col .. col + 7 of
-// the warp's lane quadrant, lo 32 columns further.
+// 3xTF32 split of 8 values into TMEM: hi = x rounded to the nearest TF32,
+// ties away from zero, lo = x - hi (exact in FP32, either sign, so the
+// tensor core's truncation of lo carries no bias); hi goes to columns
+// col .. col + 7 of the warp's lane quadrant, lo 32 columns further.  The
+// rounding is done on the bit pattern — add half a TF32 unit (bit 12) to
+// the sign-magnitude encoding and clear the 13 low mantissa bits, carries
+// running into the exponent — which gives cvt.rna.tf32.f32's result for
+// every finite x (measured bitwise-equal GEMM outputs) in two integer ops
+// (the split runs at the converter warps' throughput limit).
+__device__ __forceinline__ uint32_t tf32_rna_bits(float x) {
+    return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
+}
+
 __device__ __forceinline__ void split_store8(uint32_t col, const float (&x)[8]) {
     uint32_t h[8], l[8];
 #pragma unroll
     for (int u = 0; u < 8; u++) {
-        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h[u]) : "f"(x[u]));
+        h[u] = tf32_rna_bits(x[u]);
         l[u] = __float_as_uint(x[u] - __uint_as_float(h[u]));
     }
     tmem_st8(col, h);

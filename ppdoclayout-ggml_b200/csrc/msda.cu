@@ -45,10 +45,10 @@ __constant__ int c_lvl_w[3] = {100, 50, 25};
 __constant__ int c_lvl_h[3] = {100, 50, 25};
 __constant__ int c_lvl_start[3] = {0, 10000, 12500};
 
-// (at most 5 blocks per SM: ptxas then keeps the 16 loads of a level in
-// registers at once; with no register cap it trades them for occupancy)
+// (8 blocks per SM, 64 registers a thread: measured fastest of 4..10 blocks;
+// with no bound ptxas keeps fewer loads in flight)
 template <bool kCanon>
-__global__ void __launch_bounds__(kThreads, 5)
+__global__ void __launch_bounds__(kThreads, 8)
 msda_kernel(const float *__restrict__ val,  // [B][13125][ldv], 256 used
             const float *__restrict__ p1,   // offsets or locations [B*nq][ld1], 192 used
             const float *__restrict__ p2,   // logits or weights    [B*nq][ld2], 96 used

@@ -69,6 +69,11 @@ PPDL_OPS_API const char *ppdl_op_last_error(void) { return g_err; }
 
 PPDL_OPS_API int ppdl_op_device_error(void) { return ppdl::tc_error_fetch_and_clear() ? 1 : 0; }
 
+PPDL_OPS_API int ppdl_gemm_tf32x3_presplit(int M, int N, int K, int batch, const float *A,
+                                           int a_m_major, long long lda, long long a_bs,
+                                           const float *b_split, float *C, long long ldc_m,
+                                           long long ldc_n, long long c_bs, void *stream);
+
 PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float *A, int a_m_major,
                                   long long lda, long long a_bs, const float *B, float *b_split,
                                   float *C, long long ldc_m, long long ldc_n, long long c_bs,
@@ -77,19 +82,11 @@ PPDL_OPS_API int ppdl_gemm_tf32x3(int M, int N, int K, int batch, const float *A
     if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || !A || !B || !b_split || !C)
         return fail(PPDL_ERR_SHAPE, "gemm: bad sizes or null pointer");
     cudaStream_t st = (cudaStream_t)stream;
-    float *hi = b_split, *lo = b_split + (long long)N * K;
-    ppdl::Status s = ppdl::launch_tf32_split(B, hi, lo, (long long)N * K, st);
+    ppdl::Status s = ppdl::launch_tf32_split(B, b_split, b_split + (long long)N * K,
+                                             (long long)N * K, st);
     if (s != ppdl::OK) return to_status(s);
-    ppdl::TcEpilogue e;
-    e.C = C; e.ldc_m = ldc_m; e.ldc_n = ldc_n; e.c_bs = c_bs;
-    ppdl::TcGemm g;
-    // an M-major A whose channel rows TMA cannot take as one tensor (lda or
-    // the base not 16-byte aligned, e.g. 25 x 25 planes) is loaded row by row
-    if (!ppdl::tc_gemm_plan(&g, M, N, K, batch, A, a_m_major ? 1 : 0, lda, a_bs, hi, lo, 1, e) &&
-        !(a_m_major && ppdl::tc_gemm_plan_rows(&g, M, N, K, batch, A, lda, a_bs, hi, lo, e)))
-        return fail(PPDL_ERR_SHAPE, "gemm: operands violate the TMA rules (16-byte aligned "
-                                    "b_split and a_bs, K a multiple of 4; K-major A also lda)");
-    return to_status(ppdl::launch_tc_gemm(g, st));
+    return ppdl_gemm_tf32x3_presplit(M, N, K, batch, A, a_m_major, lda, a_bs, b_split, C, ldc_m,
+                                     ldc_n, c_bs, stream);
 }
 
 PPDL_OPS_API int ppdl_depthwise_conv2d(const float *x, int batch, int C, int H, int W,
@@ -175,13 +172,26 @@ PPDL_OPS_API long long ppdl_conv3x3_wg4_workspace(int batch, int IC, int OC, int
     return q.wg4 + 2 * q.split + q.dt + q.yt;
 }
 
-PPDL_OPS_API int ppdl_conv3x3_wg4_tf32x3(const float *x, int batch, int IC, int H, int W,
-                                         long long x_bs, const float *weight, const float *bias,
-                                         int OC, int act, float *work, float *y, long long y_bs,
-                                         void *stream) {
+PPDL_OPS_API int ppdl_conv3x3_wg4_prepare(const float *weight, int IC, int OC, float *work,
+                                          void *stream) {
     g_err[0] = 0;
-    if (!x || !weight || !work || !y || batch <= 0 || IC <= 0 || OC <= 0 || H <= 0 || W <= 0 ||
-        act < 0 || act > 3)
+    if (!weight || !work || IC <= 0 || OC <= 0 || IC % 4 || ((uintptr_t)work & 15))
+        return fail(PPDL_ERR_SHAPE, "conv3x3 prepare: bad sizes, IC not a multiple of 4 or "
+                                    "misaligned workspace");
+    cudaStream_t st = (cudaStream_t)stream;
+    const Wg4Parts q = wg4_parts(1, IC, OC, 1, 1);
+    float *wg4 = work, *hi = wg4 + q.wg4, *lo = hi + q.split;
+    ppdl::Status s = ppdl::launch_wg4_filter(weight, wg4, IC, OC, st);
+    if (s == ppdl::OK) s = ppdl::launch_wg4_kmajor_split(wg4, hi, lo, IC, OC, st);
+    return to_status(s);
+}
+
+PPDL_OPS_API int ppdl_conv3x3_wg4_run(const float *x, int batch, int IC, int H, int W,
+                                      long long x_bs, const float *bias, int OC, int act,
+                                      float *work, float *y, long long y_bs, void *stream) {
+    g_err[0] = 0;
+    if (!x || !work || !y || batch <= 0 || IC <= 0 || OC <= 0 || H <= 0 || W <= 0 || act < 0 ||
+        act > 3)
         return fail(PPDL_ERR_SHAPE, "conv3x3: bad sizes, activation or null pointer");
     if (IC % 4 || ((uintptr_t)work & 15))
         return fail(PPDL_ERR_SHAPE, "conv3x3: IC must be a multiple of 4 and the workspace "
@@ -196,14 +206,51 @@ PPDL_OPS_API int ppdl_conv3x3_wg4_tf32x3(const float *x, int batch, int IC, int 
     if (!ppdl::tc_gemm_plan(&g, T, OC, IC, batch * 36, dt, 1, Tp, (long long)IC * Tp, hi, lo, 36,
                             e))
         return fail(PPDL_ERR_SHAPE, "conv3x3: the plane GEMM cannot be planned");
-    ppdl::Status s = ppdl::launch_wg4_filter(weight, wg4, IC, OC, st);
-    if (s == ppdl::OK) s = ppdl::launch_wg4_kmajor_split(wg4, hi, lo, IC, OC, st);
-    if (s == ppdl::OK) s = ppdl::launch_wg4_input(x, x_bs, dt, IC, H, W, TW, TH, 1, batch, st, Tp);
+    ppdl::Status s = ppdl::launch_wg4_input(x, x_bs, dt, IC, H, W, TW, TH, 1, batch, st, Tp);
     if (s == ppdl::OK) s = ppdl::launch_tc_gemm(g, st);
     if (s == ppdl::OK)
         s = ppdl::launch_wg4_output(yt, bias, y, y_bs, nullptr, 0, 0, OC, H, W, TW, TH, act,
                                     batch, st, Tp);
     return to_status(s);
+}
+
+PPDL_OPS_API int ppdl_conv3x3_wg4_tf32x3(const float *x, int batch, int IC, int H, int W,
+                                         long long x_bs, const float *weight, const float *bias,
+                                         int OC, int act, float *work, float *y, long long y_bs,
+                                         void *stream) {
+    if (!x || !weight || !work || !y || batch <= 0 || IC <= 0 || OC <= 0 || H <= 0 || W <= 0 ||
+        act < 0 || act > 3) {
+        g_err[0] = 0;
+        return fail(PPDL_ERR_SHAPE, "conv3x3: bad sizes, activation or null pointer");
+    }
+    const int rc = ppdl_conv3x3_wg4_prepare(weight, IC, OC, work, stream);
+    if (rc != PPDL_OK) return rc;
+    return ppdl_conv3x3_wg4_run(x, batch, IC, H, W, x_bs, bias, OC, act, work, y, y_bs, stream);
+}
+
+PPDL_OPS_API int ppdl_tf32_split(const float *w, long long n, float *b_split, void *stream) {
+    g_err[0] = 0;
+    if (!w || !b_split || n <= 0) return fail(PPDL_ERR_SHAPE, "tf32_split: bad size or pointer");
+    return to_status(ppdl::launch_tf32_split(w, b_split, b_split + n, n, (cudaStream_t)stream));
+}
+
+PPDL_OPS_API int ppdl_gemm_tf32x3_presplit(int M, int N, int K, int batch, const float *A,
+                                           int a_m_major, long long lda, long long a_bs,
+                                           const float *b_split, float *C, long long ldc_m,
+                                           long long ldc_n, long long c_bs, void *stream) {
+    g_err[0] = 0;
+    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || !A || !b_split || !C)
+        return fail(PPDL_ERR_SHAPE, "gemm: bad sizes or null pointer");
+    cudaStream_t st = (cudaStream_t)stream;
+    const float *hi = b_split, *lo = b_split + (long long)N * K;
+    ppdl::TcEpilogue e;
+    e.C = C; e.ldc_m = ldc_m; e.ldc_n = ldc_n; e.c_bs = c_bs;
+    ppdl::TcGemm g;
+    if (!ppdl::tc_gemm_plan(&g, M, N, K, batch, A, a_m_major ? 1 : 0, lda, a_bs, hi, lo, 1, e) &&
+        !(a_m_major && ppdl::tc_gemm_plan_rows(&g, M, N, K, batch, A, lda, a_bs, hi, lo, e)))
+        return fail(PPDL_ERR_SHAPE, "gemm: operands violate the TMA rules (16-byte aligned "
+                                    "b_split and a_bs, K a multiple of 4; K-major A also lda)");
+    return to_status(ppdl::launch_tc_gemm(g, st));
 }
 
 PPDL_OPS_API int ppdl_op_launch(const ppdl_op_desc *d, void *stream_ptr) {

@@ -120,3 +120,28 @@ def test_tc_gemm_rejects_unaligned_strides(cuda):
                             ws.data_ptr(), Cc.data_ptr(), 1, 625, 0,
                             torch.cuda.current_stream().cuda_stream)
     assert st == ppdl.PPDL_ERR_SHAPE
+
+
+def test_presplit_gemm_matches_one_call(cuda):
+    """ppdl_tf32_split + ppdl_gemm_tf32x3_presplit (weights split once, as at
+    model load) give the same bits as ppdl_gemm_tf32x3."""
+    import ctypes as C
+    L = _lib()
+    L.ppdl_tf32_split.argtypes = [C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]
+    L.ppdl_gemm_tf32x3_presplit.argtypes = ([C.c_int] * 4 + [C.c_void_p, C.c_int, C.c_longlong,
+                                            C.c_longlong, C.c_void_p, C.c_void_p]
+                                            + [C.c_longlong] * 3 + [C.c_void_p])
+    M, N, K, B = 2500, 192, 320, 2
+    g = torch.Generator().manual_seed(5)
+    A = torch.randn((B, K, M), generator=g).to(cuda)
+    W = (torch.randn((N, K), generator=g) / K ** 0.5).to(cuda)
+    ws1, ws2 = torch.empty(2 * N * K, device=cuda), torch.empty(2 * N * K, device=cuda)
+    c1, c2 = torch.empty((B, N, M), device=cuda), torch.empty((B, N, M), device=cuda)
+    s = torch.cuda.current_stream().cuda_stream
+    assert L.ppdl_gemm_tf32x3(M, N, K, B, A.data_ptr(), 1, M, K * M, W.data_ptr(), ws1.data_ptr(),
+                              c1.data_ptr(), 1, M, N * M, s) == ppdl.PPDL_OK
+    assert L.ppdl_tf32_split(W.data_ptr(), N * K, ws2.data_ptr(), s) == ppdl.PPDL_OK
+    assert L.ppdl_gemm_tf32x3_presplit(M, N, K, B, A.data_ptr(), 1, M, K * M, ws2.data_ptr(),
+                                       c2.data_ptr(), 1, M, N * M, s) == ppdl.PPDL_OK
+    torch.cuda.synchronize()
+    assert torch.equal(c1, c2)
