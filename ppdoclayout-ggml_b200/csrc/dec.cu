@@ -206,33 +206,42 @@ __global__ void gather_rows_kernel(const float *__restrict__ x, const int32_t *_
 
 // ---- postprocess ---------------------------------------------------------------
 // votes[j] = sum_{i != j} sigmoid(order[j + 300 i] - order[i + 300 j]) in i
-// order; rank = position in the stable ascending sort of the votes
-__global__ void pp_votes_rank_kernel(const float *__restrict__ order, int32_t *__restrict__ rank) {
-    __shared__ float s_votes[kNQ];
-    const int b = blockIdx.x;
+// order (src/ppdoclayout.cpp:935-945).  A block takes 16 consecutive j of a
+// page: it stages the 16 rows order[j][*] and the 16 columns order[*][j]
+// in shared memory with coalesced loads, all 256 threads evaluate the
+// sigmoid terms, and one thread per j adds its 300 terms in i order (the
+// reference's order: the sums are bit-identical).  The ranks follow in
+// pp_select_kernel.
+constexpr int kVoteJ = 16;
+__global__ void __launch_bounds__(256)
+pp_votes_kernel(const float *__restrict__ order, float *__restrict__ votes) {
+    __shared__ float s_row[kVoteJ][kNQ + 1];  // order[j0 + jj][i]
+    __shared__ float s_col[kNQ][kVoteJ + 1];  // order[i][j0 + jj], then the terms
+    const int b = blockIdx.y, j0 = blockIdx.x * kVoteJ;
+    const int nj = min(kVoteJ, kNQ - j0);
     const float *o = order + (long long)b * kNQ * kNQ;
-    for (int j = threadIdx.x; j < kNQ; j += blockDim.x) {
-        // the same sum in the same order; the diagonal adds an exact +0 (acc
-        // starts at +0 and only grows), so the loop can be unrolled and the
-        // loads of ten terms are in flight together
-        float acc = 0.0f;
-#pragma unroll 10
-        for (int i = 0; i < kNQ; i++) {
-            const float diff = __fsub_rn(o[j + kNQ * i], o[i + kNQ * j]);
-            const float term = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-diff)));
-            acc = __fadd_rn(acc, i == j ? 0.0f : term);
-        }
-        s_votes[j] = acc;
+    for (int e = threadIdx.x; e < kVoteJ * kNQ; e += blockDim.x) {
+        const int jj = e / kNQ, i = e - jj * kNQ;
+        s_row[jj][i] = jj < nj ? o[(j0 + jj) * kNQ + i] : 0.0f;
+    }
+    for (int e = threadIdx.x; e < kNQ * kVoteJ; e += blockDim.x) {
+        const int i = e / kVoteJ, jj = e - i * kVoteJ;
+        s_col[i][jj] = jj < nj ? o[i * kNQ + j0 + jj] : 0.0f;
     }
     __syncthreads();
-    for (int j = threadIdx.x; j < kNQ; j += blockDim.x) {
-        const float vj = s_votes[j];
-        int r = 0;
-        for (int k = 0; k < kNQ; k++) {
-            const float vk = s_votes[k];
-            r += (vk < vj) || (vk == vj && k < j);
-        }
-        rank[b * kNQ + j] = r;
+    // term(i, j) = sigmoid(order[j + 300 i] - order[i + 300 j]); the
+    // diagonal adds an exact +0 (the sum starts at +0 and only grows)
+    for (int e = threadIdx.x; e < kNQ * kVoteJ; e += blockDim.x) {
+        const int i = e / kVoteJ, jj = e - i * kVoteJ;
+        const float diff = __fsub_rn(s_col[i][jj], s_row[jj][i]);
+        const float term = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-diff)));
+        s_col[i][jj] = (i == j0 + jj) ? 0.0f : term;
+    }
+    __syncthreads();
+    if (threadIdx.x < nj) {
+        float acc = 0.0f;
+        for (int i = 0; i < kNQ; i++) acc = __fadd_rn(acc, s_col[i][threadIdx.x]);
+        votes[b * kNQ + j0 + threadIdx.x] = acc;
     }
 }
 
@@ -240,15 +249,29 @@ __global__ void pp_votes_rank_kernel(const float *__restrict__ order, int32_t *_
 // detections rows; one block per page, block radix select (select.cuh)
 __global__ void __launch_bounds__(1024)
 pp_select_kernel(const float *__restrict__ logits, const float *__restrict__ boxes,
-                 const int32_t *__restrict__ rank, const int32_t *__restrict__ ori_hw,
+                 const float *__restrict__ votes, const int32_t *__restrict__ ori_hw,
                  float *__restrict__ dets, int32_t *__restrict__ sel) {
     constexpr int N = kNQ * kNC;
     extern __shared__ unsigned long long s_key[];  // N keys (dynamic)
     __shared__ unsigned long long s_top[kSelectMax];
+    __shared__ float s_votes[kNQ];
+    __shared__ int s_rank[kNQ];
     const int b = blockIdx.x;
     const float *lg = logits + (long long)b * N;
     for (int i = threadIdx.x; i < N; i += blockDim.x)
         s_key[i] = select_key(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-lg[i]))), (unsigned)i);
+    for (int j = threadIdx.x; j < kNQ; j += blockDim.x) s_votes[j] = votes[b * kNQ + j];
+    __syncthreads();
+    // reading order: rank = position in the stable ascending sort of the votes
+    for (int j = threadIdx.x; j < kNQ; j += blockDim.x) {
+        const float vj = s_votes[j];
+        int r = 0;
+        for (int k = 0; k < kNQ; k++) {
+            const float vk = s_votes[k];
+            r += (vk < vj) || (vk == vj && k < j);
+        }
+        s_rank[j] = r;
+    }
     __syncthreads();
     block_select_top(s_key, N, kNQ, s_top);
     const float sf_h = __fdiv_rn((float)kImg, (float)ori_hw[2 * b]);
@@ -266,7 +289,7 @@ pp_select_kernel(const float *__restrict__ logits, const float *__restrict__ box
         o[3] = __fmul_rn(__fsub_rn(bx[1], __fmul_rn(bx[3], 0.5f)), oh);
         o[4] = __fmul_rn(__fadd_rn(bx[0], __fmul_rn(bx[2], 0.5f)), ow);
         o[5] = __fmul_rn(__fadd_rn(bx[1], __fmul_rn(bx[3], 0.5f)), oh);
-        o[6] = (float)rank[b * kNQ + q];
+        o[6] = (float)s_rank[q];
         sel[b * kNQ + r] = flat;
     }
 }
@@ -287,19 +310,43 @@ __global__ void pp_masks_kernel(const float *__restrict__ ml, const int32_t *__r
 // Packed masks: word w of detection row r holds pixels 32w .. 32w + 31 of
 // the thresholded mask of the query selected for that row (bit i = pixel
 // 32w + i, logit > 0 — the reference's threshold, src/ppdoclayout.cpp:985-990).
-// A warp reads 32 consecutive logits (one 128-byte line) per word and
-// ballots them.
+// A warp owns 8 consecutive words: each lane issues its 8 loads (one per
+// word, lanes on consecutive pixels: eight 128-byte lines in flight per
+// warp) before the 8 ballots.
+constexpr int kBitsWordsPerWarp = 8;
 __global__ void pp_mask_bits_kernel(const float *__restrict__ ml, const int32_t *__restrict__ sel,
                                     uint32_t *__restrict__ bits) {
     const int r = blockIdx.y, b = blockIdx.z;
-    const int q = sel[b * kNQ + r] / kNC;
+    const int q = sel ? sel[b * kNQ + r] / kNC : r;  // no sel: row r is query r
     const float *src = ml + ((long long)b * kNQ + q) * kMaskPix;
     uint32_t *dst = bits + ((long long)b * kNQ + r) * kMaskWords;
     const int lane = threadIdx.x & 31;
-    const int w0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    for (int w = w0; w < kMaskWords; w += gridDim.x * (blockDim.x >> 5)) {
-        const uint32_t word = __ballot_sync(0xffffffffu, __ldg(src + w * 32 + lane) > 0.0f);
-        if (lane == 0) dst[w] = word;
+    const int w0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kBitsWordsPerWarp;
+    float v[kBitsWordsPerWarp];
+#pragma unroll
+    for (int j = 0; j < kBitsWordsPerWarp; j++)
+        v[j] = w0 + j < kMaskWords ? __ldg(src + (w0 + j) * 32 + lane) : 0.0f;
+    uint32_t mine = 0;
+#pragma unroll
+    for (int j = 0; j < kBitsWordsPerWarp; j++) {
+        const uint32_t word = __ballot_sync(0xffffffffu, v[j] > 0.0f);
+        if (lane == j) mine = word;
+    }
+    if (lane < kBitsWordsPerWarp && w0 + lane < kMaskWords) dst[w0 + lane] = mine;
+}
+
+// Packed masks of the detection rows from the packed masks of the queries:
+// row r of page b is query sel[b][r] / 25's 1250 words (16-byte copies).
+__global__ void pp_gather_bits_kernel(const uint32_t *__restrict__ qbits,
+                                      const int32_t *__restrict__ sel,
+                                      uint32_t *__restrict__ bits) {
+    const int r = blockIdx.y, b = blockIdx.z;
+    const int q = sel[b * kNQ + r] / kNC;
+    const uint32_t *src = qbits + ((long long)b * kNQ + q) * kMaskWords;
+    uint32_t *dst = bits + ((long long)b * kNQ + r) * kMaskWords;
+    for (int i = threadIdx.x; i < kMaskWords / 2; i += blockDim.x) {
+        // 1250 words = 625 8-byte pairs; rows start 5000 bytes apart (8-byte aligned)
+        reinterpret_cast<uint2 *>(dst)[i] = __ldg(reinterpret_cast<const uint2 *>(src) + i);
     }
 }
 
@@ -318,6 +365,13 @@ __global__ void unpack_mask_bits_kernel(const uint32_t *__restrict__ bits,
 }
 
 }  // namespace
+
+Status launch_pack_mask_bits(const float *ml, uint32_t *bits, int B, cudaStream_t st) {
+    if (B <= 0 || B > 65535) return ERR_SHAPE;
+    dim3 grid((unsigned)cdiv(kMaskWords, 8 * kBitsWordsPerWarp), kNQ, (unsigned)B);
+    pp_mask_bits_kernel<<<grid, 256, 0, st>>>(ml, nullptr, bits);
+    return cuda_status();
+}
 
 Status launch_unpack_mask_bits(const uint32_t *bits, int32_t *masks, long long rows,
                                cudaStream_t st) {
@@ -393,9 +447,9 @@ Status launch_gather_rows(const float *x, const int32_t *idx, float *y, int rows
 }
 
 Status launch_postprocess(const float *logits, const float *boxes, const float *order,
-                          const float *mask_logits, const int32_t *ori_hw, int32_t *rank,
-                          float *dets, int32_t *sel, int32_t *masks, uint32_t *mask_bits, int B,
-                          cudaStream_t st) {
+                          const float *mask_logits, const uint32_t *mask_bits_q,
+                          const int32_t *ori_hw, int32_t *rank, float *dets, int32_t *sel,
+                          int32_t *masks, uint32_t *mask_bits, int B, cudaStream_t st) {
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -406,15 +460,19 @@ Status launch_postprocess(const float *logits, const float *boxes, const float *
             return ERR_CUDA;
         attr_set[dev] = true;
     }
-    pp_votes_rank_kernel<<<B, 320, 0, st>>>(order, rank);
-    pp_select_kernel<<<B, 1024, smem, st>>>(logits, boxes, rank, ori_hw, dets, sel);
+    float *votes = reinterpret_cast<float *>(rank);  // the 300 votes of each page
+    pp_votes_kernel<<<dim3(cdiv(kNQ, kVoteJ), B), 256, 0, st>>>(order, votes);
+    pp_select_kernel<<<B, 1024, smem, st>>>(logits, boxes, votes, ori_hw, dets, sel);
     if (masks) {
         dim3 grid((unsigned)cdiv(kMaskPix / 4, 256), kNQ, (unsigned)B);
         pp_masks_kernel<<<grid, 256, 0, st>>>(mask_logits, sel, masks);
     }
-    if (mask_bits) {
-        // 1250 words per row: 5 blocks of 8 warps, each warp ~31 words
-        dim3 grid(5u, kNQ, (unsigned)B);
+    if (mask_bits && mask_bits_q) {
+        pp_gather_bits_kernel<<<dim3(1, kNQ, (unsigned)B), 128, 0, st>>>(mask_bits_q, sel,
+                                                                          mask_bits);
+    } else if (mask_bits && mask_logits) {
+        // 1250 words per row: blocks of 8 warps x 8 words
+        dim3 grid((unsigned)cdiv(kMaskWords, 8 * kBitsWordsPerWarp), kNQ, (unsigned)B);
         pp_mask_bits_kernel<<<grid, 256, 0, st>>>(mask_logits, sel, mask_bits);
     }
     return cuda_status();

@@ -41,13 +41,19 @@ Status launch_row_scale(const float *x, const float *v, float *y, long long rows
 // y[b][i][:] = x[b][idx[b][i]][:]
 Status launch_gather_rows(const float *x, const int32_t *idx, float *y, int rows_in, int rows_out,
                           int D, int B, cudaStream_t st);
-// reading-order ranks, top-300 selection, dets rows and (each if non-null)
+// reading-order ranks (rank: scratch of B * 300 words for the votes),
+// top-300 selection, dets rows and (each if non-null)
 // the thresholded, reordered masks of B pages as int32 [B][300][40000]
-// and packed [B][300][1250] words (bit i of word w = pixel 32w + i)
+// (from mask_logits) and packed [B][300][1250] words (bit i of word w =
+// pixel 32w + i; from the queries' packed masks mask_bits_q when given,
+// else from mask_logits)
 Status launch_postprocess(const float *logits, const float *boxes, const float *order,
-                          const float *mask_logits, const int32_t *ori_hw, int32_t *rank,
-                          float *dets, int32_t *sel, int32_t *masks, uint32_t *mask_bits, int B,
-                          cudaStream_t st);
+                          const float *mask_logits, const uint32_t *mask_bits_q,
+                          const int32_t *ori_hw, int32_t *rank, float *dets, int32_t *sel,
+                          int32_t *masks, uint32_t *mask_bits, int B, cudaStream_t st);
+
+// packed masks [B][300][1250] of mask logits [B][300][40000] (logit > 0)
+Status launch_pack_mask_bits(const float *ml, uint32_t *bits, int B, cudaStream_t st);
 
 // int32 masks [rows][40000] from packed masks [rows][1250]
 Status launch_unpack_mask_bits(const uint32_t *bits, int32_t *masks, long long rows,

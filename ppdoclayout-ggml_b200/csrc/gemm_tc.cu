@@ -557,6 +557,7 @@ __device__ __forceinline__ void split_row_rows(const uint8_t *tile, int r, int o
 constexpr int kModeTile = 0;  // TMA tile of A (M- or K-major), or the gather
 constexpr int kModeBox = 1;   // implicit conv from TMA windows of the input
 constexpr int kModeRows = 2;  // M-major A as 32 per-channel TMA rows
+constexpr int kModeBits = 3;  // A as kModeTile; output packed 1 bit per (m, n): total > 0
 
 template <int ACT, int AMODE>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -1057,6 +1058,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // one 16-column chunk of the register totals: staged through a
             // shared-memory box and a TMA store, or stored directly
             auto store_chunk = [&](int c0, const float (&v)[16]) {
+                if constexpr (AMODE == kModeBits) {
+                    // packed output (no epilogue ops): bit (m & 31) of word
+                    // (m >> 5) of column n is total(m, n) > 0; the warp's 32
+                    // rows are one word per column, made by one ballot
+                    uint32_t mine = 0;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const uint32_t word = __ballot_sync(0xffffffffu, row_ok && v[j] > 0.0f);
+                        if (lane == j) mine = word;
+                    }
+                    const int n = n0 + c0 + lane;
+                    if (lane < 16 && n < pN && m0 + quad * 32 < pM)
+                        reinterpret_cast<uint32_t *>(C)[(long long)n * e.ldc_n +
+                                                        ((m0 + quad * 32) >> 5)] = mine;
+                    return;
+                }
                 if (ptma == 1 || ptma == 3) {
                     // CHW output: the warp's 32 pixels x 16 channels go into a
                     // staging box (lane = pixel, conflict-free rows of 128 B)
@@ -1403,6 +1420,7 @@ namespace {
 bool plan_common(TcGemm *g, int M, int N, int K, int batch, int planes, const TcEpilogue &epi,
                  uint32_t a_bytes = kABytes, uint32_t ring_bytes = 0, long long row_tiles = 0) {
     g->ok = false;
+    g->bits = 0;
     if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || planes <= 0) return false;
     // N tile (multiple of 16, <= 128 so that the partial slots and the A
     // stages fit in the 512 TMEM columns); cost model: the tiles one CTA
@@ -1649,6 +1667,20 @@ bool tc_gemm_plan_rows(TcGemm *g, int M, int N, int K, int batch, const float *x
     return g->ok;
 }
 
+bool tc_gemm_set_bits_output(TcGemm *g, uint32_t *bits, long long words_per_n, long long bits_bs) {
+    const TcEpilogue &e = g->epi;
+    if (!g->ok || g->box || g->rows || g->gather || g->M % 32 || e.bias || e.res_mode ||
+        e.act != ACT_NONE || e.alpha != 1.0f || !bits || words_per_n * 32 < g->M)
+        return false;
+    g->bits = 1;
+    g->tma_c = 0;
+    g->epi.C = reinterpret_cast<float *>(bits);
+    g->epi.ldc_m = 0;
+    g->epi.ldc_n = words_per_n;
+    g->epi.c_bs = bits_bs;
+    return true;
+}
+
 Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     if (!g.ok || g.epi.act < 0 || g.epi.act > 3) return ERR_SHAPE;
     // per device, once: the kernels' register count is checked and their
@@ -1662,7 +1694,8 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     {
         std::lock_guard<std::mutex> lk(mu);
         if (!attr[dev]) {
-            const void *fns[12] = {
+            const void *fns[13] = {
+                (const void *)tc_gemm_kernel<0, kModeBits>,
                 (const void *)tc_gemm_kernel<0, kModeTile>, (const void *)tc_gemm_kernel<1, kModeTile>,
                 (const void *)tc_gemm_kernel<2, kModeTile>, (const void *)tc_gemm_kernel<3, kModeTile>,
                 (const void *)tc_gemm_kernel<0, kModeBox>,  (const void *)tc_gemm_kernel<1, kModeBox>,
@@ -1717,6 +1750,12 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     int grid = sm_count();
     if (g.max_ctas > 0 && grid > g.max_ctas) grid = g.max_ctas;
     if (grid > g.tiles) grid = g.tiles;
+    if (g.bits) {
+        // packed output: tile A, no epilogue ops (checked by the planner)
+        tc_gemm_kernel<ACT_NONE, kModeBits><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi,
+                                                                           g.tmBlo, g.tmC, a);
+        return cuda_status();
+    }
     const int mode = g.box ? kModeBox : (g.rows ? kModeRows : kModeTile);
     switch (mode * 4 + g.epi.act) {
 #define PPDL_TC_CASE(M_, A_)                                                                  \

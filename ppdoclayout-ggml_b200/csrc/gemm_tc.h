@@ -90,6 +90,7 @@ struct TcGemm {
     TcGather gg;
     int box = 0;         // 1: implicit conv from TMA boxes of the input (geometry cb)
     TcConvBox cb;
+    int bits = 0;        // 1: output packed 1 bit per element (tc_gemm_set_bits_output)
     int rows = 0;        // 1: M-major A loaded as 32 channel rows per k-block (rows_plane)
     long long rows_plane = 0;
     int rows_delta = 0;
@@ -146,6 +147,12 @@ bool tc_gemm_plan_rows(TcGemm *g, int M, int N, int K, int batch, const float *x
 // (hi/lo rows of tc_conv_box_kdim(IC, KS) floats, zero where no tap/channel).
 Status launch_tf32_split_box(const float *w, float *hi, float *lo, int OC, int IC, int KS,
                              cudaStream_t st);
+
+// Turn a planned tile-mode GEMM with no epilogue ops and M % 32 == 0 into
+// one that writes C packed: bit (m & 31) of word bits[z * bits_bs +
+// n * words_per_n + (m >> 5)] = (total(m, n) > 0).  False when the plan
+// does not qualify.
+bool tc_gemm_set_bits_output(TcGemm *g, uint32_t *bits, long long words_per_n, long long bits_bs);
 
 Status launch_tc_gemm(const TcGemm &g, cudaStream_t st);
 

@@ -25,6 +25,8 @@ Status launch_msda(const float *val, const float *p1, const float *p2, const flo
 
 // mask logits [rows][40000] -> [rows][4]
 Status launch_mask_box(const float *ml, float *out, int rows, cudaStream_t stream);
+// the same on packed masks [rows][1250] (bit p & 31 of word p >> 5 = pixel p)
+Status launch_mask_box_bits(const uint32_t *bits, float *out, int rows, cudaStream_t stream);
 
 // class logits [B][ntok][nc] -> [B][nq] token indices
 Status launch_topk(const float *lg, int32_t *out, int ntok, int nc, int nq, int batch,

@@ -142,7 +142,6 @@ public:
     V img;
     int32_t *ori_hw = nullptr;
     S logits, boxes, order;
-    float *mask_logits = nullptr;
     float *dets = nullptr;
     int32_t *sel = nullptr, *rank = nullptr, *masks = nullptr;
     uint32_t *mask_bits = nullptr;  // packed masks [B][300][1250], made by the forward
@@ -968,45 +967,57 @@ public:
         S tq = seq(kNQ, kDM), mq0 = seq(kNQ, 32);
         ln(target, tq, "dec_norm");
         mlp3(tq, mq0, "mq");
-        float *encm = dalloc((long long)kNQ * kMaskPix * Bmax);
         const V mf = mfeat;
-        // mask logits [b][q][p] = sum_c mq[b][q][c] mf[b][c][p]: on the tensor
-        // cores A = mf (pixels x 32 channels, M-major) and B = mq, split into
-        // TF32 halves per forward (it is an activation)
+        // mask logits [b][q][p] = sum_c mq[b][q][c] mf[b][c][p], thresholded
+        // (> 0) and packed 1 bit per pixel in the GEMM's epilogue — every
+        // consumer (mask -> box, the result masks) needs only the threshold.
+        // On the tensor cores A = mf (pixels x 32 channels, M-major) and
+        // B = mq, split into TF32 halves per forward (it is an activation).
+        uint32_t *encm = nullptr;
+        if (cudaMalloc(&encm, sizeof(uint32_t) * (size_t)kNQ * kMaskWords * Bmax) != cudaSuccess)
+            fail("cudaMalloc");
+        allocs.push_back(encm);
         float *mq_hi = dalloc((long long)kNQ * 32 * Bmax), *mq_lo = dalloc((long long)kNQ * 32 * Bmax);
-        auto mask_gemm = [=](const S &mq, float *dst) {
+        float *mask_f32 = nullptr;  // float logits, only for the SIMT fallback
+        auto mask_gemm = [&, mf, mq_hi, mq_lo](const S &mq, uint32_t *dst) {
             if (use_tc && tc_shape_ok(mf.p, mf.plane(), mf.bs, 32)) {
                 TcEpilogue e;
-                e.C = dst; e.ldc_m = 1; e.ldc_n = kMaskPix; e.c_bs = (long long)kNQ * kMaskPix;
+                e.C = reinterpret_cast<float *>(dst);
+                e.ldc_m = 1; e.ldc_n = kMaskPix; e.c_bs = (long long)kNQ * kMaskPix;
                 auto g = std::make_shared<TcGemm>();
                 if (ok && tc_gemm_plan(g.get(), kMaskPix, kNQ, 32, Bmax, mf.p, 1, mf.plane(), mf.bs,
-                                       mq_hi, mq_lo, Bmax, e)) {
+                                       mq_hi, mq_lo, Bmax, e) &&
+                    tc_gemm_set_bits_output(g.get(), dst, kMaskWords,
+                                            (long long)kNQ * kMaskWords)) {
                     push("mask_gemm", PPDL_STEP_GEMM_LINEAR, 2.0 * kNQ * kMaskPix * 32,
-                         4.0 * ((double)kNQ * kMaskPix + 32.0 * kMaskPix), [=]() {
+                         4.0 * ((double)kNQ * kMaskWords + 32.0 * kMaskPix), [=]() {
                         TRY(launch_tf32_split(mq.p, mq_hi, mq_lo, (long long)nb * mq.bs(), st));
                         return run_tc(g, 0);
                     });
                     return;
                 }
             }
+            if (!mask_f32) mask_f32 = dalloc((long long)kNQ * kMaskPix * Bmax);
+            float *mf32 = mask_f32;
             push("mask_gemm", PPDL_STEP_GEMM_LINEAR, 2.0 * kNQ * kMaskPix * 32,
                  4.0 * ((double)kNQ * kMaskPix + 32.0 * kMaskPix), [=]() {
                 GemmArgs g;
                 g.M = kNQ; g.N = kMaskPix; g.K = 32; g.batch = nb;
                 g.A = {mq.p, 32, 1, 1, mq.bs(), 0};
                 g.B = {mf.p, mf.plane(), 1, 1, mf.bs, 0};
-                g.C = dst; g.ldc_m = kMaskPix; g.ldc_n = 1; g.c_bs_hi = (long long)kNQ * kMaskPix;
-                return launch_gemm_simt(g, st);
+                g.C = mf32; g.ldc_m = kMaskPix; g.ldc_n = 1; g.c_bs_hi = (long long)kNQ * kMaskPix;
+                TRY(launch_gemm_simt(g, st));
+                return launch_pack_mask_bits(mf32, dst, nb, st);
             });
         };
         after(e_mf);
         mask_gemm(mq0, encm);
         if (dumps)
-            dump_list.push_back({"enc_masks", encm, {kMaskPix, kNQ, 1, 1}, "f32",
-                                 (size_t)kNQ * kMaskPix * 4});
+            dump_list.push_back({"enc_mask_bits", encm, {kMaskWords, kNQ, 1, 1}, "u32",
+                                 (size_t)kNQ * kMaskWords * 4});
         S refu = seq(kNQ, 4), ref = seq(kNQ, 4);
-        push("mask_box", PPDL_STEP_MASKBOX, 0.0, 4.0 * kNQ * kMaskPix,
-             [=]() { return launch_mask_box(encm, refu.p, nb * kNQ, st); });
+        push("mask_box", PPDL_STEP_MASKBOX, 0.0, 4.0 * kNQ * kMaskWords,
+             [=]() { return launch_mask_box_bits(encm, refu.p, nb * kNQ, st); });
         dump_seq("init_ref_unact", refu);
         push("ref", PPDL_STEP_GLUE, 0.0, 8.0 * refu.bs(),
              [=]() { return launch_sigmoid(refu.p, ref.p, (long long)nb * refu.bs(), st); });
@@ -1088,8 +1099,12 @@ public:
         ln(x, outq, "dec_norm");
         lin(outq, logits, "score_head");
         mlp3(outq, mq6, "mq");
-        mask_logits = dalloc((long long)kNQ * kMaskPix * Bmax);
-        mask_gemm(mq6, mask_logits);
+        uint32_t *mask_bits_q = nullptr;  // packed masks of the 300 queries
+        if (cudaMalloc(&mask_bits_q, sizeof(uint32_t) * (size_t)kNQ * kMaskWords * Bmax) !=
+            cudaSuccess)
+            fail("cudaMalloc");
+        allocs.push_back(mask_bits_q);
+        mask_gemm(mq6, mask_bits_q);
         // the reading-order head on lane 2, beside the class/mask heads
         S oh = seq(kNQ, kDM), gp = seq(kNQ, 128);
         on_lane(2);
@@ -1130,13 +1145,12 @@ public:
             // int32 form of the reference's result is expanded from it only
             // for the calls that return it (expand_masks)
             const S lg = logits, bx = boxes, od = order;
-            const float *mlp = mask_logits;
             uint32_t *mb = mask_bits;
             after(e_order);
             push("postprocess", PPDL_STEP_POSTPROCESS, 0.0,
-                 4.0 * ((double)kNQ * kNQ + kNQ * kMaskPix) + 4.0 * kNQ * kMaskWords, [=]() {
-                return launch_postprocess(lg.p, bx.p, od.p, mlp, ori_hw, rank, dets, sel, nullptr,
-                                          mb, nb, st);
+                 4.0 * ((double)kNQ * kNQ + 2.0 * kNQ * kMaskWords), [=]() {
+                return launch_postprocess(lg.p, bx.p, od.p, nullptr, mask_bits_q, ori_hw, rank,
+                                          dets, sel, nullptr, mb, nb, st);
             });
         }
         if (!ok) return;
