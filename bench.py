@@ -594,8 +594,10 @@ def run_forward(args, world, rank, local, pg):
     ctx.close()
     if rank == 0 and world == 1 and not args.no_sweeps:
         # the metric's other two clauses, measured after the timed region:
-        # MSDeformAttn HBM GB/s (config 1, B = 32) and conv TFLOPS (config 2)
+        # MSDeformAttn HBM GB/s (config 1, B = 32) and conv TFLOPS (config 2);
+        # and config 4 (2048 pages, 32 per batch) on this GPU
         line.update(kernel_sweeps(dev, hbm, tc))
+        line["config4_stress_1gpu"] = config4_stress(dev, 1, 0, None)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_forward(gguf, budget_s=args.cpu_seconds)
         if not args.no_sweeps:
@@ -859,7 +861,7 @@ def cpu_baseline_forward(gguf, budget_s=10.0, sample_pages=None):
 def run_reference(args, world, rank):
     if rank != 0:
         return None
-    if args.workload in ("gemm", "conv"):
+    if args.workload in ("gemm", "conv", "stress"):
         return {"impl": "reference", "unavailable": f"the {args.workload} workload is a kernel-level "
                 "measurement of this build only (its same-box bar, cuBLAS FP32 SGEMM, is part of "
                 "the forward workload's config2_conv); the reference arm times the forward"}
@@ -984,6 +986,130 @@ def run_gemm(args, world, rank, local, pg):
     }
 
 
+STRESS_PAGES, STRESS_B = 2048, 32
+
+
+def _stage_of(names):
+    """Stage of every plan step of the forward (by its position between
+    landmark steps): backbone, encoder (AIFI, FPN/PAN, mask-feature head),
+    selection (decoder input, two-stage query selection, initial boxes),
+    decoder (the six layers), heads, postprocess."""
+    first = {}
+    for i, n in enumerate(names):
+        first.setdefault(n, i)
+    enc0, sel0 = first.get("enc_in0", 0), first.get("dec_in0", 0)
+    dec_idx = [i for i, n in enumerate(names) if n.startswith("dec") and n[3:4].isdigit()]
+    dec0, dec1 = (dec_idx[0], dec_idx[-1]) if dec_idx else (len(names), len(names))
+    out = []
+    for i, n in enumerate(names):
+        if n == "postprocess":
+            out.append("postprocess")
+        elif i < enc0:
+            out.append("backbone")
+        elif i < sel0:
+            out.append("encoder")
+        elif i < dec0:
+            out.append("selection")
+        elif i <= dec1:
+            out.append("decoder")
+        else:
+            out.append("heads")
+    return out
+
+
+def config4_stress(dev, world, rank, pg, total_pages=STRESS_PAGES, B=STRESS_B, ctx=None):
+    """Config 4 of the baseline: total_pages pages split over the ranks, B
+    per GPU per batch, through the pipelined host API (ppdl_submit_batch /
+    ppdl_wait_batch: pinned pages in, dets + packed masks out, two batches in
+    flight), timed by the host clock, slowest rank; plus the per-stage split
+    of one batch (device time of the forward's steps, one after another, and
+    the host<->device copies timed alone)."""
+    import numpy as np
+    import torch
+    import ppdl
+    import synth
+    own = ctx is None
+    if own:
+        ctx = ppdl.Context(synth.cached_gguf(0), device=dev.index, max_batch=B)
+    # a pool of 2B distinct seeded pages, cycled (generating 2048 pages on
+    # the host would take minutes); each batch is B distinct pages
+    pool = torch.from_numpy(np.stack([synth.synth_page(20000 + rank * 2 * B + i)
+                                      for i in range(2 * B)])).pin_memory().numpy()
+    hw = np.full((B, 2), 800, np.int32)
+    halves = [pool[:B], pool[B:]]  # contiguous views of the pinned pool
+    per_rank = (total_pages + world - 1) // world
+    n_batches = (per_rank + B - 1) // B
+    for i in range(2):
+        ctx.wait(ctx.submit(halves[i], hw), B, copy=False)
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    t0 = time.perf_counter()
+    pending = []
+    for i in range(n_batches):
+        pending.append(ctx.submit(halves[i & 1], hw))
+        if len(pending) == 2:
+            ctx.wait(pending.pop(0), B, copy=False)
+    for t in pending:
+        ctx.wait(t, B, copy=False)
+    wall = time.perf_counter() - t0
+    barrier(pg)
+    wall = max_over_ranks(pg, wall)
+    pages = n_batches * B * world
+    # per-stage split of one batch
+    steps = ctx.profile_steps(B)
+    stages = {}
+    for st_name, (name, kind, ms, fl, by) in zip(_stage_of([x[0] for x in steps]), steps):
+        stages[st_name] = stages.get(st_name, 0.0) + ms
+    d_in = torch.empty((B, 3, 800, 800), device=dev)
+    d_out = torch.empty(B * 300 * (7 + 1250), device=dev)
+    h_out = torch.empty(d_out.shape, dtype=torch.float32).pin_memory()
+    h_in = torch.from_numpy(halves[0])  # pinned (a view of the pinned pool)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    e[0].record()
+    d_in.copy_(h_in, non_blocking=True)
+    e[1].record()
+    e[2].record()
+    h_out.copy_(d_out, non_blocking=True)
+    e[3].record()
+    torch.cuda.synchronize(dev)
+    stages["h2d"] = e[0].elapsed_time(e[1])
+    stages["d2h"] = e[2].elapsed_time(e[3])
+    if own:
+        ctx.close()
+    return {"pages": pages, "pages_per_gpu_per_batch": B, "batches_per_gpu": n_batches,
+            "wall_s": round(wall, 3), "pages_per_s": round(pages / wall, 2),
+            "stage_ms_per_batch": {k: round(v, 3) for k, v in stages.items()},
+            "note": "pages cycled from a pool of 2B distinct seeded pages per rank; stage split: "
+                    "device time of the forward's steps one after another (lower bounds; the "
+                    "captured forward overlaps its three lanes) and the copies of one batch "
+                    "timed alone (in the pipelined run they overlap the next batch's forward)"}
+
+
+def run_stress(args, world, rank, local, pg):
+    """--workload stress: config 4 on all ranks (torchrun for N GPUs)."""
+    import torch
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    r = config4_stress(dev, world, rank, pg, total_pages=args.stress_pages)
+    clk = clocks.stop()
+    return {
+        "metric": METRIC, "value": r["pages_per_s"], "unit": "pages/s", "n_gpus": world,
+        "steps": r["batches_per_gpu"], "warmup": 2,
+        "ms_per_step": round(r["wall_s"] * 1e3 / r["batches_per_gpu"], 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic pages (config 0 recipe) and seeded random weights",
+        "config": {"workload": f"config 4: {args.stress_pages} pages, {STRESS_B} per GPU per "
+                               "batch, host pages in / dets + packed masks out",
+                   "parallelism": f"dp{world} (pages sharded, no collective)"},
+        "e2e": {"value": r["pages_per_s"], "unit": "pages/s",
+                "h2d_bytes_per_step": STRESS_B * (3 * 800 * 800 * 4 + 8),
+                "d2h_bytes_per_step": STRESS_B * 300 * (7 + 1250) * 4},
+        "config4": r, "gpu_launches": r["batches_per_gpu"] * 338, "clocks": clk,
+    }
+
+
 def run_conv(args, world, rank, local, pg):
     """Config 2 of the baseline, one conv shape: the forward's conv path
     through the C ABI (Winograd F(4,3) for 3x3-s1, the 3xTF32 GEMM for 1x1,
@@ -1041,7 +1167,10 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="forward", choices=["forward", "msda", "gemm", "conv"])
+    ap.add_argument("--workload", default="forward",
+                    choices=["forward", "msda", "gemm", "conv", "stress"])
+    ap.add_argument("--stress-pages", type=int, default=STRESS_PAGES,
+                    help="stress workload: pages in all (config 4: 2048)")
     ap.add_argument("--conv", default="",
                     help="conv workload: kind,IC,H,OC,pages with kind 3x3-s1, 1x1 or 3x3-s2 "
                          "(default 3x3-s1,256,100,256,8)")
@@ -1070,6 +1199,8 @@ def main():
             line = run_gemm(args, world, rank, local, pg)
         elif args.workload == "conv":
             line = run_conv(args, world, rank, local, pg)
+        elif args.workload == "stress":
+            line = run_stress(args, world, rank, local, pg)
         else:
             line = run_msda(args, world, rank, local, pg)
         if rank == 0 and line is not None:
