@@ -59,11 +59,15 @@ int sm_count() {
 }
 
 // ---- Winograd input transform -----------------------------------------------
-// thread per (page, ic, tile); dt[(b*36 + p)*IC + ic][T] (the reference's
-// (T, IC, 36) plane layout per page)
+// thread per (page, ic, tile); value (page b, plane p, channel ic, tile t) at
+// dt[b*bstride + p*pstride + ic*ldt + t]: the reference's (T, IC, 36) plane
+// layout per page (bstride = 36*IC*ldt, pstride = IC*ldt), or the pages side
+// by side in each channel row (ldt = B*Tp, pstride = IC*ldt, bstride = Tp),
+// which the forward uses so that one plane GEMM's rows run over all pages
 __global__ void __launch_bounds__(256, 4)
 wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ dt, int IC,
-                 int H, int W, int TW, int TH, int pad, int B, int ldt) {
+                 int H, int W, int TW, int TH, int pad, int B, long long ldt, long long pstride,
+                 long long bstride) {
     // grid (IC*T / 256, B): one 32-bit division per thread
     const int T = TW * TH;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -92,7 +96,7 @@ wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__
             for (int a = 0; a < 6; a++) s = fmaf(c_wgB[u * 6 + a], d[a][v], s);
             t1[u][v] = s;
         }
-    float *o = dt + ((long long)b * 36 * IC + ic) * ldt + tile;
+    float *o = dt + b * bstride + ic * ldt + tile;
 #pragma unroll
     for (int u = 0; u < 6; u++)
 #pragma unroll
@@ -100,7 +104,7 @@ wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__
             float s = 0.0f;
 #pragma unroll
             for (int c = 0; c < 6; c++) s = fmaf(t1[u][c], c_wgB[w * 6 + c], s);
-            o[(long long)(u * 6 + w) * IC * ldt] = s;
+            o[(long long)(u * 6 + w) * pstride] = s;
         }
 }
 
@@ -112,17 +116,17 @@ __global__ void __launch_bounds__(256, 4)
 wg4_output_kernel(const float *__restrict__ yt, const float *__restrict__ bias,
                   float *__restrict__ y, long long ybs, const float *__restrict__ res,
                   long long rbs, int res_mode, int OC, int OH, int OW, int TW, int TH, int act,
-                  int B, int ldt) {
-    // grid (OC*T / 256, B)
+                  int B, long long ldt, long long pstride, long long bstride) {
+    // grid (OC*T / 256, B); yt addressed as dt of the input transform
     const int T = TW * TH;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= OC * T) return;
     const int oc = i / T, tile = i - oc * T, b = blockIdx.y;
     const int ty = tile / TW, tx = tile - ty * TW;
-    const float *m = yt + ((long long)b * 36 * OC + oc) * ldt + tile;
+    const float *m = yt + b * bstride + oc * ldt + tile;
     float mm[36];
 #pragma unroll
-    for (int p = 0; p < 36; p++) mm[p] = __ldg(m + (long long)p * OC * ldt);
+    for (int p = 0; p < 36; p++) mm[p] = __ldg(m + (long long)p * pstride);
     float t1[4][6];
 #pragma unroll
     for (int a = 0; a < 4; a++)
@@ -506,24 +510,30 @@ Status launch_pad_rows(const float *x, long long xbs, float *y, long long ybs, i
 }
 
 Status launch_wg4_input(const float *x, long long xbs, float *dt, int IC, int H, int W, int TW,
-                        int TH, int pad, int B, cudaStream_t st, int ldt) {
+                        int TH, int pad, int B, cudaStream_t st, long long ldt, long long pstride,
+                        long long bstride) {
     if (!grid3_ok((long long)TW * TH, IC, B)) return ERR_SHAPE;
     if (ldt <= 0) ldt = TW * TH;
     if (ldt < TW * TH) return ERR_SHAPE;
-    wg4_input_kernel<<<grid3((long long)TW * TH, IC, B), 256, 0, st>>>(x, xbs, dt, IC, H, W, TW,
-                                                                       TH, pad, B, ldt);
+    if (pstride <= 0) pstride = IC * ldt;
+    if (bstride <= 0) bstride = 36 * pstride;
+    wg4_input_kernel<<<grid3((long long)TW * TH, IC, B), 256, 0, st>>>(
+        x, xbs, dt, IC, H, W, TW, TH, pad, B, ldt, pstride, bstride);
     return cuda_status();
 }
 
 Status launch_wg4_output(const float *yt, const float *bias, float *y, long long ybs,
                          const float *res, long long rbs, int res_mode, int OC, int OH, int OW,
-                         int TW, int TH, int act, int B, cudaStream_t st, int ldt) {
+                         int TW, int TH, int act, int B, cudaStream_t st, long long ldt,
+                         long long pstride, long long bstride) {
     if (!grid3_ok((long long)TW * TH, OC, B)) return ERR_SHAPE;
     if (TW < (OW + 3) / 4 || TH < (OH + 3) / 4) return ERR_SHAPE;
     if (ldt <= 0) ldt = TW * TH;
     if (ldt < TW * TH) return ERR_SHAPE;
+    if (pstride <= 0) pstride = OC * ldt;
+    if (bstride <= 0) bstride = 36 * pstride;
     wg4_output_kernel<<<grid3((long long)TW * TH, OC, B), 256, 0, st>>>(
-        yt, bias, y, ybs, res, rbs, res_mode, OC, OH, OW, TW, TH, act, B, ldt);
+        yt, bias, y, ybs, res, rbs, res_mode, OC, OH, OW, TW, TH, act, B, ldt, pstride, bstride);
     return cuda_status();
 }
 

@@ -8,18 +8,21 @@
 
 namespace ppdl {
 
-// x [B][IC][H][W] -> dt [B*36][IC][T], tiles TW x TH of 4x4 outputs; `pad`
-// is the left/top zero padding (1 for a k3-s1-p1 conv on the unpadded
-// tensor, 0 for the reference's op 10 on an already padded tensor).
-// `ldt` is the row stride of the [IC][T] plane rows (>= T; 0 = T).
+// x [B][IC][H][W] -> dt, tiles TW x TH of 4x4 outputs; `pad` is the
+// left/top zero padding (1 for a k3-s1-p1 conv on the unpadded tensor, 0 for
+// the reference's op 10 on an already padded tensor).  Value (page b, plane
+// p, channel ic, tile t) at dt[b*bstride + p*pstride + ic*ldt + t]; the
+// defaults (0) give [B*36][IC][ldt] with ldt = T.
 Status launch_wg4_input(const float *x, long long xbs, float *dt, int IC, int H, int W, int TW,
-                        int TH, int pad, int B, cudaStream_t st, int ldt = 0);
+                        int TH, int pad, int B, cudaStream_t st, long long ldt = 0,
+                        long long pstride = 0, long long bstride = 0);
 
-// yt [B*36][OC][T] -> y = act(A^T m A + bias (+res if res_mode==1)) (+res if
-// res_mode==2), y/res [B][OC][OH][OW] views.
+// yt (addressed as dt above, OC channels) -> y = act(A^T m A + bias (+res if
+// res_mode==1)) (+res if res_mode==2), y/res [B][OC][OH][OW] views.
 Status launch_wg4_output(const float *yt, const float *bias, float *y, long long ybs,
                          const float *res, long long rbs, int res_mode, int OC, int OH, int OW,
-                         int TW, int TH, int act, int B, cudaStream_t st, int ldt = 0);
+                         int TW, int TH, int act, int B, cudaStream_t st, long long ldt = 0,
+                         long long pstride = 0, long long bstride = 0);
 
 // wg4 [36][IC][OC] -> K-major TF32 halves hi/lo [36][OC][IC]
 Status launch_wg4_kmajor_split(const float *wg4, float *hi, float *lo, int IC, int OC,

@@ -257,13 +257,14 @@ public:
         return e;
     }
     // launch a planned tensor-core GEMM for the current batch: rows_per_page > 0
-    // folds the pages into M, otherwise every page (x zmul planes) is a z slice
+    // folds the pages into M (zmul z slices, e.g. the 36 Winograd planes),
+    // otherwise every page (x zmul planes) is a z slice
     Status run_tc(const std::shared_ptr<TcGemm> &g, int rows_per_page, int zmul = 1) {
         TcGemm r = *g;
         if (rows_per_page > 0) {
             r.M = nb * rows_per_page;
             r.m_tiles = (r.M + 127) / 128;
-            r.batch = 1;
+            r.batch = zmul;
         } else {
             r.batch = nb * zmul;
         }
@@ -480,12 +481,22 @@ public:
             const int ss = scratch;
             wg_dt_ns[ss] = std::max(wg_dt_ns[ss], 36LL * IC * Tp * Bmax);
             wg_yt_ns[ss] = std::max(wg_yt_ns[ss], 36LL * OC * Tp * Bmax);
+            // tensor cores: the planes keep the pages side by side in each
+            // channel row ([36][C][B*Tp]), so one plane GEMM's rows run over
+            // all pages — a 25 x 25 conv's 49 tiles per page fill 128-row M
+            // tiles instead of 38 % of one per page.  The SIMT fallback keeps
+            // the per-page layout [B*36][C][Tp].
+            const bool fold = use_tc && IC % 4 == 0;
+            const long long ldt = fold ? (long long)Bmax * Tp : Tp;
+            const long long in_ps = IC * ldt, out_ps = OC * ldt;
+            const long long bstr_in = fold ? Tp : 36 * in_ps, bstr_out = fold ? Tp : 36 * out_ps;
             push(name + ".wg_in", PPDL_STEP_WG_INPUT, 0.0,
                  4.0 * ((double)IC * x.plane() + 36.0 * IC * T), [=]() {
-                return launch_wg4_input(x.p, x.bs, wg_dt_s[ss], IC, x.H, x.W, TW, TH, 1, nb, st, Tp);
+                return launch_wg4_input(x.p, x.bs, wg_dt_s[ss], IC, x.H, x.W, TW, TH, 1, nb, st,
+                                        ldt, in_ps, bstr_in);
             });
             std::shared_ptr<TcGemm> g;
-            if (use_tc && IC % 4 == 0) {
+            if (fold) {
                 // B = wg4 as K-major TF32 halves [36][OC][IC]; A (the dt planes)
                 // exists only once the scratch is allocated -> plan in finalize
                 float *bhi = dalloc(36LL * IC * OC), *blo = dalloc(36LL * IC * OC);
@@ -494,15 +505,15 @@ public:
                 g = std::make_shared<TcGemm>();
                 finalizers.push_back([=]() {
                     TcEpilogue e;
-                    e.C = wg_yt_s[ss]; e.ldc_m = 1; e.ldc_n = Tp; e.c_bs = (long long)OC * Tp;
-                    if (!tc_gemm_plan(g.get(), T, OC, IC, Bmax * 36, wg_dt_s[ss], 1, Tp,
-                                      (long long)IC * Tp, bhi, blo, 36, e))
+                    e.C = wg_yt_s[ss]; e.ldc_m = 1; e.ldc_n = ldt; e.c_bs = out_ps;
+                    if (!tc_gemm_plan(g.get(), (int)ldt, OC, IC, 36, wg_dt_s[ss], 1, ldt, in_ps,
+                                      bhi, blo, 36, e))
                         g->ok = false;
                 });
             }
             push(name + ".wg_madd", PPDL_STEP_WG_MADD, 2.0 * 36 * T * IC * OC,
                  4.0 * (36.0 * T * (IC + OC) + 36.0 * IC * OC), [=]() {
-                if (g && g->ok) return run_tc(g, 0, 36);
+                if (g) return g->ok ? run_tc(g, Tp, 36) : ERR_SHAPE;
                 GemmArgs q;
                 q.M = OC; q.N = T; q.K = IC; q.batch = nb * 36;
                 q.A = {wg4, 1, OC, 36, 0, (long long)IC * OC};
@@ -513,7 +524,7 @@ public:
             push(name + ".wg_out", PPDL_STEP_WG_OUTPUT, 0.0,
                  4.0 * (36.0 * OC * T + (double)OC * OH * OW * (res_mode ? 2 : 1)), [=]() {
                 return launch_wg4_output(wg_yt_s[ss], bp, y.p, y.bs, res.p, res.bs, res_mode, OC, OH, OW,
-                                         TW, TH, act, nb, st, Tp);
+                                         TW, TH, act, nb, st, ldt, out_ps, bstr_out);
             });
             return;
         }
