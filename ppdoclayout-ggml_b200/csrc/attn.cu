@@ -18,9 +18,13 @@ namespace {
 
 constexpr int kHeadDim = 32;  // head dim
 constexpr int kBQ = 32;       // queries per block
-constexpr int kKT = 64;       // keys per shared-memory tile
 constexpr int kThreads = 256;
 constexpr int kLD = 36;       // row stride of the Q and K/V tiles
+// Key tiles: sequences of up to kKTAll keys (the decoder's 300 queries) keep
+// all keys in one tile, so K and then V each arrive with one wait (V's
+// during the softmax) in a single buffer; longer ones (AIFI's 625 tokens)
+// stream tiles of 64 keys through two buffers.
+constexpr int kKTAll = 320;
 
 __device__ __forceinline__ void cp_async16(float *dst, const float *src, bool valid) {
     const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
@@ -49,18 +53,21 @@ __device__ __forceinline__ float warp_sum32(float v) {
 
 // q, k: token-major [B][T][ldqk] (page stride bsqk), v, o: [B][T][ldvo]
 // (page stride bsvo), head h at columns h*32 .. h*32+31 of each.
-// Shared memory: Q [32][36] | two K/V tiles [64][36] | scores [32][ldS], ldS
-// a multiple of 4.  Rows of 36 floats keep the 16-byte loads of a quarter
-// warp on distinct banks.  The K and V tiles stream through the two buffers
-// with cp.async, the next tile landing while the current one is used.
+// Shared memory: Q [32][36] | kBufs K/V tiles [kKT][36] | scores [32][ldS],
+// ldS a multiple of 4.  Rows of 36 floats keep the 16-byte loads of a quarter
+// warp on distinct banks.  K and V tiles arrive by cp.async: with two buffers
+// the next tile lands while the current one is used; with one (all keys in
+// one tile) V lands while the softmax runs.
+template <int kKT, int kBufs>
 __global__ void __launch_bounds__(kThreads, 2)
 attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
             float *__restrict__ o, int T, int ldqk, long long bsqk, int ldvo, long long bsvo,
             float scale, int ldS) {
+    static_assert(kKT % 64 == 0, "the score loop walks 64-key slices of a tile");
     extern __shared__ float sm[];
-    float *Qs = sm;                 // [kBQ][kLD]
-    float *Tb = Qs + kBQ * kLD;     // [2][kKT][kLD]
-    float *Ss = Tb + 2 * kKT * kLD; // [kBQ][ldS]
+    float *Qs = sm;                      // [kBQ][kLD]
+    float *Tb = Qs + kBQ * kLD;          // [kBufs][kKT][kLD]
+    float *Ss = Tb + kBufs * kKT * kLD;  // [kBQ][ldS]
     const int q0 = blockIdx.x * kBQ, h = blockIdx.y, b = blockIdx.z;
     const int t = threadIdx.x, lane = t & 31, wq = t >> 5;  // wq: query group of 4
     const long long base_qk = (long long)b * bsqk + h * kHeadDim;
@@ -70,9 +77,9 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
         const int r = i >> 5, d = i & 31;
         Qs[r * kLD + d] = q0 + r < T ? q[base_qk + (long long)(q0 + r) * ldqk + d] : 0.0f;
     }
-    // tile j of K or V into buffer (j & 1); rows past T are zero-filled
+    // tile j of K or V into buffer j % kBufs; rows past T are zero-filled
     auto load_tile = [&](const float *src, int j, int ld, long long base) {
-        float *dst = Tb + (j & 1) * kKT * kLD;
+        float *dst = Tb + (j % kBufs) * kKT * kLD;
         for (int i = t; i < kKT * kHeadDim / 4; i += kThreads) {
             const int r = i >> 3, c4 = i & 7, row = j * kKT + r;
             const bool ok = row < T;
@@ -82,46 +89,51 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
         cp_async_commit();
     };
     const int nt = (T + kKT - 1) / kKT;
-    // ---- scores: thread -> queries 4wq..4wq+3, keys lane and lane+32 of a tile
+    // ---- scores: thread -> queries 4wq..4wq+3
     load_tile(k, 0, ldqk, base_qk);
     for (int jt = 0; jt < nt; jt++) {
         const int j0 = jt * kKT;
-        if (jt + 1 < nt) {
+        if (kBufs > 1 && jt + 1 < nt) {
             load_tile(k, jt + 1, ldqk, base_qk);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
         __syncthreads();
-        const float *Ts = Tb + (jt & 1) * kKT * kLD;
-        float acc[4][2];
+        // 64-key slices of the tile: keys lane and lane + 32 of each
+        for (int s0 = 0; s0 < kKT && j0 + s0 < T; s0 += 64) {
+            const float *Ts = Tb + (jt % kBufs) * kKT * kLD + s0 * kLD;
+            float acc[4][2];
 #pragma unroll
-        for (int r = 0; r < 4; r++) acc[r][0] = acc[r][1] = 0.0f;
+            for (int r = 0; r < 4; r++) acc[r][0] = acc[r][1] = 0.0f;
 #pragma unroll 2
-        for (int d4 = 0; d4 < kHeadDim / 4; d4++) {
-            const float4 k0 = *reinterpret_cast<const float4 *>(Ts + lane * kLD + 4 * d4);
-            const float4 k1 = *reinterpret_cast<const float4 *>(Ts + (lane + 32) * kLD + 4 * d4);
+            for (int d4 = 0; d4 < kHeadDim / 4; d4++) {
+                const float4 k0 = *reinterpret_cast<const float4 *>(Ts + lane * kLD + 4 * d4);
+                const float4 k1 = *reinterpret_cast<const float4 *>(Ts + (lane + 32) * kLD + 4 * d4);
 #pragma unroll
-            for (int r = 0; r < 4; r++) {
-                const float4 qv = *reinterpret_cast<const float4 *>(Qs + (wq * 4 + r) * kLD + 4 * d4);
-                acc[r][0] = fmaf(qv.x, k0.x, acc[r][0]);
-                acc[r][0] = fmaf(qv.y, k0.y, acc[r][0]);
-                acc[r][0] = fmaf(qv.z, k0.z, acc[r][0]);
-                acc[r][0] = fmaf(qv.w, k0.w, acc[r][0]);
-                acc[r][1] = fmaf(qv.x, k1.x, acc[r][1]);
-                acc[r][1] = fmaf(qv.y, k1.y, acc[r][1]);
-                acc[r][1] = fmaf(qv.z, k1.z, acc[r][1]);
-                acc[r][1] = fmaf(qv.w, k1.w, acc[r][1]);
+                for (int r = 0; r < 4; r++) {
+                    const float4 qv =
+                        *reinterpret_cast<const float4 *>(Qs + (wq * 4 + r) * kLD + 4 * d4);
+                    acc[r][0] = fmaf(qv.x, k0.x, acc[r][0]);
+                    acc[r][0] = fmaf(qv.y, k0.y, acc[r][0]);
+                    acc[r][0] = fmaf(qv.z, k0.z, acc[r][0]);
+                    acc[r][0] = fmaf(qv.w, k0.w, acc[r][0]);
+                    acc[r][1] = fmaf(qv.x, k1.x, acc[r][1]);
+                    acc[r][1] = fmaf(qv.y, k1.y, acc[r][1]);
+                    acc[r][1] = fmaf(qv.z, k1.z, acc[r][1]);
+                    acc[r][1] = fmaf(qv.w, k1.w, acc[r][1]);
+                }
             }
+#pragma unroll
+            for (int r = 0; r < 4; r++)
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    const int j = j0 + s0 + lane + 32 * c;
+                    if (j < T) Ss[(wq * 4 + r) * ldS + j] = __fmul_rn(acc[r][c], scale);
+                }
         }
-#pragma unroll
-        for (int r = 0; r < 4; r++)
-#pragma unroll
-            for (int c = 0; c < 2; c++) {
-                const int j = j0 + lane + 32 * c;
-                if (j < T) Ss[(wq * 4 + r) * ldS + j] = __fmul_rn(acc[r][c], scale);
-            }
-        __syncthreads();  // the buffer is refilled two tiles later
+        __syncthreads();  // the buffer is refilled (kBufs tiles later)
+        if (kBufs == 1 && jt + 1 < nt) load_tile(k, jt + 1, ldqk, base_qk);
     }
     load_tile(v, 0, ldvo, base_vo);  // lands during the softmax
     // ---- row softmax: warp wq owns rows 4wq..4wq+3
@@ -145,14 +157,14 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int jt = 0; jt < nt; jt++) {
         const int j0 = jt * kKT;
-        if (jt + 1 < nt) {
+        if (kBufs > 1 && jt + 1 < nt) {
             load_tile(v, jt + 1, ldvo, base_vo);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
         __syncthreads();
-        const float *Ts = Tb + (jt & 1) * kKT * kLD;
+        const float *Ts = Tb + (jt % kBufs) * kKT * kLD;
         const int jn = T - j0 < kKT ? T - j0 : kKT;
         int jj = 0;
         for (; jj + 4 <= jn; jj += 4) {
@@ -173,6 +185,7 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
             for (int r = 0; r < 4; r++) acc[r] = fmaf(Ss[(wq * 4 + r) * ldS + j0 + jj], vv, acc[r]);
         }
         __syncthreads();
+        if (kBufs == 1 && jt + 1 < nt) load_tile(v, jt + 1, ldvo, base_vo);
     }
 #pragma unroll
     for (int r = 0; r < 4; r++) {
@@ -183,8 +196,8 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
 
 int attention_lds(int T) { return (T + 3) / 4 * 4; }
 size_t attention_smem_bytes(int T) {
-    return sizeof(float) *
-           ((size_t)kBQ * kLD + 2 * (size_t)kKT * kLD + (size_t)kBQ * attention_lds(T));
+    const size_t tiles = T <= kKTAll ? (size_t)kKTAll : 2 * 64;
+    return sizeof(float) * ((size_t)kBQ * kLD + tiles * kLD + (size_t)kBQ * attention_lds(T));
 }
 
 }  // namespace
@@ -204,14 +217,22 @@ Status launch_attention(const float *q, const float *k, const float *v, float *o
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr[dev]) {
-        if (cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(attn_kernel<kKTAll, 1>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 227 * 1024) != cudaSuccess ||
+            cudaFuncSetAttribute(attn_kernel<64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  227 * 1024) != cudaSuccess)
             return ERR_CUDA;
         attr[dev] = true;
     }
     const int ldS = attention_lds(T);
-    attn_kernel<<<dim3((T + kBQ - 1) / kBQ, heads, B), kThreads, smem, st>>>(
-        q, k, v, o, T, ldqk, bsqk, ldvo, bsvo, scale, ldS);
+    const dim3 grid((T + kBQ - 1) / kBQ, heads, B);
+    if (T <= kKTAll)
+        attn_kernel<kKTAll, 1><<<grid, kThreads, smem, st>>>(q, k, v, o, T, ldqk, bsqk, ldvo, bsvo,
+                                                             scale, ldS);
+    else
+        attn_kernel<64, 2><<<grid, kThreads, smem, st>>>(q, k, v, o, T, ldqk, bsqk, ldvo, bsvo,
+                                                         scale, ldS);
     return cuda_status();
 }
 

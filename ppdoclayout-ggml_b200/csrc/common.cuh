@@ -22,12 +22,36 @@ constexpr int kNTok = 13125;
 
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_SILU = 2, ACT_GELU = 3 };
 
+// Round-to-nearest a / d for d = 1 + exp(-a) (d in [1, 2^128) or +inf), with
+// no branch, so that a loop over several values keeps them all in flight.
+// Markstein's method (P. Markstein, "Computation of elementary functions on
+// the IBM RISC System/6000 processor", IBM J. Res. Develop. 34(1), 1990):
+// an approximate reciprocal y of d refined by one Newton step
+// y += y (1 - d y), the quotient q = a y, then one correction with the exact
+// remainder, q += y (a - d q), both residuals taken with a single rounding
+// by fma.  Denominators above 2^64 scale a and d by 2^-64 first (exact), so
+// that 1/d stays a normal number; d = +inf gives a signed zero, as a / inf.
+__device__ __forceinline__ float silu_quotient(float a, float d) {
+    const bool big = d > 0x1p64f;
+    const float s = big ? 0x1p-64f : 1.0f;
+    const float as = a * s, ds = d * s;
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(ds));
+    y = __fmaf_rn(__fmaf_rn(-ds, y, 1.0f), y, y);
+    float q = __fmul_rn(as, y);
+    q = __fmaf_rn(__fmaf_rn(-ds, q, as), y, q);
+    if (d == 1.0f || a == 0.0f) q = a;  // exact quotients (a zero keeps its sign)
+    if (d == INFINITY) q = copysignf(0.0f, a);
+    return q;
+}
+
 // Activation exactly as the reference evaluates it: ReLU fmaxf, SiLU
-// x / (1 + exp(-x)) (patch:383-386, 426-430; ggml_silu), GELU with erf
-// (ggml_gelu_erf, src/ppdoclayout.cpp:687).
+// x / (1 + exp(-x)) (patch:383-386, 426-430; ggml_silu; the quotient
+// correctly rounded by silu_quotient), GELU with erf (ggml_gelu_erf,
+// src/ppdoclayout.cpp:687).
 __device__ __forceinline__ float act_apply(float v, int act) {
     if (act == ACT_RELU) return fmaxf(v, 0.0f);
-    if (act == ACT_SILU) return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+    if (act == ACT_SILU) return silu_quotient(v, __fadd_rn(1.0f, expf(-v)));
     if (act == ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
     return v;
 }

@@ -1129,7 +1129,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                 if (e.res_mode == 1) x = x + rres[j];
                                 box[j * 32 + lane] = x;
                             }
-#pragma unroll 1
+                            // four independent activations per pass: one at a
+                            // time, SiLU's exp -> divide chain is latency-bound
+#pragma unroll 4
                             for (int j = 0; j < 16; j++)
                                 box[j * 32 + lane] = act_apply(box[j * 32 + lane], ACT);
                         }

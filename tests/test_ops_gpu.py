@@ -166,6 +166,28 @@ def test_bias_act_and_copy(cuda):
     assert torch.equal(y, src)
 
 
+def test_silu_quotient_is_correctly_rounded(cuda):
+    """SiLU as every epilogue applies it, x / (1 + exp(-x)) with a
+    branch-free quotient, equals the same formula on the device with IEEE
+    division (torch: the same expf, then a correctly rounded divide) bit for
+    bit: 16M values over [-110, 40] (the overflow of exp(-x) below -88.7
+    included), the ranges near 0 and the powers of two."""
+    g = torch.Generator(device=cuda).manual_seed(5)
+    x = torch.cat([torch.rand(1 << 24, generator=g, device=cuda) * 150.0 - 110.0,
+                   torch.randn(1 << 20, generator=g, device=cuda),
+                   torch.randn(1 << 20, generator=g, device=cuda) * 1e-30,
+                   2.0 ** torch.arange(-126, 7, device=cuda, dtype=torch.float32),
+                   -(2.0 ** torch.arange(-126, 7, device=cuda, dtype=torch.float32)),
+                   torch.tensor([0.0, -0.0, 17.0, 88.7, -88.7, -89.0, -1e4], device=cuda)])
+    y = torch.empty_like(x)
+    zero = torch.tensor([-0.0], device=cuda)  # x + (-0) == x, signed zeros included
+    ppdl.check(ppdl.op_launch(ppdl.OP_BIASACT, y, [x, zero], params=[2]))
+    ref = x / (1 + torch.exp(-x))
+    torch.cuda.synchronize()
+    bad = (y.view(torch.int32) != ref.view(torch.int32)).nonzero().flatten()
+    assert bad.numel() == 0, (x[bad[:5]].tolist(), y[bad[:5]].tolist(), ref[bad[:5]].tolist())
+
+
 def test_errors_are_status_codes(cuda):
     out = torch.empty((300, 3), device=cuda)
     ml = torch.zeros((300, 40000), device=cuda)
