@@ -240,6 +240,7 @@ __device__ __forceinline__ void cp_async_zfill4(uint32_t dst, const float *src, 
 
 constexpr int kDwTW = 32, kDwTH = 32;  // 256 threads: 8 x 4-output groups x 32 rows
 constexpr size_t kDwPlaneSmemMax = 64 * 1024;  // whole-plane form up to this much input
+constexpr size_t kDwBandSmem = 24 * 1024;      // input rows of one band of the band form
 template <int K, int S>
 __global__ void __launch_bounds__(256)
 dwconv_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
@@ -353,6 +354,82 @@ dwconv_plane_kernel(const float *__restrict__ x, long long xbs, const float *__r
 #pragma unroll
         for (int o = 0; o < 4; o++)
             if (ox0 + o < OW) yr[o] = act_apply(__fadd_rn(s[o], bv), act);
+    }
+}
+
+// Band form, for planes too large for the whole-plane form (the 200 -> 100
+// downsample): one block per (page, channel, band of BR output rows, BR a
+// multiple of 4) loads the band's (BR - 1) S + K input rows, zero-bordered
+// (border P), into shared memory at a row pitch ld of 1 mod 32 with
+// asynchronous 4-byte copies, then computes the band.  Blocks are small
+// enough that several stay resident per SM, so one block's copies overlap
+// another's arithmetic.  A thread computes 4 vertically adjacent outputs of
+// one column, consecutive threads on consecutive columns: a warp's
+// shared-memory reads fall on consecutive words (conflict-free at stride 1,
+// two-way at stride 2; four consecutive outputs of a row per thread would
+// be four-way) and its stores on consecutive addresses.  Input rows stream
+// through K registers; each output sums over kh, then kw, as the tiled form.
+template <int K, int S>
+__global__ void __launch_bounds__(256)
+dwconv_band_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
+                   const float *__restrict__ bias, float *__restrict__ y, long long ybs, int C,
+                   int H, int W, int OH, int OW, int P, int act, int ld, int cols, int BR,
+                   int nbands) {
+    extern __shared__ float band_rows[];  // ((BR - 1) S + K) rows of ld floats
+    constexpr int NV = 3 * S + K;         // input rows of a 4-row output group
+    const long long plane = blockIdx.x / nbands;
+    const int band = (int)(blockIdx.x - plane * nbands);
+    const int b = (int)(plane / C), c = (int)(plane - (long long)b * C);
+    const float *xp = x + (long long)b * xbs + (long long)c * H * W;
+    const int oy0 = band * BR;
+    const int br = OH - oy0 < BR ? OH - oy0 : BR;
+    const int rows = (br - 1) * S + K, iy0 = oy0 * S - P;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const uint32_t dst = (uint32_t)__cvta_generic_to_shared(band_rows);
+    for (int r = warp; r < rows; r += nwarps) {
+        const int iy = iy0 + r;
+        const bool row_in = (unsigned)iy < (unsigned)H;
+        const float *xr = xp + (long long)iy * W;
+        for (int q = lane; q < cols; q += 32) {
+            const int ix = q - P;
+            const bool in = row_in && (unsigned)ix < (unsigned)W;
+            cp_async_zfill4(dst + (uint32_t)(r * ld + q) * 4u, in ? xr + ix : xp, in);
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    float wk[K * K];
+#pragma unroll
+    for (int i = 0; i < K * K; i++) wk[i] = __ldg(w + (long long)c * K * K + i);
+    const float bv = bias ? __ldg(bias + c) : 0.0f;
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    float *yp = y + (long long)b * ybs + (long long)c * OH * OW;
+    const int groups = (br + 3) >> 2;
+    for (int it = threadIdx.x; it < groups * OW; it += blockDim.x) {
+        const int rg = it / OW, ox = it - rg * OW;
+        float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        // input rows 4 rg S + j, j < NV, columns ox S .. ox S + K - 1; rows
+        // past the band's last are read from the buffer's unwritten tail, and
+        // their sums are not stored
+        const float *tp = band_rows + (4 * rg * S) * ld + ox * S;
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+            float r[K];
+#pragma unroll
+            for (int kw = 0; kw < K; kw++) r[kw] = tp[j * ld + kw];
+#pragma unroll
+            for (int o = 0; o < 4; o++) {
+                const int kh = j - o * S;
+                if (kh >= 0 && kh < K) {
+#pragma unroll
+                    for (int kw = 0; kw < K; kw++) s[o] = fmaf(r[kw], wk[kh * K + kw], s[o]);
+                }
+            }
+        }
+        float *yc = yp + (long long)(oy0 + 4 * rg) * OW + ox;
+#pragma unroll
+        for (int o = 0; o < 4; o++)
+            if (4 * rg + o < br) yc[(long long)o * OW] = act_apply(__fadd_rn(s[o], bv), act);
     }
 }
 
@@ -604,6 +681,54 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
         else
             return ERR_UNSUPPORTED;
 #undef PPDL_DW_PLANE
+        return cuda_status();
+    }
+    // band form for larger planes: bands of BR output rows (a multiple of 4)
+    // whose input rows fit kDwBandSmem bytes, unless not even four output rows do
+    const int bcols = W + 2 * P;  // >= (OW - 1) S + K
+    const int bld = (bcols + 30) / 32 * 32 + 1;
+    const int rows_fit = (int)(kDwBandSmem / 4 / bld);
+    if (rows_fit >= 3 * S + K) {
+        int BR = ((rows_fit - K) / S + 1) / 4 * 4;
+        const int OH4 = (OH + 3) / 4 * 4;
+        if (BR > OH4) BR = OH4;
+        const int nbands = (OH + BR - 1) / BR;
+        // equal bands (the last one no shorter than needed)
+        BR = ((OH + nbands - 1) / nbands + 3) / 4 * 4;
+        const long long nblk = (long long)B * C * nbands;
+        if (nblk > 0x7fffffffLL) return ERR_SHAPE;
+        const int smem = ((BR - 1) * S + K) * bld * 4;
+        // threads: the band's output groups in as few passes of at most 256
+        // threads as possible, in whole warps
+        const int items = ((BR + 3) / 4) * OW;
+        const int passes = (items + 255) / 256;
+        const int nthr = ((items + passes - 1) / passes + 31) / 32 * 32;
+        int dev = 0;
+        cudaGetDevice(&dev);
+#define PPDL_DW_BAND(KK, SS)                                                                      \
+    do {                                                                                         \
+        static bool attr[64] = {false};                                                          \
+        if (dev >= 64 || !attr[dev]) {                                                           \
+            if (cudaFuncSetAttribute(dwconv_band_kernel<KK, SS>,                                 \
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,                \
+                                     (int)kDwBandSmem) != cudaSuccess)                           \
+                return ERR_CUDA;                                                                 \
+            if (dev < 64) attr[dev] = true;                                                      \
+        }                                                                                        \
+        dwconv_band_kernel<KK, SS><<<(unsigned)nblk, nthr, smem, st>>>(                          \
+            x, xbs, w, bias, y, ybs, C, H, W, OH, OW, P, act, bld, bcols, BR, nbands);             \
+    } while (0)
+        if (K == 3 && S == 1)
+            PPDL_DW_BAND(3, 1);
+        else if (K == 3 && S == 2)
+            PPDL_DW_BAND(3, 2);
+        else if (K == 5 && S == 1)
+            PPDL_DW_BAND(5, 1);
+        else if (K == 5 && S == 2)
+            PPDL_DW_BAND(5, 2);
+        else
+            return ERR_UNSUPPORTED;
+#undef PPDL_DW_BAND
         return cuda_status();
     }
     const int tiles_x = (OW + kDwTW - 1) / kDwTW, tiles_y = (OH + kDwTH - 1) / kDwTH;

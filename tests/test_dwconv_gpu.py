@@ -5,9 +5,11 @@ light-block convs (K5, P2).
 Checked against a float64 torch grouped conv2d on the CPU of the same seeded
 data.  The kernel accumulates K*K FP32 fmas per output, so the gate is
 max|diff| / max|ref| <= 1e-6.  The cases cover the model's plane sizes
-(200 -> 100, 100 -> 50, 50 -> 25 and 50x50 / 25x25 stride 1), both forms
-(whole plane in shared memory, and 32x32 tiles for larger planes, with tiles
-cut by the plane edges), page batches, a NULL bias and every activation.
+(200 -> 100, 100 -> 50, 50 -> 25 and 50x50 / 25x25 stride 1), the three
+forms (whole plane in shared memory; bands of output rows for larger planes,
+with a shorter last band; 32x32 tiles for rows too wide for a band, with
+tiles cut by the plane edges), page batches, a NULL bias and every
+activation.
 """
 import ctypes as C
 
@@ -46,7 +48,7 @@ def _ref(x, w, b, S, P, act):
 
 @pytest.mark.parametrize("case", [
     # B, C, H, W, K, S, P, act, bias     (model layer it stands for)
-    (2, 16, 200, 200, 3, 2, 1, 0, True),   # st1.ds (128 ch at 200x200 in the model)
+    (2, 16, 200, 200, 3, 2, 1, 0, True),   # st1.ds (128 ch at 200x200 in the model), bands
     (2, 32, 100, 100, 3, 2, 1, 0, True),   # st2.ds
     (3, 64, 50, 50, 3, 2, 1, 0, True),     # st3.ds
     (2, 48, 50, 50, 5, 1, 2, 0, True),     # st2 light blocks, 5x5
@@ -54,9 +56,11 @@ def _ref(x, w, b, S, P, act):
     (1, 8, 37, 45, 3, 1, 1, 1, True),      # odd sizes, ReLU
     (1, 8, 41, 33, 5, 2, 2, 2, False),     # 5x5 stride 2, SiLU, no bias
     (1, 4, 70, 70, 3, 1, 1, 3, True),      # GELU
-    (1, 4, 150, 130, 3, 1, 1, 1, True),    # tiled form (plane too large), edge tiles
-    (1, 3, 257, 300, 5, 1, 2, 3, True),    # tiled form, 5x5, odd height
-    (1, 3, 203, 191, 5, 2, 2, 0, False),   # tiled form, 5x5 stride 2
+    (1, 4, 150, 130, 3, 1, 1, 1, True),    # 5 bands of 30 rows
+    (1, 3, 257, 300, 5, 1, 2, 3, True),    # 18 bands, 5x5, odd height
+    (1, 3, 203, 191, 5, 2, 2, 0, False),   # bands, 5x5 stride 2
+    (1, 2, 20, 1300, 5, 1, 2, 0, True),    # tiled form: 5 rows of 1300 exceed a band buffer
+    (2, 2, 9, 2100, 3, 2, 1, 1, True),     # tiled form, stride 2, edge tiles
 ])
 def test_depthwise_matches_float64(cuda, case):
     B, Cc, H, W, K, S, P, act, with_bias = case
