@@ -381,7 +381,8 @@ FWD_B = 8
 GEMM_KINDS = ("gemm_1x1", "wg_madd", "gemm_implicit", "gemm_linear")
 HBM_KINDS = ("wg_input", "wg_output", "dwconv", "msda", "mask_box", "glue", "postprocess", "topk",
              "im2col")
-SIMT_KINDS = ("attention",)  # FP32 CUDA-core q-k products: their FLOP rate, no roofline class
+# FP32 CUDA-core work (q-k products, the stem's narrow convs): their FLOP rate, no roofline class
+SIMT_KINDS = ("attention", "conv_direct")
 # DRAM traffic of the tensor-core GEMM per page of one forward (sum over its
 # launches of dram__bytes_read.sum + dram__bytes_write.sum), from an ncu
 # capture of one eager forward at 2 pages; None until measured.

@@ -138,6 +138,20 @@ PPDL_OPS_API int ppdl_conv2d_tf32x3(const float * x, int batch, int IC, int H, i
                                     int OC, int K, int S, int P, int OH, int OW, int act,
                                     float * b_split, float * y, long long y_bs, void * stream);
 
+/* No counterpart in the reference (its stem convs are im2col + mul_mat,
+   src/ppdoclayout.cpp:535-542): the direct FP32 convolution the forward uses
+   for narrow convs — at most 128 products per output (IC*K*K) into at most
+   32 channels, K 2..3, S 1..2 (the stem's 3 -> 32 k3-s2 and its 32 -> 16 /
+   16 -> 32 k2 convs) — on the CUDA cores; the forward routes its first
+   conv (27 products per output) here.  Same arguments and formula as
+   ppdl_conv2d_tf32x3 minus b_split; each output sums over ic, kh, kw in that
+   order in FP32.  Returns PPDL_OK, PPDL_ERR_UNSUPPORTED (outside the narrow
+   shapes), PPDL_ERR_SHAPE or PPDL_ERR_CUDA. */
+PPDL_OPS_API int ppdl_conv2d_direct(const float * x, int batch, int IC, int H, int W,
+                                    long long x_bs, const float * weight, const float * bias,
+                                    int OC, int K, int S, int P, int OH, int OW, int act,
+                                    float * y, long long y_bs, void * stream);
+
 /* Floats of b_split that ppdl_conv2d_tf32x3 needs for these sizes (0 for
    non-positive sizes). */
 PPDL_OPS_API long long ppdl_conv2d_tf32x3_workspace(int IC, int OC, int K);

@@ -158,6 +158,8 @@ PPDL_API void * ppdl_stream(ppdl_ctx * ctx);
 #define PPDL_STEP_IM2COL        13  /* conv operand packing for the GEMM */
 #define PPDL_STEP_ATTENTION     14  /* q-k products on SIMT FP32: fused
                                        softmax(q k^T) v, reading-order scores */
+#define PPDL_STEP_CONV_DIRECT   15  /* narrow convs on SIMT FP32 (the stem's
+                                       first three: IC*K*K <= 128, OC <= 32) */
 typedef struct {
     char    name[48];
     int32_t kind;   /* PPDL_STEP_* */

@@ -241,6 +241,8 @@ __device__ __forceinline__ void cp_async_zfill4(uint32_t dst, const float *src, 
 constexpr int kDwTW = 32, kDwTH = 32;  // 256 threads: 8 x 4-output groups x 32 rows
 constexpr size_t kDwPlaneSmemMax = 64 * 1024;  // whole-plane form up to this much input
 constexpr size_t kDwBandSmem = 24 * 1024;      // input rows of one band of the band form
+constexpr int kDirectTaps = 128;                   // products per output of the direct form
+constexpr size_t kDirectWindowBytes = 40 * 1024;   // input window per channel chunk
 template <int K, int S>
 __global__ void __launch_bounds__(256)
 dwconv_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
@@ -430,6 +432,132 @@ dwconv_band_kernel(const float *__restrict__ x, long long xbs, const float *__re
 #pragma unroll
         for (int o = 0; o < 4; o++)
             if (4 * rg + o < br) yc[(long long)o * OW] = act_apply(__fadd_rn(s[o], bv), act);
+    }
+}
+
+// ---- direct convolution of narrow convs (the stem) -------------------------
+// For convs whose outputs each sum at most kDirectTaps products (IC K K) into
+// at most 32 channels (the stem's 3 -> 32 k3-s2 and its 32 -> 16 / 16 -> 32
+// k2 convs), a tensor-core tile of 128 pixels x N <= 32 channels carries more
+// operand bytes than arithmetic; these run on the CUDA cores in FP32.
+// Register tiling: a thread computes 4 consecutive output pixels of a row for
+// 16 channels (64 accumulators); per (input channel, kernel row) it reads the
+// 3 S + K window values its pixels share as float4s from shared memory, per
+// tap the 16 weights as 4 broadcast float4s, and issues 64 FMAs.  Block:
+// 256 threads = 16 output rows x 64 columns (16 lanes per row).  Shared
+// memory: the weights of the block's 16 channels [ic][kh][kw][16] and the
+// input window, ICB channels at a time, filled with asynchronous 4-byte
+// copies (zeros outside the input: padding P at the top/left, the bottom /
+// right padding follows from OH, OW).  Window rows have a pitch of a
+// multiple of 4 floats and start at the block's first input column, so a
+// thread's reads are 16-byte aligned.  Each output sums over ic, kh, kw in
+// that order with fmaf, then adds the bias.
+constexpr int kDirectRows = 16, kDirectCols = 64, kDirectOCB = 16;
+template <int K, int S>
+__global__ void __launch_bounds__(256)
+conv_direct_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
+                   const float *__restrict__ bias, float *__restrict__ y, long long ybs, int IC,
+                   int H, int W, int OC, int OH, int OW, int P, int act, int tiles_x, int ICB) {
+    constexpr int NX = 3 * S + K;        // window values of a thread's 4 pixels per row
+    constexpr int N4 = (NX + 3) / 4;     // float4 reads covering them
+    constexpr int IH = (kDirectRows - 1) * S + K;
+    constexpr int IWP = ((kDirectCols / 4 - 1) * 4 * S + 4 * N4 + 3) / 4 * 4;  // row pitch
+    constexpr int IW = (kDirectCols - 1) * S + K;  // columns copied
+    extern __shared__ float4 dsm4[];
+    float *ws = reinterpret_cast<float *>(dsm4);           // [IC * K * K][16]
+    float *xs = ws + (size_t)IC * K * K * kDirectOCB;      // [ICB][IH][IWP]
+    const int tyi = blockIdx.x / tiles_x;
+    const int tx0 = (blockIdx.x - tyi * tiles_x) * kDirectCols, ty0 = tyi * kDirectRows;
+    const int oc0 = blockIdx.y * kDirectOCB, b = blockIdx.z;
+    const int t = threadIdx.x, ly = t >> 4, lx = t & 15;  // output row, 4-pixel group
+    for (int i = t; i < IC * K * K * kDirectOCB; i += blockDim.x) {
+        const int j = i & (kDirectOCB - 1), tap = i >> 4;  // tap = (ic * K + kh) * K + kw
+        ws[i] = oc0 + j < OC ? __ldg(w + (long long)(oc0 + j) * IC * K * K + tap) : 0.0f;
+    }
+    const float *xb = x + (long long)b * xbs;
+    const int iy0 = ty0 * S - P, ix0 = tx0 * S - P;
+    const uint32_t xs_s = (uint32_t)__cvta_generic_to_shared(xs);
+    float acc[4][kDirectOCB];
+#pragma unroll
+    for (int p = 0; p < 4; p++)
+#pragma unroll
+        for (int j = 0; j < kDirectOCB; j++) acc[p][j] = 0.0f;
+    for (int ic0 = 0; ic0 < IC; ic0 += ICB) {
+        const int nc = IC - ic0 < ICB ? IC - ic0 : ICB;
+        __syncthreads();  // the previous chunk is consumed (and the weights written)
+        // one window row per warp pass: 16-byte copies of 4 columns where the
+        // row and the 4 columns allow, 4-byte copies (zero-filled outside the
+        // input) elsewhere
+        const int warp = t >> 5, lane = t & 31;
+        for (int rr = warp; rr < nc * IH; rr += 8) {  // rr = c * IH + r
+            const int c = rr / IH, r = rr - c * IH;
+            const int iy = iy0 + r;
+            const uint32_t drow = xs_s + (uint32_t)(rr * IWP) * 4u;
+            if ((unsigned)iy >= (unsigned)H) {
+                for (int q = lane; q < IW; q += 32) cp_async_zfill4(drow + 4u * q, xb, false);
+                continue;
+            }
+            const float *srow = xb + (long long)(ic0 + c) * H * W + (long long)iy * W;
+            const bool vec = ((uintptr_t)(srow + ix0) & 15) == 0;
+            for (int q4 = 4 * lane; q4 < IW; q4 += 128) {
+                const int ix = ix0 + q4;
+                if (vec && ix >= 0 && ix + 3 < W && q4 + 3 < IWP) {
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(drow + 4u * q4),
+                                 "l"(srow + ix)
+                                 : "memory");
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const bool in = ix + u >= 0 && ix + u < W && q4 + u < IW;
+                        if (q4 + u < IW) cp_async_zfill4(drow + 4u * (q4 + u), in ? srow + ix + u : xb, in);
+                    }
+                }
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();
+        for (int c = 0; c < nc; c++) {
+            const float4 *wc = reinterpret_cast<const float4 *>(ws) +
+                               (size_t)(ic0 + c) * K * K * (kDirectOCB / 4);
+#pragma unroll
+            for (int kh = 0; kh < K; kh++) {
+                const float4 *xr = reinterpret_cast<const float4 *>(
+                    xs + ((size_t)c * IH + ly * S + kh) * IWP + lx * 4 * S);
+                float xv[4 * N4];
+#pragma unroll
+                for (int u = 0; u < N4; u++) {
+                    const float4 v = xr[u];
+                    xv[4 * u] = v.x; xv[4 * u + 1] = v.y; xv[4 * u + 2] = v.z; xv[4 * u + 3] = v.w;
+                }
+#pragma unroll
+                for (int kw = 0; kw < K; kw++) {
+                    float wv[kDirectOCB];
+#pragma unroll
+                    for (int q = 0; q < kDirectOCB / 4; q++) {
+                        const float4 v = wc[(kh * K + kw) * (kDirectOCB / 4) + q];
+                        wv[4 * q] = v.x; wv[4 * q + 1] = v.y; wv[4 * q + 2] = v.z; wv[4 * q + 3] = v.w;
+                    }
+#pragma unroll
+                    for (int p = 0; p < 4; p++)
+#pragma unroll
+                        for (int j = 0; j < kDirectOCB; j++)
+                            acc[p][j] = fmaf(xv[p * S + kw], wv[j], acc[p][j]);
+                }
+            }
+        }
+    }
+    const int oy = ty0 + ly, ox0 = tx0 + 4 * lx;
+    if (oy >= OH) return;
+    float *yp = y + (long long)b * ybs + (long long)oy * OW;
+#pragma unroll
+    for (int j = 0; j < kDirectOCB; j++) {
+        if (oc0 + j >= OC) break;
+        const float bv = bias ? __ldg(bias + oc0 + j) : 0.0f;
+        float *yc = yp + (long long)(oc0 + j) * OH * OW;
+#pragma unroll
+        for (int p = 0; p < 4; p++)
+            if (ox0 + p < OW) yc[ox0 + p] = act_apply(__fadd_rn(acc[p][j], bv), act);
     }
 }
 
@@ -743,6 +871,57 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
         dwconv_kernel<5, 2><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
     else
         return ERR_UNSUPPORTED;
+    return cuda_status();
+}
+
+bool conv_direct_ok(int IC, int OC, int K, int S) {
+    return IC > 0 && OC > 0 && OC <= 32 && IC * K * K <= kDirectTaps && (K == 2 || K == 3) &&
+           (S == 1 || S == 2);
+}
+
+Status launch_conv_direct(const float *x, long long xbs, const float *w, const float *bias,
+                          float *y, long long ybs, int IC, int H, int W, int OC, int K, int S,
+                          int P, int OH, int OW, int act, int B, cudaStream_t st) {
+    if (!conv_direct_ok(IC, OC, K, S) || H <= 0 || W <= 0 || OH <= 0 || OW <= 0 || P < 0 ||
+        P >= K || B <= 0 || B > 65535 || act < 0 || act > 3)
+        return ERR_SHAPE;
+    const int tiles_x = (OW + kDirectCols - 1) / kDirectCols;
+    const int tiles_y = (OH + kDirectRows - 1) / kDirectRows;
+    if ((long long)tiles_x * tiles_y > 0x7fffffffLL) return ERR_SHAPE;
+    const int N4 = (3 * S + K + 3) / 4;
+    const int IH = (kDirectRows - 1) * S + K;
+    const int IWP = ((kDirectCols / 4 - 1) * 4 * S + 4 * N4 + 3) / 4 * 4;
+    // input channels per chunk: a window of up to kDirectWindowBytes
+    int ICB = (int)(kDirectWindowBytes / (4 * IH * IWP));
+    if (ICB > IC) ICB = IC;
+    if (ICB < 1) ICB = 1;
+    const int smem = 4 * (IC * K * K * kDirectOCB + ICB * IH * IWP);
+    const dim3 g((unsigned)(tiles_x * tiles_y), (unsigned)((OC + kDirectOCB - 1) / kDirectOCB),
+                 (unsigned)B);
+    int dev = 0;
+    cudaGetDevice(&dev);
+#define PPDL_DIRECT(KK, SS)                                                                       \
+    do {                                                                                         \
+        static bool attr[64] = {false};                                                          \
+        if (dev >= 64 || !attr[dev]) {                                                           \
+            if (cudaFuncSetAttribute(conv_direct_kernel<KK, SS>,                                 \
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,                \
+                                     64 * 1024) != cudaSuccess)                                  \
+                return ERR_CUDA;                                                                 \
+            if (dev < 64) attr[dev] = true;                                                      \
+        }                                                                                        \
+        conv_direct_kernel<KK, SS><<<g, 256, smem, st>>>(x, xbs, w, bias, y, ybs, IC, H, W, OC,  \
+                                                        OH, OW, P, act, tiles_x, ICB);           \
+    } while (0)
+    if (K == 2 && S == 1)
+        PPDL_DIRECT(2, 1);
+    else if (K == 2 && S == 2)
+        PPDL_DIRECT(2, 2);
+    else if (K == 3 && S == 1)
+        PPDL_DIRECT(3, 1);
+    else
+        PPDL_DIRECT(3, 2);
+#undef PPDL_DIRECT
     return cuda_status();
 }
 

@@ -43,6 +43,14 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
 
 // 2x2 stride-1 max pool of the input zero-padded by one row/column at the
 // end: out is H x W like the input (W a multiple of 4, 16-byte aligned planes)
+// Direct FP32 conv for narrow convs: OC <= 32, IC*K*K <= 128, K 2..3, S 1..2.
+// y[b][oc] = act(bias + sum_{ic,kh,kw} w[oc][ic][kh][kw] x[b][ic][oy S + kh - P][ox S + kw - P]),
+// zero outside H x W (bottom/right padding from OH, OW); bias may be null.
+bool conv_direct_ok(int IC, int OC, int K, int S);
+Status launch_conv_direct(const float *x, long long xbs, const float *w, const float *bias,
+                          float *y, long long ybs, int IC, int H, int W, int OC, int K, int S,
+                          int P, int OH, int OW, int act, int B, cudaStream_t st);
+
 Status launch_maxpool2_pad(const float *x, long long xbs, float *y, long long ybs, int C, int H,
                            int W, int B, cudaStream_t st);
 

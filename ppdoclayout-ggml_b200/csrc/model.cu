@@ -528,6 +528,20 @@ public:
             });
             return;
         }
+        // the stem's first conv (27 products per output into 32 channels):
+        // direct FP32 on the CUDA cores, 157 us against 196 us for the
+        // implicit GEMM, whose k-blocks would be two-thirds padding.  The k2
+        // stem convs (64 and 128 products) measured faster on the tensor cores
+        // (168 / 206 us against 223 / 219 us direct), so the forward keeps them
+        // there.
+        if (!res_mode && IC * K * K <= 32 && conv_direct_ok(IC, OC, K, s)) {
+            push(name, PPDL_STEP_CONV_DIRECT, 2.0 * OC * OH * OW * IC * K * K,
+                 4.0 * ((double)IC * x.plane() + (double)OC * OH * OW), [=]() {
+                return launch_conv_direct(x.p, x.bs, wp, bp, y.p, y.bs, IC, x.H, x.W, OC, K, s, p,
+                                          OH, OW, act, nb, st);
+            });
+            return;
+        }
         // k3-s2 / k2: implicit GEMM on the CHW input (no im2col buffer)
         if (use_tc) {
             auto g = plan_conv_implicit(x, K, s, p, OC, OH, OW, wp,

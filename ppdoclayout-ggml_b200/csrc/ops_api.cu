@@ -103,6 +103,24 @@ PPDL_OPS_API int ppdl_depthwise_conv2d(const float *x, int batch, int C, int H, 
                                          batch, (cudaStream_t)stream));
 }
 
+PPDL_OPS_API int ppdl_conv2d_direct(const float *x, int batch, int IC, int H, int W,
+                                    long long x_bs, const float *weight, const float *bias,
+                                    int OC, int K, int S, int P, int OH, int OW, int act,
+                                    float *y, long long y_bs, void *stream) {
+    g_err[0] = 0;
+    if (!x || !weight || !y || batch <= 0 || H <= 0 || W <= 0 || OH <= 0 || OW <= 0 || act < 0 ||
+        act > 3 || P < 0 || P >= K)
+        return fail(PPDL_ERR_SHAPE, "conv2d_direct: bad sizes, activation or null pointer");
+    if (!ppdl::conv_direct_ok(IC, OC, K, S))
+        return fail(PPDL_ERR_UNSUPPORTED,
+                    "conv2d_direct: needs OC <= 32, IC*K*K <= 128, K 2..3, S 1..2");
+    if ((long long)(OH - 1) * S - P >= H || (long long)(OW - 1) * S - P >= W)
+        return fail(PPDL_ERR_SHAPE, "conv2d_direct: output %dx%d larger than the input allows",
+                    OH, OW);
+    return to_status(ppdl::launch_conv_direct(x, x_bs, weight, bias, y, y_bs, IC, H, W, OC, K, S,
+                                              P, OH, OW, act, batch, (cudaStream_t)stream));
+}
+
 PPDL_OPS_API long long ppdl_conv2d_tf32x3_workspace(int IC, int OC, int K) {
     if (IC <= 0 || OC <= 0 || K <= 0) return 0;
     const long long kp = (IC * K * K + 3) / 4 * 4, kb = ppdl::tc_conv_box_kdim(IC, K);

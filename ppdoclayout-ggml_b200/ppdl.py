@@ -145,7 +145,7 @@ def op_supported(op_id, params=()) -> bool:
 STEP_KINDS = {0: "other", 1: "gemm_1x1", 2: "wg_madd", 3: "gemm_implicit", 4: "gemm_linear",
               5: "wg_input", 6: "wg_output", 7: "dwconv", 8: "msda", 9: "mask_box", 10: "topk",
               11: "postprocess", 12: "glue", 13: "im2col",
-              14: "attention"}
+              14: "attention", 15: "conv_direct"}
 
 
 class StepStat(C.Structure):
