@@ -67,7 +67,8 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms during the
+    timed region (a 20-step forward region lasts about 0.3 s)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -82,7 +83,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
@@ -96,7 +97,7 @@ class ClockSampler:
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
+        time.sleep(0.06)  # the sample in flight at the end of the region
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -607,14 +608,19 @@ def run_forward(args, world, rank, local, pg):
 
 
 # --------------------------------------------- per-kernel sweeps (configs 1, 2)
-L2_FLUSH_BYTES = 256 << 20  # written between timed launches (L2 is 126 MB)
+L2_FLUSH_BYTES = 256 << 20  # written, then another buffer read, between timed launches (L2 is 126 MB)
 
 
 def _time_launches(fn, dev, iters=10, warmup=3, flush=True):
     """Mean device time (ms) of fn() over iters launches, CUDA events on the
-    current stream around each launch, L2 flushed in between (untimed)."""
+    current stream around each launch, L2 flushed in between (untimed): a
+    write of a buffer larger than L2, then a read of another one, so that the
+    write's dirty lines go back to HBM before the timed launch rather than
+    during it."""
     import torch
     buf = torch.empty(L2_FLUSH_BYTES // 4, device=dev) if flush else None
+    rd = torch.ones(L2_FLUSH_BYTES // 4, device=dev) if flush else None
+    acc = torch.empty((), device=dev) if flush else None
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize(dev)
@@ -623,6 +629,7 @@ def _time_launches(fn, dev, iters=10, warmup=3, flush=True):
     for _ in range(iters):
         if buf is not None:
             buf.fill_(1.0)
+            torch.sum(rd, dim=0, out=acc)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(st)
         fn()
@@ -744,7 +751,7 @@ def kernel_sweeps(dev, hbm, tc):
                         dev)
     out["config1_msda"] = {"pages": B, "ms": round(ms, 5), "gbs": round(alg / ms / 1e6, 1),
                            "frac_of_hbm": round(alg / ms / 1e6 / hbm, 4),
-                           "algorithmic_bytes": alg, "l2": "flushed between launches"}
+                           "algorithmic_bytes": alg, "l2": "flushed between launches (256 MB write, then 256 MB read)"}
     del val, loc, w, o
     # ---- config 2
     _bind_conv_entries(L)
@@ -1151,7 +1158,7 @@ def run_conv(args, world, rank, local, pg):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: activations N(0,1), Kaiming weights, bias N(0,0.1), ReLU",
         "config": {"workload": f"config 2: {kind} conv {H}x{H}x{IC}->{OC}, {Bc} pages",
-                   "l2": "flushed between launches", "parallelism": f"dp{world} (no collective)"},
+                   "l2": "flushed between launches (256 MB write, then 256 MB read)", "parallelism": f"dp{world} (no collective)"},
         "roofline": {"bound": "tensor", "achieved": round(executed / ms / 1e9, 2),
                      "peak": round(tc, 1), "unit": "TFLOP/s",
                      "frac": round(executed / ms / 1e9 / tc, 4),
