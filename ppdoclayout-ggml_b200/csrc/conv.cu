@@ -301,31 +301,55 @@ dwconv_kernel(const float *__restrict__ x, long long xbs, const float *__restric
 
 // Whole-plane form for planes whose padded input fits in shared memory (the
 // light blocks' 50x50 and 25x25 planes, the 100 -> 50 and 50 -> 25
-// downsamples): one block per (page, channel) reads the plane exactly once,
-// row by row, into a zero-bordered copy (border P), then computes every
-// output as above, 4 consecutive outputs of a row per work item, and writes
-// the plane contiguously.  The tiled kernel re-reads halo rows and columns
-// of neighbouring tiles and wastes threads on partly empty edge tiles.
-template <int K, int S>
+// downsamples): one block per (page, channel) copies the plane once into a
+// zero-bordered copy (border P; 8-byte asynchronous copies when P and W are
+// even, 4-byte otherwise), then a thread computes a 4 x 4 block of outputs:
+// per input row of its (3 S + K)-square window it reads the row segment as
+// float4s (rows of ld floats, ld % 4 == 0, so the reads are 16-byte aligned
+// and a quarter warp's are contiguous), and adds it into the outputs whose
+// kernel row it is.  Per output the sum runs over kh, then kw, with fmaf,
+// then + bias and the activation (ACT: 0 none, 1 ReLU, -1 the runtime act);
+// rows of even width leave as float2 stores (when y allows 8-byte stores).
+// The form is issue-bound, so its shape keeps the instructions per output
+// low: 25 FMAs, about one shared load and a fraction of a copy.
+template <int K, int S, int ACT>
 __global__ void __launch_bounds__(256)
 dwconv_plane_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
                     const float *__restrict__ bias, float *__restrict__ y, long long ybs, int H,
-                    int W, int OH, int OW, int P, int act, int ld) {
-    extern __shared__ float plane[];  // (H + 2P) rows of ld >= W + 2P floats
-    constexpr int NV = 3 * S + K;
+                    int W, int OH, int OW, int P, int act, int ld, int HPp, int GX, int GY,
+                    int pairs, int even) {
+    extern __shared__ float4 plane4[];
+    float *plane = reinterpret_cast<float *>(plane4);  // HPp rows of ld floats
+    constexpr int NX = 3 * S + K;                      // window rows / columns of a 4 x 4 block
+    constexpr int N4 = (NX + 3) / 4;
     const int c = blockIdx.x, b = blockIdx.y;
     const float *xp = x + (long long)b * xbs + (long long)c * H * W;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    const int HP = H + 2 * P, WP = W + 2 * P;
     const uint32_t plane_s = (uint32_t)__cvta_generic_to_shared(plane);
-    for (int r = warp; r < HP; r += nwarps) {
+    // one row per warp pass
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    for (int r = warp; r < HPp; r += nwarps) {
         const int iy = r - P;
         const bool row_in = (unsigned)iy < (unsigned)H;
         const float *xr = xp + (long long)iy * W;
-        for (int q = lane; q < WP; q += 32) {
-            const int ix = q - P;
-            const bool in = row_in && (unsigned)ix < (unsigned)W;
-            cp_async_zfill4(plane_s + (uint32_t)(r * ld + q) * 4u, in ? xr + ix : xp, in);
+        float *prow = plane + r * ld;
+        const uint32_t srow = plane_s + (uint32_t)(r * ld) * 4u;
+        if (pairs) {
+            // P and W even: a column pair is wholly inside or outside the image
+            for (int q = 2 * lane; q < ld; q += 64) {
+                const int ix = q - P;
+                if (row_in && (unsigned)ix < (unsigned)W)
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(srow + 4u * q),
+                                 "l"(xr + ix)
+                                 : "memory");
+                else
+                    *reinterpret_cast<float2 *>(prow + q) = make_float2(0.0f, 0.0f);
+            }
+        } else {
+            for (int q = lane; q < ld; q += 32) {
+                const int ix = q - P;
+                const bool in = row_in && (unsigned)ix < (unsigned)W;
+                cp_async_zfill4(srow + 4u * q, in ? xr + ix : xp, in);
+            }
         }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -335,27 +359,56 @@ dwconv_plane_kernel(const float *__restrict__ x, long long xbs, const float *__r
     const float bv = bias ? __ldg(bias + c) : 0.0f;
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    const int ng = (OW + 3) >> 2;  // 4-output groups per row
     float *yp = y + (long long)b * ybs + (long long)c * OH * OW;
-    for (int item = threadIdx.x; item < OH * ng; item += blockDim.x) {
-        const int oy = item / ng, g = item - oy * ng;
-        const int ox0 = 4 * g;
-        float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        const float *tp = plane + (oy * S) * ld + ox0 * S;
+    for (int it = threadIdx.x; it < GX * GY; it += blockDim.x) {
+        const int ty = it / GX, tx = it - ty * GX;
+        const int oy0 = 4 * ty, ox0 = 4 * tx;
+        float s[4][4];
 #pragma unroll
-        for (int kh = 0; kh < K; kh++) {
-            float v[NV];
+        for (int r = 0; r < 4; r++)
 #pragma unroll
-            for (int i = 0; i < NV; i++) v[i] = tp[kh * ld + i];
+            for (int q = 0; q < 4; q++) s[r][q] = 0.0f;
+        const float4 *wp = reinterpret_cast<const float4 *>(plane + (oy0 * S) * ld + ox0 * S);
 #pragma unroll
-            for (int o = 0; o < 4; o++)
+        for (int j = 0; j < NX; j++) {
+            float v[4 * N4];
 #pragma unroll
-                for (int kw = 0; kw < K; kw++) s[o] = fmaf(v[o * S + kw], wk[kh * K + kw], s[o]);
+            for (int u = 0; u < N4; u++) {
+                const float4 t = wp[(j * ld >> 2) + u];
+                v[4 * u] = t.x; v[4 * u + 1] = t.y; v[4 * u + 2] = t.z; v[4 * u + 3] = t.w;
+            }
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const int kh = j - r * S;
+                if (kh >= 0 && kh < K) {
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+#pragma unroll
+                        for (int kw = 0; kw < K; kw++)
+                            s[r][q] = fmaf(v[q * S + kw], wk[kh * K + kw], s[r][q]);
+                }
+            }
         }
-        float *yr = yp + (long long)oy * OW + ox0;
 #pragma unroll
-        for (int o = 0; o < 4; o++)
-            if (ox0 + o < OW) yr[o] = act_apply(__fadd_rn(s[o], bv), act);
+        for (int r = 0; r < 4; r++) {
+            const int oy = oy0 + r;
+            if (oy >= OH) break;
+            float o[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float v = __fadd_rn(s[r][q], bv);
+                o[q] = ACT == 0 ? v : ACT == 1 ? fmaxf(v, 0.0f) : act_apply(v, act);
+            }
+            float *yr = yp + (long long)oy * OW + ox0;
+            if (even && ox0 + 4 <= OW) {
+                reinterpret_cast<float2 *>(yr)[0] = make_float2(o[0], o[1]);
+                reinterpret_cast<float2 *>(yr)[1] = make_float2(o[2], o[3]);
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; q++)
+                    if (ox0 + q < OW) yr[q] = o[q];
+            }
+        }
     }
 }
 
@@ -767,49 +820,73 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
     const int OH = (H + 2 * P - K) / S + 1, OW = (W + 2 * P - K) / S + 1;
     if (OH <= 0 || OW <= 0 || C <= 0 || C > 65535 || B <= 0 || B > 65535 || P < 0 || P >= K)
         return ERR_SHAPE;
-    // whole-plane form: the zero-bordered input plane plus the columns the
-    // last 4-output group reads past it, row pitch 1 mod 32
-    const int need_w = 4 * S * ((OW + 3) / 4) - S + K;  // columns the last group reads
-    const int WP = W + 2 * P > need_w ? W + 2 * P : need_w;
-    const int ld = (WP + 30) / 32 * 32 + 1;
-    const int HPR = (OH - 1) * S + K > H + 2 * P ? (OH - 1) * S + K : H + 2 * P;
-    const size_t plane_bytes = (size_t)HPR * ld * 4;
-    if (plane_bytes <= kDwPlaneSmemMax) {
-        const dim3 g(C, B);
-        const int sm = (int)plane_bytes;
-        // threads: the 4-output items of the plane spread over as few passes
-        // of at most 256 threads as possible, in whole warps (a 25 x 25 plane:
-        // 175 items, 192 threads), so small planes keep more blocks resident
-        const int items = OH * ((OW + 3) / 4);
-        const int passes = (items + 255) / 256;
-        const int nthr = ((items + passes - 1) / passes + 31) / 32 * 32;
-        int dev = 0;
-        cudaGetDevice(&dev);
-#define PPDL_DW_PLANE(KK, SS)                                                                     \
+    // whole-plane form: the zero-bordered plane with the rows and columns the
+    // 4 x 4 output blocks read (their float4 row segments included), row
+    // pitch a multiple of 4 floats
+    {
+        const int GX = (OW + 3) / 4, GY = (OH + 3) / 4;
+        const int n4 = (3 * S + K + 3) / 4;
+        int cols = (4 * GX - 1) * S + K;
+        if (cols < 4 * (GX - 1) * S + 4 * n4) cols = 4 * (GX - 1) * S + 4 * n4;
+        if (cols < W + 2 * P) cols = W + 2 * P;
+        const int ld = (cols + 3) / 4 * 4;
+        const int HPp = (4 * GY - 1) * S + K;
+        const size_t plane_bytes = (size_t)HPp * ld * 4;
+        // 8-byte copies: even P and W keep every pair wholly inside or outside
+        // the image, and x, the page stride and the plane 8-byte aligned
+        const int pairs = (P % 2 == 0 && W % 2 == 0 && ((uintptr_t)x & 7) == 0 && xbs % 2 == 0)
+                              ? 1 : 0;
+        // float2 stores: even rows, y and its page stride 8-byte aligned
+        const int even = (OW % 2 == 0 && ((uintptr_t)y & 7) == 0 && ybs % 2 == 0) ? 1 : 0;
+        if (plane_bytes <= kDwPlaneSmemMax && (long long)HPp * ld < (1LL << 31)) {
+            const dim3 g(C, B);
+            const int sm = (int)plane_bytes;
+            // threads: the 4 x 4 blocks of the plane in as few passes of at most
+            // 256 threads as possible, in whole warps (a 50 x 50 plane: 169
+            // blocks, 192 threads), and at least 128 for the copy
+            const int items = GX * GY;
+            const int passes = (items + 255) / 256;
+            int nthr = ((items + passes - 1) / passes + 31) / 32 * 32;
+            if (nthr < 128) nthr = 128;
+            int dev = 0;
+            cudaGetDevice(&dev);
+            const int af = act == ACT_NONE ? 0 : act == ACT_RELU ? 1 : 2;
+#define PPDL_DW_PLANE(KK, SS, AA)                                                                 \
     do {                                                                                         \
         static bool attr[64] = {false};                                                          \
         if (dev >= 64 || !attr[dev]) {                                                           \
-            if (cudaFuncSetAttribute(dwconv_plane_kernel<KK, SS>,                                \
+            if (cudaFuncSetAttribute(dwconv_plane_kernel<KK, SS, AA>,                            \
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,                \
                                      (int)kDwPlaneSmemMax) != cudaSuccess)                       \
                 return ERR_CUDA;                                                                 \
             if (dev < 64) attr[dev] = true;                                                      \
         }                                                                                        \
-        dwconv_plane_kernel<KK, SS><<<g, nthr, sm, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW,  \
-                                                        P, act, ld);                             \
+        dwconv_plane_kernel<KK, SS, AA><<<g, nthr, sm, st>>>(                                    \
+            x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, ld, HPp, GX, GY, pairs, even);        \
     } while (0)
-        if (K == 3 && S == 1)
-            PPDL_DW_PLANE(3, 1);
-        else if (K == 3 && S == 2)
-            PPDL_DW_PLANE(3, 2);
-        else if (K == 5 && S == 1)
-            PPDL_DW_PLANE(5, 1);
-        else if (K == 5 && S == 2)
-            PPDL_DW_PLANE(5, 2);
-        else
-            return ERR_UNSUPPORTED;
+#define PPDL_DW_PLANE_ACT(KK, SS)                                                                 \
+    do {                                                                                         \
+        if (af == 0)                                                                             \
+            PPDL_DW_PLANE(KK, SS, 0);                                                            \
+        else if (af == 1)                                                                        \
+            PPDL_DW_PLANE(KK, SS, 1);                                                            \
+        else                                                                                     \
+            PPDL_DW_PLANE(KK, SS, -1);                                                           \
+    } while (0)
+            if (K == 3 && S == 1)
+                PPDL_DW_PLANE_ACT(3, 1);
+            else if (K == 3 && S == 2)
+                PPDL_DW_PLANE_ACT(3, 2);
+            else if (K == 5 && S == 1)
+                PPDL_DW_PLANE_ACT(5, 1);
+            else if (K == 5 && S == 2)
+                PPDL_DW_PLANE_ACT(5, 2);
+            else
+                return ERR_UNSUPPORTED;
+#undef PPDL_DW_PLANE_ACT
 #undef PPDL_DW_PLANE
-        return cuda_status();
+            return cuda_status();
+        }
     }
     // band form for larger planes: bands of BR output rows (a multiple of 4)
     // whose input rows fit kDwBandSmem bytes, unless not even four output rows do

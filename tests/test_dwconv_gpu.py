@@ -59,6 +59,8 @@ def _ref(x, w, b, S, P, act):
     (1, 4, 150, 130, 3, 1, 1, 1, True),    # 5 bands of 30 rows
     (1, 3, 257, 300, 5, 1, 2, 3, True),    # 18 bands, 5x5, odd height
     (1, 3, 203, 191, 5, 2, 2, 0, False),   # bands, 5x5 stride 2
+    (2, 5, 51, 47, 5, 1, 2, 1, True),      # odd W: 4-byte copies, scalar stores
+    (1, 6, 30, 30, 3, 2, 1, 2, True),      # odd P (4-byte copies), SiLU
     (1, 2, 20, 1300, 5, 1, 2, 0, True),    # tiled form: 5 rows of 1300 exceed a band buffer
     (2, 2, 9, 2100, 3, 2, 1, 1, True),     # tiled form, stride 2, edge tiles
 ])
