@@ -108,6 +108,65 @@ wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__
         }
 }
 
+// Rows of 4 * TW floats (W % 4 == 0, 16-byte aligned rows) and padding 1, the
+// forward's case: the thread of tile (ty, tx) reads the 4 aligned columns
+// 4 tx .. 4 tx + 3 of each of its 6 window rows as one float4 (a warp's
+// reads are contiguous), and takes column 4 tx - 1 from the previous lane's
+// float4 and column 4 tx + 4 from the next lane's by warp shuffles (a scalar
+// load at the warp's edges; zeros at the plane's left and right borders).
+// 6 vector loads per (tile, channel) instead of 36 scalar ones; the transform
+// and the stores are those of wg4_input_kernel.
+__global__ void __launch_bounds__(256, 4)
+wg4_input_vec_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ dt, int IC,
+                     int H, int W, int TW, int TH, int B, long long ldt, long long pstride,
+                     long long bstride) {
+    const int T = TW * TH;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const bool live = i < IC * T;  // every lane takes part in the shuffles
+    const int ii = live ? i : IC * T - 1;
+    const int ic = ii / T, tile = ii - ic * T, b = blockIdx.y;
+    const int ty = tile / TW, tx = tile - ty * TW;
+    const float *xp = x + (long long)b * xbs + (long long)ic * H * W;
+    float d[6][6];
+#pragma unroll
+    for (int a = 0; a < 6; a++) {
+        const int iy = 4 * ty + a - 1;
+        const bool row_in = (unsigned)iy < (unsigned)H;
+        const float *xr = xp + (long long)iy * W + 4 * tx;
+        const float4 v = row_in ? __ldg(reinterpret_cast<const float4 *>(xr))
+                                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const float up = __shfl_up_sync(0xffffffffu, v.w, 1);
+        const float dn = __shfl_down_sync(0xffffffffu, v.x, 1);
+        float left = 0.0f, right = 0.0f;
+        if (tx > 0) left = lane > 0 ? up : (row_in ? __ldg(xr - 1) : 0.0f);
+        if (tx < TW - 1) right = lane < 31 ? dn : (row_in ? __ldg(xr + 4) : 0.0f);
+        d[a][0] = left; d[a][1] = v.x; d[a][2] = v.y; d[a][3] = v.z; d[a][4] = v.w;
+        d[a][5] = right;
+    }
+    if (!live) return;
+    float t1[6][6];
+#pragma unroll
+    for (int u = 0; u < 6; u++)
+#pragma unroll
+        for (int v = 0; v < 6; v++) {
+            float s = 0.0f;
+#pragma unroll
+            for (int a = 0; a < 6; a++) s = fmaf(c_wgB[u * 6 + a], d[a][v], s);
+            t1[u][v] = s;
+        }
+    float *o = dt + b * bstride + ic * ldt + tile;
+#pragma unroll
+    for (int u = 0; u < 6; u++)
+#pragma unroll
+        for (int w = 0; w < 6; w++) {
+            float s = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 6; c++) s = fmaf(t1[u][c], c_wgB[w * 6 + c], s);
+            o[(long long)(u * 6 + w) * pstride] = s;
+        }
+}
+
 // ---- Winograd output transform ----------------------------------------------
 // (both transforms are held to 64 registers, four 256-thread blocks per SM:
 // their loads are independent and latency-bound, so more warps in flight
@@ -775,8 +834,12 @@ Status launch_wg4_input(const float *x, long long xbs, float *dt, int IC, int H,
     if (ldt < TW * TH) return ERR_SHAPE;
     if (pstride <= 0) pstride = IC * ldt;
     if (bstride <= 0) bstride = 36 * pstride;
-    wg4_input_kernel<<<grid3((long long)TW * TH, IC, B), 256, 0, st>>>(
-        x, xbs, dt, IC, H, W, TW, TH, pad, B, ldt, pstride, bstride);
+    if (pad == 1 && W == 4 * TW && ((uintptr_t)x & 15) == 0 && xbs % 4 == 0)
+        wg4_input_vec_kernel<<<grid3((long long)TW * TH, IC, B), 256, 0, st>>>(
+            x, xbs, dt, IC, H, W, TW, TH, B, ldt, pstride, bstride);
+    else
+        wg4_input_kernel<<<grid3((long long)TW * TH, IC, B), 256, 0, st>>>(
+            x, xbs, dt, IC, H, W, TW, TH, pad, B, ldt, pstride, bstride);
     return cuda_status();
 }
 
