@@ -152,6 +152,20 @@ PPDL_OPS_API int ppdl_conv2d_direct(const float * x, int batch, int IC, int H, i
                                     int OC, int K, int S, int P, int OH, int OW, int act,
                                     float * y, long long y_bs, void * stream);
 
+/* No counterpart in the reference (its attention is ggml_mul_mat(k, q) ->
+   ggml_scale -> ggml_soft_max -> ggml_mul_mat with v, src/ppdoclayout.cpp:
+   572-587): the fused attention core of the forward, per head of 32 dims,
+     o[b][i][h*32 + d] = sum_j softmax_j(scale * q[b][i][h*32 ..] . k[b][j][h*32 ..]) v[b][j][h*32 + d]
+   in FP32 on the CUDA cores.  q, k: rows of ldqk floats (page stride bsqk),
+   v, o: rows of ldvo floats (page stride bsvo); heads * 32 <= ld; pointers
+   16-byte aligned, ld and page strides multiples of 4.  T <= 320 (the
+   decoder's 300 queries) keeps all keys on chip; longer sequences (AIFI's
+   625 tokens) stream 64-key tiles.  Returns PPDL_OK, PPDL_ERR_SHAPE or
+   PPDL_ERR_CUDA. */
+PPDL_OPS_API int ppdl_attention_f32(const float * q, const float * k, const float * v, float * o,
+                                    int batch, int T, int heads, int ldqk, long long bsqk,
+                                    int ldvo, long long bsvo, float scale, void * stream);
+
 /* Floats of b_split that ppdl_conv2d_tf32x3 needs for these sizes (0 for
    non-positive sizes). */
 PPDL_OPS_API long long ppdl_conv2d_tf32x3_workspace(int IC, int OC, int K);

@@ -13,6 +13,7 @@
 #include "../../include/ppdl_ops.h"
 #include "kernels.h"
 #include "conv.h"
+#include "dec.h"
 #include "gemm_tc.h"
 #include "ops_internal.h"
 
@@ -119,6 +120,20 @@ PPDL_OPS_API int ppdl_conv2d_direct(const float *x, int batch, int IC, int H, in
                     OH, OW);
     return to_status(ppdl::launch_conv_direct(x, x_bs, weight, bias, y, y_bs, IC, H, W, OC, K, S,
                                               P, OH, OW, act, batch, (cudaStream_t)stream));
+}
+
+PPDL_OPS_API int ppdl_attention_f32(const float *q, const float *k, const float *v, float *o,
+                                    int batch, int T, int heads, int ldqk, long long bsqk,
+                                    int ldvo, long long bsvo, float scale, void *stream) {
+    g_err[0] = 0;
+    if (!q || !k || !v || !o || batch <= 0 || T <= 0 || heads <= 0)
+        return fail(PPDL_ERR_SHAPE, "attention: bad sizes or null pointer");
+    const ppdl::Status s = ppdl::launch_attention(q, k, v, o, T, heads, ldqk, bsqk, ldvo, bsvo,
+                                                  scale, batch, (cudaStream_t)stream);
+    if (s == ppdl::ERR_SHAPE)
+        return fail(PPDL_ERR_SHAPE, "attention: rows of 32-float heads need 16-byte alignment "
+                                    "and strides that are multiples of 4 floats");
+    return to_status(s);
 }
 
 PPDL_OPS_API long long ppdl_conv2d_tf32x3_workspace(int IC, int OC, int K) {
