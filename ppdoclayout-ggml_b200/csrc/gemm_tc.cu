@@ -1196,7 +1196,24 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     // token-major output: the warp's 32 rows x 16 columns go into
                     // a row-major staging box (lane = row, four 16-byte stores)
                     // and out with one TMA store; the ops pass walks the box
-                    // linearly, so consecutive lanes touch consecutive words
+                    // linearly, so consecutive lanes touch consecutive words:
+                    // element i of the pass (box word i * 32 + lane) is column
+                    // lane % 16 of row 2 i + lane / 16.  Without an activation
+                    // (the decoder's residual linears) the 16 residual loads
+                    // are issued together before the box is touched; with one,
+                    // four at a time in a rolled loop (registers).
+                    constexpr bool kResAhead = ACT == ACT_NONE;
+                    float rres[kResAhead ? 16 : 1];
+                    if (kResAhead && e.res_mode) {
+#pragma unroll
+                        for (int i = 0; i < (kResAhead ? 16 : 1); i++) {
+                            const int n = n0 + c0 + (lane & 15);
+                            const int mr = m0 + quad * 32 + 2 * i + (lane >> 4);
+                            rres[i] = (n < pN && mr < pM)
+                                          ? R[(long long)mr * e.res_ldm + (long long)n * e.res_ldn]
+                                          : 0.0f;
+                        }
+                    }
                     const int b = nbox & 1;
                     if (nbox >= 2) {
                         if (lane == 0) bulk_wait_read_1();
@@ -1209,7 +1226,24 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         row4[q] = make_float4(v[4 * q], v[4 * q + 1],
                                               v[4 * q + 2],
                                               v[4 * q + 3]);
-                    if (ops) {
+                    if (ops && kResAhead) {
+                        __syncwarp();  // the pass reads the other lanes' rows
+                        const int n = n0 + c0 + (lane & 15);
+                        float bb = 0.0f;
+                        if constexpr (kPreOps)
+                            bb = bias_of(c0 + (lane & 15));
+                        else
+                            bb = (e.bias && n < pN) ? __ldg(e.bias + n) : 0.0f;
+#pragma unroll
+                        for (int i = 0; i < (kResAhead ? 16 : 1); i++) {
+                            const int idx = i * 32 + lane;
+                            float x = box[idx];
+                            if (e.alpha != 1.0f) x = x * e.alpha;
+                            if (e.bias) x = x + bb;
+                            if (e.res_mode) x = x + rres[i];
+                            box[idx] = x;
+                        }
+                    } else if (ops) {
                         __syncwarp();  // the pass reads the other lanes' rows
 #pragma unroll 1
                         for (int i0 = 0; i0 < 16; i0 += 4) {
