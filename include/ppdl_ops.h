@@ -249,6 +249,19 @@ PPDL_OPS_API int ppdl_gemm_tf32x3_static(int M, int N, int K, int batch, const f
                                          long long ldc_m, long long ldc_n, long long c_bs,
                                          void * stream);
 
+/* No counterpart in the reference.  ppdl_gemm_tf32x3_presplit for a K-major
+   A (rows of lda floats) and a token-major C [M][N], with K split into
+   `splits` ranges of 32-wide k-blocks: one launch computes every range's
+   totals into ws (splits * M * N floats, 16-byte aligned), a second sums
+   them in range order and applies C = act(total + bias) + res (bias and
+   res may be NULL; res [M][N]; act 0/1/2/3 = none/ReLU/SiLU/GELU) — the
+   forward's path for its long-K linears (K = 2048).  Returns PPDL_OK,
+   PPDL_ERR_SHAPE or PPDL_ERR_CUDA. */
+PPDL_OPS_API int ppdl_gemm_tf32x3_split_k(int M, int N, int K, const float * A, long long lda,
+                                          const float * b_split, const float * bias,
+                                          const float * res, int act, int splits, float * ws,
+                                          float * C, void * stream);
+
 /* Human-readable text of the last error of ppdl_op_launch on this thread. */
 PPDL_OPS_API const char * ppdl_op_last_error(void);
 

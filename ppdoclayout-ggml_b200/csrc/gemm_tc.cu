@@ -122,7 +122,7 @@ static_assert(128 * kRegsConv + 128 * kRegsMma + 256 * kRegsEpi <= kThreads * kL
 
 struct Args {
     int M, N, K, batch, planes, a_mn, bn, stages, m_tiles, n_tiles, tiles;
-    int gather, tma_c, box, rows, rows_offmul, rows_delta;
+    int gather, tma_c, box, rows, rows_offmul, rows_delta, kps;
     long long rows_plane;
     uint32_t stage_bytes, tx_bytes, idesc, staging_off;
     TcGather gg;
@@ -615,6 +615,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int kblocks = (a.K + kBK - 1) / kBK;
+    // k-blocks of the tiles of batch entry z: all of them, or with split K
+    // (a.kps > 0) the range [z kps, z kps + kps) of the entry's split z
+    const int pkps = a.kps;
+    auto kb_first = [&](int z) { return pkps ? z * pkps : 0; };
+    auto kb_count = [&](int z) {
+        return pkps ? (kblocks - z * pkps < pkps ? kblocks - z * pkps : pkps) : kblocks;
+    };
 
     // register split: the converter and producer / MMA warpgroups hand
     // registers to the two epilogue warpgroups, whose 64-float running
@@ -646,7 +653,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const int mt = r / pnt;
                     const int m0 = mt * kBM, n0 = (r - mt * pnt) * pbn;
                     const int pz = z % pplanes;
-                    for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
+                    const int nkb = kb_count(z);
+                    for (int kb = 0; kb < nkb; kb++, it++, rs.next()) {
                         const int s = rs.i;
                         bool good = true;
                         if (lane == 0) {
@@ -659,7 +667,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         }
                         const uint32_t st = stage0 + s * pstage;
                         const uint32_t fb = bar_full + 8 * s;
-                        const int k0 = kb * kBK;
+                        const int k0 = (kb_first(z) + kb) * kBK;
                         if (lane < 4) {
                             const long long xr = (long long)lane * rplane + m0 + rdelta;
                             tma_load_3d(st + (uint32_t)(lane * kRowsQBytes), &tmA, fb,
@@ -700,8 +708,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         oy0 = ty * 4;
                         ox0 = (mt - ty * a.cb.tiles_x) * 32;
                     }
-                    for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
-                        const int k0 = kb * kBK;
+                    // split K: every split reads the one A (batch entry 0) and
+                    // B plane 0 at its own k range
+                    const int nkb = kb_count(z), kbz = kb_first(z), az = pkps ? 0 : z;
+                    const int bz = pkps ? 0 : pz;
+                    for (int kb = 0; kb < nkb; kb++, it++, rs.next()) {
+                        const int k0 = (kbz + kb) * kBK;
                         if (pbox && j == 0) {
                             if (!mbar_wait(bar_bempty + 8 * rb.i, rb.ph ^ 1, abort_flag)) {
                                 ok = false;
@@ -732,13 +744,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         if (pgather || pbox) {
                             // A is written by the converter warps / comes from a window
                         } else if (pamn) {
-                            tma_load_3d(st, &tmA, fb, m0, k0, z);
+                            tma_load_3d(st, &tmA, fb, m0, k0, az);
                         } else {
-                            tma_load_3d(st, &tmA, fb, k0, m0, z);
+                            tma_load_3d(st, &tmA, fb, k0, m0, az);
                         }
                         const uint32_t stb = st + (uint32_t)a.stage_bytes - 2u * 128u * pbn;
-                        tma_load_3d(stb, &tmBhi, fb, k0, n0, pz);
-                        tma_load_3d(stb + pbn * 128, &tmBlo, fb, k0, n0, pz);
+                        tma_load_3d(stb, &tmBhi, fb, k0, n0, bz);
+                        tma_load_3d(stb + pbn * 128, &tmBlo, fb, k0, n0, bz);
                         if (pbox && ++j == a.cb.kbpb) {
                             j = 0;
                             if (++kh == a.cb.KS) {
@@ -780,7 +792,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 Ring rs(S), rp(kSlots), ra(kAStages);
                 bool ok = true;
                 for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
-                    for (int kb = 0; kb < kblocks;
+                    const int nkb = kb_count(t / (pmt * pnt));
+                    for (int kb = 0; kb < nkb;
                          kb++, it++, rs.next(), rp.next(), ra.next()) {
                         if (it % kMmaWarps != q) continue;
                         // the A stage is written only after the stage's TMA landed,
@@ -899,7 +912,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     oy0 = oy * gg.S - gg.P;
                     ox0 = ox * gg.S - gg.P;
                 }
-                for (int kb = 0; kb < kblocks; kb++, it++, rs.next()) {
+                const int nkb = kb_count(z);
+                for (int kb = 0; kb < nkb; kb++, it++, rs.next()) {
                     if (pbox) {
                         if (wj == 0) {
                             bool good = true;
@@ -1013,7 +1027,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const int o = c - c_lo;
                 return __shfl_sync(0xffffffffu, o >= 32 ? bias_hi : bias_lo, o & 31);
             };
-            for (int c = 0; c < kblocks; c++, ctr++, rp.next(), re.next()) {
+            const int nkb = kb_count(z);
+            for (int c = 0; c < nkb; c++, ctr++, rp.next(), re.next()) {
                 const int p = rp.i;
                 if (!mbar_wait(bar_empty + 8 * re.i, re.ph, abort_flag)) {
                     ok = false;
@@ -1572,6 +1587,62 @@ bool tc_gemm_plan(TcGemm *g, int M, int N, int K, int batch, const float *A, int
     return g->ok;
 }
 
+bool tc_gemm_plan_split_k(TcGemm *g, int M, int N, int K, const float *A, int a_mn, long long lda,
+                          const float *Bhi, const float *Blo, const TcEpilogue &epi, int splits,
+                          float *ws) {
+    g->ok = false;
+    const int kbl = (K + kBK - 1) / kBK;
+    if (K % 4 || splits < 2 || !ws || ((uintptr_t)ws & 15) || N % 4) return false;
+    const int kps = (kbl + splits - 1) / splits;
+    splits = (kbl + kps - 1) / kps;
+    if (splits < 2) return false;
+    // the raw totals' epilogue: token-major [splits][M][N]
+    TcEpilogue raw;
+    raw.C = ws; raw.ldc_m = N; raw.ldc_n = 1; raw.c_bs = (long long)M * N;
+    if (!plan_common(g, M, N, K, splits, 1, raw)) return false;
+    g->a_mn = a_mn;
+    g->gather = 0;
+    g->box = 0;
+    g->rows = 0;
+    // every split reads the one A: a map of one batch entry
+    bool ok;
+    if (a_mn)
+        ok = encode3d(&g->tmA, A, (uint64_t)M, (uint64_t)K, 1, (uint64_t)lda * 4, 0, kBM, kBK,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    else
+        ok = encode3d(&g->tmA, A, (uint64_t)K, (uint64_t)M, 1, (uint64_t)lda * 4, 0, 32, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    g->ok = ok && encode_b(g, Bhi, Blo, K);
+    if (!g->ok) return false;
+    encode_c(g);
+    if (g->tma_c != 2) {  // the raw totals leave by TMA stores of token-major boxes
+        g->ok = false;
+        return false;
+    }
+    g->kps = kps;
+    g->ws = ws;
+    g->ws_bs = (long long)M * N;
+    g->epi = epi;  // applied by the reduction
+    return true;
+}
+
+bool tc_gemm_split_k_shape(int M, int N, int K, int splits, int *splits_out, int *kps, int *tiles,
+                           int *bn) {
+    const int kbl = (K + kBK - 1) / kBK;
+    if (K % 4 || splits < 2 || N % 4) return false;
+    const int k = (kbl + splits - 1) / splits;
+    splits = (kbl + k - 1) / k;
+    if (splits < 2) return false;
+    TcGemm h;
+    TcEpilogue raw;
+    if (!plan_common(&h, M, N, K, splits, 1, raw)) return false;
+    *splits_out = splits;
+    *kps = k;
+    *tiles = h.tiles;
+    *bn = h.bn;
+    return true;
+}
+
 bool tc_gemm_plan_gather(TcGemm *g, int M, int N, int K, int batch, const TcGather &gg,
                          const float *Bhi, const float *Blo, const TcEpilogue &epi) {
     g->ok = false;
@@ -1717,6 +1788,29 @@ bool tc_gemm_set_bits_output(TcGemm *g, uint32_t *bits, long long words_per_n, l
     return true;
 }
 
+namespace {
+// Split-K reduction: out(m, n) = epilogue(sum over splits in order of
+// ws[z][m][n]) with the ops in the tensor-core epilogue's order (alpha,
+// + bias, + residual mode 1, activation, + residual mode 2).
+__global__ void splitk_reduce_kernel(const float *__restrict__ ws, long long ws_bs, int splits,
+                                     int M, int N, TcEpilogue e) {
+    const long long n_all = (long long)M * N;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n_all;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int m = (int)(i / N), n = (int)(i - (long long)m * N);
+        float x = ws[i];
+        for (int z = 1; z < splits; z++) x = x + ws[z * ws_bs + i];
+        if (e.alpha != 1.0f) x = x * e.alpha;
+        if (e.bias) x = x + __ldg(e.bias + n);
+        const float r = e.res_mode ? e.res[(long long)m * e.res_ldm + (long long)n * e.res_ldn] : 0.0f;
+        if (e.res_mode == 1) x = x + r;
+        x = act_apply(x, e.act);
+        if (e.res_mode == 2) x = x + r;
+        e.C[(long long)m * e.ldc_m + (long long)n * e.ldc_n] = x;
+    }
+}
+}  // namespace
+
 Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     if (!g.ok || g.epi.act < 0 || g.epi.act > 3) return ERR_SHAPE;
     // per device, once: the kernels' register count is checked and their
@@ -1765,6 +1859,13 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     a.rows_plane = g.rows_plane;
     a.rows_offmul = (int)(g.rows_plane & 3);
     a.rows_delta = g.rows_delta;
+    a.kps = g.kps;
+    const int splits = g.kps ? ((g.K + kBK - 1) / kBK + g.kps - 1) / g.kps : 1;
+    if (g.kps) {
+        // all splits run as batch entries; the raw totals go to the workspace
+        a.batch = splits;
+        a.tiles = g.m_tiles * g.n_tiles * splits;
+    }
     const uint32_t b_bytes = 2u * 128u * (uint32_t)g.bn;
     if (g.box) {
         a.stage_bytes = b_bytes;
@@ -1783,9 +1884,26 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     a.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(g.bn >> 3) << 17) |
               ((uint32_t)(kBM >> 4) << 24);
     a.epi = g.epi;
+    if (g.kps) {
+        TcEpilogue raw;
+        raw.C = g.ws; raw.ldc_m = g.N; raw.ldc_n = 1; raw.c_bs = g.ws_bs;
+        a.epi = raw;
+    }
     int grid = sm_count();
     if (g.max_ctas > 0 && grid > g.max_ctas) grid = g.max_ctas;
-    if (grid > g.tiles) grid = g.tiles;
+    if (grid > a.tiles) grid = a.tiles;
+    if (g.kps) {
+        if (g.gather || g.box || g.rows || g.bits || g.batch < 1) return ERR_SHAPE;
+        tc_gemm_kernel<ACT_NONE, kModeTile><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi,
+                                                                           g.tmBlo, g.tmC, a);
+        const Status s0 = cuda_status();
+        if (s0 != OK) return s0;
+        const long long n_all = (long long)g.M * g.N;
+        int rb = (int)((n_all + 255) / 256);
+        if (rb > 8 * sm_count()) rb = 8 * sm_count();
+        splitk_reduce_kernel<<<rb, 256, 0, st>>>(g.ws, g.ws_bs, splits, g.M, g.N, g.epi);
+        return cuda_status();
+    }
     if (g.bits) {
         // packed output: tile A, no epilogue ops (checked by the planner)
         tc_gemm_kernel<ACT_NONE, kModeBits><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi,

@@ -99,9 +99,28 @@ struct TcGemm {
     size_t smem = 0;
     int m_tiles = 0, n_tiles = 0, tiles = 0;
     int max_ctas = 0;    // > 0: at most this many CTAs (SMs left to concurrent launches)
-    TcEpilogue epi;
+    int kps = 0;         // > 0: split K, this many k-blocks per split (tc_gemm_set_split_k)
+    TcEpilogue epi;      // with split K: the reduction's ops (the GEMM writes raw totals)
+    float *ws = nullptr;  // split K: the splits' totals [splits][M][N]
+    long long ws_bs = 0;  // split K: floats between two splits' totals
     bool ok = false;
 };
+
+// Plan a GEMM as tc_gemm_plan (batch 1, one B plane) with K split into
+// `splits` ranges of k-blocks: the tiles of all ranges run as one launch and
+// write their raw FP32 totals to ws [splits][M][N] (token-major, 16-byte
+// aligned, splits * M * N floats); launch_tc_gemm then sums them in split
+// order and applies epi (alpha, bias, residual, activation) in a second
+// kernel.  For GEMMs with few output tiles and a long K (the decoder's
+// 2048 -> 256 linear).  False when the form does not apply.
+bool tc_gemm_plan_split_k(TcGemm *g, int M, int N, int K, const float *A, int a_mn, long long lda,
+                          const float *Bhi, const float *Blo, const TcEpilogue &epi, int splits,
+                          float *ws);
+
+// The tile shape tc_gemm_plan_split_k would choose (no tensor maps encoded):
+// splits after rounding, k-blocks per split, tiles of the launch, N tile.
+bool tc_gemm_split_k_shape(int M, int N, int K, int splits, int *splits_out, int *kps, int *tiles,
+                           int *bn);
 
 // Pre-split a K-major weight [rows][K] into hi (low 13 mantissa bits
 // cleared) and lo = w - hi.

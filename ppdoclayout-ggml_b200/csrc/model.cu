@@ -676,6 +676,21 @@ public:
             auto g = std::make_shared<TcGemm>();
             if (ok && tc_gemm_plan(g.get(), Bmax * x.T, out, in, 1, x.p, 0, in, 0, wsp.hi, wsp.lo, 1,
                                    e)) {
+                // a long K (the decoder's 2048 -> 256 linear: 64 k-blocks per
+                // tile over 114 tiles) splits into ranges of about 24
+                // k-blocks.  The split depends on K only, so every batch
+                // capacity sums each output in the same order.
+                const int kbl = (in + 31) / 32;
+                if (max_ctas == 0 && kbl >= 48) {
+                    int sp = (kbl + 23) / 24;
+                    if (sp > 8) sp = 8;
+                    float *ws = dalloc((long long)sp * Bmax * x.T * out);
+                    auto h = std::make_shared<TcGemm>();
+                    if (ok && ws &&
+                        tc_gemm_plan_split_k(h.get(), Bmax * x.T, out, in, x.p, 0, in, wsp.hi,
+                                             wsp.lo, e, sp, ws))
+                        g = h;
+                }
                 g->max_ctas = max_ctas;
                 const int T = x.T;
                 push(name, PPDL_STEP_GEMM_LINEAR, 2.0 * x.T * out * in,

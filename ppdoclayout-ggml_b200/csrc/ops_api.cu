@@ -286,6 +286,27 @@ PPDL_OPS_API int ppdl_gemm_tf32x3_presplit(int M, int N, int K, int batch, const
     return to_status(ppdl::launch_tc_gemm(g, st));
 }
 
+PPDL_OPS_API int ppdl_gemm_tf32x3_split_k(int M, int N, int K, const float *A, long long lda,
+                                          const float *b_split, const float *bias,
+                                          const float *res, int act, int splits, float *ws,
+                                          float *C, void *stream) {
+    g_err[0] = 0;
+    if (M <= 0 || N <= 0 || K <= 0 || !A || !b_split || !ws || !C || act < 0 || act > 3)
+        return fail(PPDL_ERR_SHAPE, "gemm split-K: bad sizes, activation or null pointer");
+    ppdl::TcEpilogue e;
+    e.C = C; e.ldc_m = N; e.ldc_n = 1;
+    e.bias = bias; e.act = act;
+    if (res) {
+        e.res = res; e.res_ldm = N; e.res_ldn = 1; e.res_mode = 2;
+    }
+    ppdl::TcGemm g;
+    if (!ppdl::tc_gemm_plan_split_k(&g, M, N, K, A, 0, lda, b_split, b_split + (long long)N * K, e,
+                                    splits, ws))
+        return fail(PPDL_ERR_SHAPE, "gemm split-K: K and N multiples of 4, lda too, 16-byte "
+                                    "aligned operands, at least two splits of 32-wide k-blocks");
+    return to_status(ppdl::launch_tc_gemm(g, (cudaStream_t)stream));
+}
+
 PPDL_OPS_API int ppdl_op_launch(const ppdl_op_desc *d, void *stream_ptr) {
     g_err[0] = 0;
     if (!d) return fail(PPDL_ERR_SHAPE, "null descriptor");

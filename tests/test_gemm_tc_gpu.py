@@ -145,3 +145,53 @@ def test_presplit_gemm_matches_one_call(cuda):
                                        c2.data_ptr(), 1, M, N * M, s) == ppdl.PPDL_OK
     torch.cuda.synchronize()
     assert torch.equal(c1, c2)
+
+
+@pytest.mark.parametrize("M,N,K,splits,act,use_res", [(2400, 256, 2048, 3, 0, True),
+                                                      (300, 256, 2048, 3, 0, True),
+                                                      (517, 96, 1000, 4, 1, False),
+                                                      (130, 40, 64, 2, 2, True)])
+def test_split_k_matches_float64(cuda, M, N, K, splits, act, use_res):
+    """ppdl_gemm_tf32x3_split_k (the forward's path for the decoder's
+    2048 -> 256 linear): K in `splits` ranges summed in order, then bias,
+    activation and residual; against float64, and the same per-row result
+    at 2400 and 300 rows (the split depends on K only)."""
+    import ctypes as C
+    L = ppdl.lib()
+    L.ppdl_tf32_split.argtypes = [C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]
+    L.ppdl_gemm_tf32x3_split_k.argtypes = ([C.c_int] * 3 + [C.c_void_p, C.c_longlong]
+                                           + [C.c_void_p] * 3 + [C.c_int, C.c_int]
+                                           + [C.c_void_p] * 3)
+    g = torch.Generator(device=cuda).manual_seed(M + K)
+    A = torch.randn((M, K), generator=g, device=cuda)
+    W = torch.randn((N, K), generator=g, device=cuda) / K ** 0.5
+    b = torch.randn((N,), generator=g, device=cuda) * 0.1
+    R = torch.randn((M, N), generator=g, device=cuda) if use_res else None
+    ws = torch.empty(2 * N * K, device=cuda)
+    work = torch.empty(splits * M * N, device=cuda)
+    out = torch.full((M, N), float("nan"), device=cuda)
+    s = torch.cuda.current_stream().cuda_stream
+    assert L.ppdl_tf32_split(W.data_ptr(), N * K, ws.data_ptr(), s) == 0
+    st = L.ppdl_gemm_tf32x3_split_k(M, N, K, A.data_ptr(), K, ws.data_ptr(), b.data_ptr(),
+                                    R.data_ptr() if use_res else None, act, splits,
+                                    work.data_ptr(), out.data_ptr(), s)
+    assert st == ppdl.PPDL_OK, ppdl.last_error()
+    torch.cuda.synchronize()
+    ref = A.double() @ W.double().T + b.double()
+    if act == 1:
+        ref = torch.relu(ref)
+    elif act == 2:
+        ref = ref * torch.sigmoid(ref)
+    if use_res:
+        ref = ref + R.double()
+    err = float((out.double() - ref).abs().max() / ref.abs().max())
+    assert err < 1e-6, err
+    if M == 2400:
+        # the first 300 rows alone give the same bits
+        out2 = torch.empty((300, N), device=cuda)
+        work2 = torch.empty(splits * 300 * N, device=cuda)
+        assert L.ppdl_gemm_tf32x3_split_k(300, N, K, A.data_ptr(), K, ws.data_ptr(), b.data_ptr(),
+                                          R.data_ptr() if use_res else None, act, splits,
+                                          work2.data_ptr(), out2.data_ptr(), s) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(out2, out[:300])
