@@ -1260,20 +1260,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         }
                     } else if (ops) {
                         __syncwarp();  // the pass reads the other lanes' rows
+                        // a lane's elements share one column: one bias for all
+                        const int n = n0 + c0 + (lane & 15);
+                        float bb = 0.0f;
+                        if constexpr (kPreOps)
+                            bb = bias_of(c0 + (lane & 15));
+                        else
+                            bb = (e.bias && n < pN) ? __ldg(e.bias + n) : 0.0f;
 #pragma unroll 1
                         for (int i0 = 0; i0 < 16; i0 += 4) {
-                            float bb[4], rr[4];
+                            float rr[4];
 #pragma unroll
                             for (int u = 0; u < 4; u++) {
-                                const int idx = (i0 + u) * 32 + lane;
-                                const int n = n0 + c0 + (idx & 15);
-                                const int mr = m0 + quad * 32 + (idx >> 4);
-                                const bool okk = n < pN && mr < pM;
-                                if constexpr (kPreOps)
-                                    bb[u] = bias_of(c0 + (idx & 15));
-                                else
-                                    bb[u] = (e.bias && okk) ? __ldg(e.bias + n) : 0.0f;
-                                rr[u] = (e.res_mode && okk)
+                                const int mr = m0 + quad * 32 + 2 * (i0 + u) + (lane >> 4);
+                                rr[u] = (e.res_mode && n < pN && mr < pM)
                                             ? R[(long long)mr * e.res_ldm + (long long)n * e.res_ldn]
                                             : 0.0f;
                             }
@@ -1282,7 +1282,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                 const int idx = (i0 + u) * 32 + lane;
                                 float x = box[idx];
                                 if (e.alpha != 1.0f) x = x * e.alpha;
-                                if (e.bias) x = x + bb[u];
+                                if (e.bias) x = x + bb;
                                 if (e.res_mode == 1) x = x + rr[u];
                                 x = act_apply(x, ACT);
                                 if (e.res_mode == 2) x = x + rr[u];
