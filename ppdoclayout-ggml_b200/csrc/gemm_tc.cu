@@ -792,7 +792,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 Ring rs(S), rp(kSlots), ra(kAStages);
                 bool ok = true;
                 for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
-                    const int nkb = kb_count(t / (pmt * pnt));
+                    const int nkb = pkps ? kb_count(t / (pmt * pnt)) : kblocks;
                     for (int kb = 0; kb < nkb;
                          kb++, it++, rs.next(), rp.next(), ra.next()) {
                         if (it % kMmaWarps != q) continue;
