@@ -213,18 +213,9 @@ Status launch_attention(const float *q, const float *k, const float *v, float *o
         return ERR_SHAPE;
     const size_t smem = attention_smem_bytes(T);
     if (smem > 227 * 1024) return ERR_SHAPE;
-    static bool attr[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr[dev]) {
-        if (cudaFuncSetAttribute(attn_kernel<kKTAll, 1>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 227 * 1024) != cudaSuccess ||
-            cudaFuncSetAttribute(attn_kernel<64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 227 * 1024) != cudaSuccess)
-            return ERR_CUDA;
-        attr[dev] = true;
-    }
+    if (!smem_attr_once((const void *)attn_kernel<kKTAll, 1>, 227 * 1024) ||
+        !smem_attr_once((const void *)attn_kernel<64, 2>, 227 * 1024))
+        return ERR_CUDA;
     const int ldS = attention_lds(T);
     const dim3 grid((T + kBQ - 1) / kBQ, heads, B);
     if (T <= kKTAll)

@@ -4,6 +4,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 namespace ppdl {
 
 // Model constants (reference src/ppdoclayout.cpp:31-44).
@@ -58,6 +62,23 @@ __device__ __forceinline__ float act_apply(float v, int act) {
 
 // Status returned by the internal launchers.
 enum Status : int { OK = 0, ERR_UNSUPPORTED = 1, ERR_SHAPE = 2, ERR_CUDA = 3 };
+
+// Raise kernel fn's dynamic shared-memory limit to `bytes` on the current
+// device, once per process, kernel and device (host threads may make their
+// first launches together, so the record is kept under a mutex).
+inline bool smem_attr_once(const void *fn, int bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<const void *, int>> done;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count({fn, dev})) return true;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+        cudaSuccess)
+        return false;
+    done.insert({fn, dev});
+    return true;
+}
 
 inline Status cuda_status() {
     return cudaGetLastError() == cudaSuccess ? OK : ERR_CUDA;

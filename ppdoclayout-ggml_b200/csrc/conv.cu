@@ -911,19 +911,12 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
             const int passes = (items + 255) / 256;
             int nthr = ((items + passes - 1) / passes + 31) / 32 * 32;
             if (nthr < 128) nthr = 128;
-            int dev = 0;
-            cudaGetDevice(&dev);
             const int af = act == ACT_NONE ? 0 : act == ACT_RELU ? 1 : 2;
 #define PPDL_DW_PLANE(KK, SS, AA)                                                                 \
     do {                                                                                         \
-        static bool attr[64] = {false};                                                          \
-        if (dev >= 64 || !attr[dev]) {                                                           \
-            if (cudaFuncSetAttribute(dwconv_plane_kernel<KK, SS, AA>,                            \
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,                \
-                                     (int)kDwPlaneSmemMax) != cudaSuccess)                       \
-                return ERR_CUDA;                                                                 \
-            if (dev < 64) attr[dev] = true;                                                      \
-        }                                                                                        \
+        if (!smem_attr_once((const void *)dwconv_plane_kernel<KK, SS, AA>,                    \
+                            (int)kDwPlaneSmemMax))                                       \
+            return ERR_CUDA;                                                                 \
         dwconv_plane_kernel<KK, SS, AA><<<g, nthr, sm, st>>>(                                    \
             x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, ld, HPp, GX, GY, pairs, even);        \
     } while (0)
@@ -971,18 +964,10 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
         const int items = ((BR + 3) / 4) * OW;
         const int passes = (items + 255) / 256;
         const int nthr = ((items + passes - 1) / passes + 31) / 32 * 32;
-        int dev = 0;
-        cudaGetDevice(&dev);
 #define PPDL_DW_BAND(KK, SS)                                                                      \
     do {                                                                                         \
-        static bool attr[64] = {false};                                                          \
-        if (dev >= 64 || !attr[dev]) {                                                           \
-            if (cudaFuncSetAttribute(dwconv_band_kernel<KK, SS>,                                 \
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,                \
-                                     (int)kDwBandSmem) != cudaSuccess)                           \
-                return ERR_CUDA;                                                                 \
-            if (dev < 64) attr[dev] = true;                                                      \
-        }                                                                                        \
+        if (!smem_attr_once((const void *)dwconv_band_kernel<KK, SS>, (int)kDwBandSmem))     \
+            return ERR_CUDA;                                                                 \
         dwconv_band_kernel<KK, SS><<<(unsigned)nblk, nthr, smem, st>>>(                          \
             x, xbs, w, bias, y, ybs, C, H, W, OH, OW, P, act, bld, bcols, BR, nbands);             \
     } while (0)
@@ -1038,18 +1023,10 @@ Status launch_conv_direct(const float *x, long long xbs, const float *w, const f
     const int smem = 4 * (IC * K * K * kDirectOCB + ICB * IH * IWP);
     const dim3 g((unsigned)(tiles_x * tiles_y), (unsigned)((OC + kDirectOCB - 1) / kDirectOCB),
                  (unsigned)B);
-    int dev = 0;
-    cudaGetDevice(&dev);
 #define PPDL_DIRECT(KK, SS)                                                                       \
     do {                                                                                         \
-        static bool attr[64] = {false};                                                          \
-        if (dev >= 64 || !attr[dev]) {                                                           \
-            if (cudaFuncSetAttribute(conv_direct_kernel<KK, SS>,                                 \
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,                \
-                                     64 * 1024) != cudaSuccess)                                  \
-                return ERR_CUDA;                                                                 \
-            if (dev < 64) attr[dev] = true;                                                      \
-        }                                                                                        \
+        if (!smem_attr_once((const void *)conv_direct_kernel<KK, SS>, 64 * 1024))            \
+            return ERR_CUDA;                                                                 \
         conv_direct_kernel<KK, SS><<<g, 256, smem, st>>>(x, xbs, w, bias, y, ybs, IC, H, W, OC,  \
                                                         OH, OW, P, act, tiles_x, ICB);           \
     } while (0)

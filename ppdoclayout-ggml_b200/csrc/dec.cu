@@ -450,16 +450,8 @@ Status launch_postprocess(const float *logits, const float *boxes, const float *
                           const float *mask_logits, const uint32_t *mask_bits_q,
                           const int32_t *ori_hw, int32_t *rank, float *dets, int32_t *sel,
                           int32_t *masks, uint32_t *mask_bits, int B, cudaStream_t st) {
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
     const int smem = kNQ * kNC * (int)sizeof(unsigned long long);
-    if (dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(pp_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 smem) != cudaSuccess)
-            return ERR_CUDA;
-        attr_set[dev] = true;
-    }
+    if (!smem_attr_once((const void *)pp_select_kernel, smem)) return ERR_CUDA;
     float *votes = reinterpret_cast<float *>(rank);  // the 300 votes of each page
     pp_votes_kernel<<<dim3(cdiv(kNQ, kVoteJ), B), 256, 0, st>>>(order, votes);
     pp_select_kernel<<<B, 1024, smem, st>>>(logits, boxes, votes, ori_hw, dets, sel);

@@ -115,17 +115,9 @@ Status launch_topk(const float *lg, int32_t *out, int ntok, int nc, int nq, int 
     while (n2 < ntok) n2 <<= 1;
     if (n2 < 2) n2 = 2;
     const size_t smem = (size_t)n2 * sizeof(unsigned long long);
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kMaxKeys * (int)sizeof(unsigned long long)) != cudaSuccess ||
-            cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kSelSmemMax) != cudaSuccess)
-            return ERR_CUDA;
-        attr_set[dev] = true;
-    }
+    if (!smem_attr_once((const void *)topk_kernel, kMaxKeys * (int)sizeof(unsigned long long)) ||
+        !smem_attr_once((const void *)topk_select_kernel, (int)kSelSmemMax))
+        return ERR_CUDA;
     const size_t sel_smem = (size_t)ntok * sizeof(unsigned long long) + (size_t)kChunk * nc * 4;
     if (nq <= kSelectMax && sel_smem <= kSelSmemMax)
         topk_select_kernel<<<batch, kThreads, sel_smem, stream>>>(lg, out, ntok, nc, nq);
