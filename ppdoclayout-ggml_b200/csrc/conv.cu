@@ -167,6 +167,24 @@ wg4_input_vec_kernel(const float *__restrict__ x, long long xbs, float *__restri
         }
 }
 
+// ---- RepVGG branch folding ---------------------------------------------------
+// The reference's RepVGG block (src/ppdoclayout.cpp:656-661) adds a 3x3 conv
+// (w3 [OC][IC][3][3], b3) and a 1x1 conv (w1 [OC][IC], b1) of the same input.
+// One 3x3 conv with wm = w3 plus w1 on the centre tap and bm = b3 + b1 is the
+// same map in real arithmetic; the forward runs that conv (one Winograd conv
+// instead of a 1x1 GEMM, a Winograd conv and a residual read).
+__global__ void rep_fold_kernel(const float *__restrict__ w3, const float *__restrict__ b3,
+                                const float *__restrict__ w1, const float *__restrict__ b1,
+                                float *__restrict__ wm, float *__restrict__ bm, int IC, int OC) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i < 9LL * IC * OC) {
+        float v = w3[i];
+        if (i % 9 == 4) v = __fadd_rn(v, w1[i / 9]);
+        wm[i] = v;
+    }
+    if (i < OC) bm[i] = __fadd_rn(b3[i], b1[i]);
+}
+
 // ---- Winograd output transform ----------------------------------------------
 // (both transforms are held to 64 registers, four 256-thread blocks per SM:
 // their loads are independent and latency-bound, so more warps in flight
@@ -861,6 +879,14 @@ Status launch_wg4_output(const float *yt, const float *bias, float *y, long long
 Status launch_wg4_filter(const float *w, float *wg4, int IC, int OC, cudaStream_t st) {
     const long long n = 36LL * IC * OC;
     wg4_filter_kernel<<<blocks(n), 256, 0, st>>>(w, wg4, IC, OC);
+    return cuda_status();
+}
+
+Status launch_rep_fold(const float *w3, const float *b3, const float *w1, const float *b1,
+                       float *wm, float *bm, int IC, int OC, cudaStream_t st) {
+    if (IC <= 0 || OC <= 0) return ERR_SHAPE;
+    const long long n = 9LL * IC * OC;
+    rep_fold_kernel<<<blocks(n), 256, 0, st>>>(w3, b3, w1, b1, wm, bm, IC, OC);
     return cuda_status();
 }
 

@@ -33,6 +33,11 @@ Status launch_wg4_kmajor_split(const float *wg4, float *hi, float *lo, int IC, i
 Status launch_kmajor_split(const float *src, float *hi, float *lo, int planes, int IC, int ld,
                            long long pstride, int nc, cudaStream_t st);
 
+// RepVGG fold: wm = w3 [OC][IC][3][3] with w1 [OC][IC] added to the centre
+// tap, bm = b3 + b1 (wm: 9 IC OC floats, bm: OC floats)
+Status launch_rep_fold(const float *w3, const float *b3, const float *w1, const float *b1,
+                       float *wm, float *bm, int IC, int OC, cudaStream_t st);
+
 // w [OC][IC][3][3] -> wg4 [36][IC][OC] (G g G^T with the reference's G)
 Status launch_wg4_filter(const float *w, float *wg4, int IC, int OC, cudaStream_t st);
 

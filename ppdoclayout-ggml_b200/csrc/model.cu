@@ -396,8 +396,10 @@ public:
     // y = act(conv(x) + bias (+ res if res_mode == 1)) (+ res if res_mode == 2)
     // p_hi < 0: symmetric padding p; otherwise bottom/right padding p_hi
     // (the stem's ggml_pad, :621-624).
+    // w_fold / b_fold: weights to use instead of the named ones (same shapes)
     void conv(const V &x, const V &y, const std::string &name, int s, int p, int act,
-              const V &res = V(), int res_mode = 0, int p_hi = -1) {
+              const V &res = V(), int res_mode = 0, int p_hi = -1,
+              const float *w_fold = nullptr, const float *b_fold = nullptr) {
         const WT &wt = W(name + ".weight");
         const WT &bt = W(name + ".bias");
         if (!ok) return;
@@ -410,7 +412,7 @@ public:
             fail("conv " + name + ": shape mismatch");
             return;
         }
-        const float *wp = wt.p, *bp = bt.p;
+        const float *wp = w_fold ? w_fold : wt.p, *bp = b_fold ? b_fold : bt.p;
         if (dw) {
             if (res_mode || p_hi >= 0) {
                 fail("conv " + name + ": depthwise form not supported");
@@ -800,13 +802,33 @@ public:
         conv(agg0, out, pfx + ".agg1", 1, 0, ACT_RELU, res, res_mode);
     }
 
+    // RepVGG block (src/ppdoclayout.cpp:656-661): silu(c1(x) + c2(x)), c1 3x3
+    // and c2 1x1, run as one 3x3 conv with c2 folded into c1's centre tap
+    // (launch_rep_fold, at load)
+    void repvgg(const V &x, const V &y, const std::string &pfx) {
+        const WT &w3 = W(pfx + ".c1.weight"), &b3 = W(pfx + ".c1.bias");
+        const WT &w1 = W(pfx + ".c2.weight"), &b1 = W(pfx + ".c2.bias");
+        if (!ok) return;
+        const int IC = (int)w3.ne[2], OC = (int)w3.ne[3];
+        if (w3.ne[0] != 3 || w3.ne[1] != 3 || w1.ne[0] != 1 || w1.ne[1] != 1 ||
+            w1.ne[2] != IC || w1.ne[3] != OC || b3.ne[0] != OC || b1.ne[0] != OC) {
+            fail("repvgg " + pfx + ": shape mismatch");
+            return;
+        }
+        float *wm = dalloc(9LL * IC * OC), *bm = dalloc(OC);
+        if (!ok) return;
+        if (launch_rep_fold(w3.p, b3.p, w1.p, b1.p, wm, bm, IC, OC, st) != OK) {
+            fail("repvgg " + pfx + ": fold launch failed");
+            return;
+        }
+        conv(x, y, pfx + ".c1", 1, 1, ACT_SILU, V(), 0, -1, wm, bm);
+    }
+
     void csp(const V &x, const V &out, const std::string &pfx) {
-        V a = tensor(256, x.H, x.W), b = tensor(256, x.H, x.W), t = tensor(256, x.H, x.W);
+        V a = tensor(256, x.H, x.W), b = tensor(256, x.H, x.W);
         conv(x, a, pfx + ".c1", 1, 0, ACT_SILU);
         for (int i = 0; i < 3; i++) {
-            const std::string bp = pfx + ".bn" + std::to_string(i);
-            conv(a, t, bp + ".c2", 1, 0, ACT_NONE);
-            conv(a, b, bp + ".c1", 1, 1, ACT_SILU, t, 1);  // silu(c1(x) + c2(x))
+            repvgg(a, b, pfx + ".bn" + std::to_string(i));
             std::swap(a, b);
         }
         conv(x, out, pfx + ".c2", 1, 0, ACT_SILU, a, 2);  // a + c2(x)
