@@ -63,6 +63,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
             float *__restrict__ o, int T, int ldqk, long long bsqk, int ldvo, long long bsvo,
             float scale, int ldS) {
+    pdl_begin();
     static_assert(kKT % 64 == 0, "the score loop walks 64-key slices of a tile");
     extern __shared__ float sm[];
     float *Qs = sm;                      // [kBQ][kLD]
@@ -219,10 +220,10 @@ Status launch_attention(const float *q, const float *k, const float *v, float *o
     const int ldS = attention_lds(T);
     const dim3 grid((T + kBQ - 1) / kBQ, heads, B);
     if (T <= kKTAll)
-        attn_kernel<kKTAll, 1><<<grid, kThreads, smem, st>>>(q, k, v, o, T, ldqk, bsqk, ldvo, bsvo,
+        pdl_launch(attn_kernel<kKTAll, 1>, grid, kThreads, smem, st, q, k, v, o, T, ldqk, bsqk, ldvo, bsvo,
                                                              scale, ldS);
     else
-        attn_kernel<64, 2><<<grid, kThreads, smem, st>>>(q, k, v, o, T, ldqk, bsqk, ldvo, bsvo,
+        pdl_launch(attn_kernel<64, 2>, grid, kThreads, smem, st, q, k, v, o, T, ldqk, bsqk, ldvo, bsvo,
                                                          scale, ldS);
     return cuda_status();
 }

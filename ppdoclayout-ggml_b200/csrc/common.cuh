@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -78,6 +79,48 @@ inline bool smem_attr_once(const void *fn, int bytes) {
         return false;
     done.insert({fn, dev});
     return true;
+}
+
+// ---- programmatic dependent launch -------------------------------------------
+// Every kernel of the library starts with pdl_begin(): it waits until the
+// grids it depends on in its stream have completed and their writes are
+// visible (at once for a launch without the attribute).  Launched through
+// pdl_launch, a kernel's launch and its blocks' set-up overlap the end of the
+// previous kernel, while all of its global-memory reads and writes follow the
+// wait.  No kernel signals its dependents early (griddepcontrol.
+// launch_dependents): the next grid launches as the blocks exit; an early
+// signal at block start measured slower in the forward (dependent blocks
+// holding SMs while they wait).
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// PPDL_PDL=0 in the environment launches without the attribute
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("PPDL_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// kernel<<<g, b, smem, st>>>(args...) with programmatic stream
+// serialization allowed; errors surface through cudaGetLastError as for the
+// triple-chevron launch
+template <typename... KArgs, typename... Args>
+inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 g, dim3 b, size_t smem,
+                              cudaStream_t st, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = g;
+    cfg.blockDim = b;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 inline Status cuda_status() {

@@ -68,6 +68,7 @@ __global__ void __launch_bounds__(256, 4)
 wg4_input_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ dt, int IC,
                  int H, int W, int TW, int TH, int pad, int B, long long ldt, long long pstride,
                  long long bstride) {
+    pdl_begin();
     // grid (IC*T / 256, B): one 32-bit division per thread
     const int T = TW * TH;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -120,6 +121,7 @@ __global__ void __launch_bounds__(256, 4)
 wg4_input_vec_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ dt, int IC,
                      int H, int W, int TW, int TH, int B, long long ldt, long long pstride,
                      long long bstride) {
+    pdl_begin();
     const int T = TW * TH;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & 31;
@@ -176,6 +178,7 @@ wg4_input_vec_kernel(const float *__restrict__ x, long long xbs, float *__restri
 __global__ void rep_fold_kernel(const float *__restrict__ w3, const float *__restrict__ b3,
                                 const float *__restrict__ w1, const float *__restrict__ b1,
                                 float *__restrict__ wm, float *__restrict__ bm, int IC, int OC) {
+    pdl_begin();
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (i < 9LL * IC * OC) {
         float v = w3[i];
@@ -194,6 +197,7 @@ wg4_output_kernel(const float *__restrict__ yt, const float *__restrict__ bias,
                   float *__restrict__ y, long long ybs, const float *__restrict__ res,
                   long long rbs, int res_mode, int OC, int OH, int OW, int TW, int TH, int act,
                   int B, long long ldt, long long pstride, long long bstride) {
+    pdl_begin();
     // grid (OC*T / 256, B); yt addressed as dt of the input transform
     const int T = TW * TH;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -258,6 +262,7 @@ wg4_output_kernel(const float *__restrict__ yt, const float *__restrict__ bias,
 // order of src/ppdoclayout.cpp:321-333.
 __global__ void wg4_filter_kernel(const float *__restrict__ w, float *__restrict__ wg4, int IC,
                                   int OC) {
+    pdl_begin();
     const long long n = 36LL * IC * OC;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
@@ -282,6 +287,7 @@ __global__ void wg4_filter_kernel(const float *__restrict__ w, float *__restrict
 __global__ void kmajor_split_kernel(const float *__restrict__ src, float *__restrict__ hi,
                                     float *__restrict__ lo, int planes, int IC, int ld,
                                     long long pstride, int nc) {
+    pdl_begin();
     const long long n = (long long)planes * IC * nc;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
@@ -325,6 +331,7 @@ __global__ void __launch_bounds__(256)
 dwconv_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
               const float *__restrict__ bias, float *__restrict__ y, long long ybs, int H, int W,
               int OH, int OW, int P, int act, int tiles_x) {
+    pdl_begin();
     constexpr int IW = (kDwTW - 1) * S + K, IH = (kDwTH - 1) * S + K;
     constexpr int LD = (IW + 30) / 32 * 32 + 1;  // >= IW, 1 mod 32
     constexpr int NV = 3 * S + K;                // window columns of 4 outputs
@@ -395,6 +402,7 @@ dwconv_plane_kernel(const float *__restrict__ x, long long xbs, const float *__r
                     const float *__restrict__ bias, float *__restrict__ y, long long ybs, int H,
                     int W, int OH, int OW, int P, int act, int ld, int HPp, int GX, int GY,
                     int pairs, int even) {
+    pdl_begin();
     extern __shared__ float4 plane4[];
     float *plane = reinterpret_cast<float *>(plane4);  // HPp rows of ld floats
     constexpr int NX = 3 * S + K;                      // window rows / columns of a 4 x 4 block
@@ -507,6 +515,7 @@ dwconv_band_kernel(const float *__restrict__ x, long long xbs, const float *__re
                    const float *__restrict__ bias, float *__restrict__ y, long long ybs, int C,
                    int H, int W, int OH, int OW, int P, int act, int ld, int cols, int BR,
                    int nbands) {
+    pdl_begin();
     extern __shared__ float band_rows[];  // ((BR - 1) S + K) rows of ld floats
     constexpr int NV = 3 * S + K;         // input rows of a 4-row output group
     const long long plane = blockIdx.x / nbands;
@@ -588,6 +597,7 @@ __global__ void __launch_bounds__(256)
 conv_direct_kernel(const float *__restrict__ x, long long xbs, const float *__restrict__ w,
                    const float *__restrict__ bias, float *__restrict__ y, long long ybs, int IC,
                    int H, int W, int OC, int OH, int OW, int P, int act, int tiles_x, int ICB) {
+    pdl_begin();
     constexpr int NX = 3 * S + K;        // window values of a thread's 4 pixels per row
     constexpr int N4 = (NX + 3) / 4;     // float4 reads covering them
     constexpr int IH = (kDirectRows - 1) * S + K;
@@ -697,6 +707,7 @@ conv_direct_kernel(const float *__restrict__ x, long long xbs, const float *__re
 // row loads plus the next column, one 16-byte store
 __global__ void maxpool2_pad_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
                                     long long ybs, int C, int H, int W, int B) {
+    pdl_begin();
     // grid (C*H*W / 1024, B)
     const int w4 = W >> 2;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -751,6 +762,7 @@ template <int V>
 __global__ void interp_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
                               long long ybs, const float *__restrict__ base, long long bbs, int C,
                               int H, int W, int OH, int OW, int bilinear, int B) {
+    pdl_begin();
     // grid (C*OH*OW / (256 V), B)
     const int ow = OW / V;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -785,6 +797,7 @@ __global__ void interp_kernel(const float *__restrict__ x, long long xbs, float 
 // ---- CHW <-> token-major ([H*W][C]) through a shared-memory tile ------------
 __global__ void transpose_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
                                  long long ybs, int R, int Cc, long long ldx, long long ldy) {
+    pdl_begin();
     // y[c][r] = x[r][c] for a R x Cc matrix; x row stride ldx, y row stride ldy
     __shared__ float tile[32][33];
     const int b = blockIdx.z;
@@ -808,6 +821,7 @@ __global__ void transpose_kernel(const float *__restrict__ x, long long xbs, flo
 // Each thread writes four floats with one 16-byte store.
 __global__ void pad_rows_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
                                 long long ybs, int C, int H, int W, int Wp) {
+    pdl_begin();
     const int q = Wp >> 2;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const long long n = (long long)C * H * q;
@@ -840,7 +854,7 @@ Status launch_pad_rows(const float *x, long long xbs, float *y, long long ybs, i
         ((uintptr_t)y & 15) || ybs % 4)
         return ERR_SHAPE;
     const long long n = (long long)C * H * (Wp / 4);
-    pad_rows_kernel<<<dim3(blocks(n), B), 256, 0, st>>>(x, xbs, y, ybs, C, H, W, Wp);
+    pdl_launch(pad_rows_kernel, dim3(blocks(n), B), 256, 0, st, x, xbs, y, ybs, C, H, W, Wp);
     return cuda_status();
 }
 
@@ -853,10 +867,10 @@ Status launch_wg4_input(const float *x, long long xbs, float *dt, int IC, int H,
     if (pstride <= 0) pstride = IC * ldt;
     if (bstride <= 0) bstride = 36 * pstride;
     if (pad == 1 && W == 4 * TW && ((uintptr_t)x & 15) == 0 && xbs % 4 == 0)
-        wg4_input_vec_kernel<<<grid3((long long)TW * TH, IC, B), 256, 0, st>>>(
+        pdl_launch(wg4_input_vec_kernel, grid3((long long)TW * TH, IC, B), 256, 0, st, 
             x, xbs, dt, IC, H, W, TW, TH, B, ldt, pstride, bstride);
     else
-        wg4_input_kernel<<<grid3((long long)TW * TH, IC, B), 256, 0, st>>>(
+        pdl_launch(wg4_input_kernel, grid3((long long)TW * TH, IC, B), 256, 0, st, 
             x, xbs, dt, IC, H, W, TW, TH, pad, B, ldt, pstride, bstride);
     return cuda_status();
 }
@@ -871,14 +885,14 @@ Status launch_wg4_output(const float *yt, const float *bias, float *y, long long
     if (ldt < TW * TH) return ERR_SHAPE;
     if (pstride <= 0) pstride = OC * ldt;
     if (bstride <= 0) bstride = 36 * pstride;
-    wg4_output_kernel<<<grid3((long long)TW * TH, OC, B), 256, 0, st>>>(
+    pdl_launch(wg4_output_kernel, grid3((long long)TW * TH, OC, B), 256, 0, st, 
         yt, bias, y, ybs, res, rbs, res_mode, OC, OH, OW, TW, TH, act, B, ldt, pstride, bstride);
     return cuda_status();
 }
 
 Status launch_wg4_filter(const float *w, float *wg4, int IC, int OC, cudaStream_t st) {
     const long long n = 36LL * IC * OC;
-    wg4_filter_kernel<<<blocks(n), 256, 0, st>>>(w, wg4, IC, OC);
+    pdl_launch(wg4_filter_kernel, blocks(n), 256, 0, st, w, wg4, IC, OC);
     return cuda_status();
 }
 
@@ -886,7 +900,7 @@ Status launch_rep_fold(const float *w3, const float *b3, const float *w1, const 
                        float *wm, float *bm, int IC, int OC, cudaStream_t st) {
     if (IC <= 0 || OC <= 0) return ERR_SHAPE;
     const long long n = 9LL * IC * OC;
-    rep_fold_kernel<<<blocks(n), 256, 0, st>>>(w3, b3, w1, b1, wm, bm, IC, OC);
+    pdl_launch(rep_fold_kernel, blocks(n), 256, 0, st, w3, b3, w1, b1, wm, bm, IC, OC);
     return cuda_status();
 }
 
@@ -894,7 +908,7 @@ Status launch_kmajor_split(const float *src, float *hi, float *lo, int planes, i
                            long long pstride, int nc, cudaStream_t st) {
     if (planes <= 0 || IC <= 0 || nc <= 0 || ld < nc) return ERR_SHAPE;
     const long long n = (long long)planes * IC * nc;
-    kmajor_split_kernel<<<blocks(n), 256, 0, st>>>(src, hi, lo, planes, IC, ld, pstride, nc);
+    pdl_launch(kmajor_split_kernel, blocks(n), 256, 0, st, src, hi, lo, planes, IC, ld, pstride, nc);
     return cuda_status();
 }
 
@@ -943,7 +957,7 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
         if (!smem_attr_once((const void *)dwconv_plane_kernel<KK, SS, AA>,                    \
                             (int)kDwPlaneSmemMax))                                       \
             return ERR_CUDA;                                                                 \
-        dwconv_plane_kernel<KK, SS, AA><<<g, nthr, sm, st>>>(                                    \
+        pdl_launch(dwconv_plane_kernel<KK, SS, AA>, g, nthr, sm, st,                                     \
             x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, ld, HPp, GX, GY, pairs, even);        \
     } while (0)
 #define PPDL_DW_PLANE_ACT(KK, SS)                                                                 \
@@ -994,7 +1008,7 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
     do {                                                                                         \
         if (!smem_attr_once((const void *)dwconv_band_kernel<KK, SS>, (int)kDwBandSmem))     \
             return ERR_CUDA;                                                                 \
-        dwconv_band_kernel<KK, SS><<<(unsigned)nblk, nthr, smem, st>>>(                          \
+        pdl_launch(dwconv_band_kernel<KK, SS>, (unsigned)nblk, nthr, smem, st,                           \
             x, xbs, w, bias, y, ybs, C, H, W, OH, OW, P, act, bld, bcols, BR, nbands);             \
     } while (0)
         if (K == 3 && S == 1)
@@ -1013,13 +1027,13 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
     const int tiles_x = (OW + kDwTW - 1) / kDwTW, tiles_y = (OH + kDwTH - 1) / kDwTH;
     const dim3 g(tiles_x * tiles_y, C, B);
     if (K == 3 && S == 1)
-        dwconv_kernel<3, 1><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
+        pdl_launch(dwconv_kernel<3, 1>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
     else if (K == 3 && S == 2)
-        dwconv_kernel<3, 2><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
+        pdl_launch(dwconv_kernel<3, 2>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
     else if (K == 5 && S == 1)
-        dwconv_kernel<5, 1><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
+        pdl_launch(dwconv_kernel<5, 1>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
     else if (K == 5 && S == 2)
-        dwconv_kernel<5, 2><<<g, 256, 0, st>>>(x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
+        pdl_launch(dwconv_kernel<5, 2>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
     else
         return ERR_UNSUPPORTED;
     return cuda_status();
@@ -1053,7 +1067,7 @@ Status launch_conv_direct(const float *x, long long xbs, const float *w, const f
     do {                                                                                         \
         if (!smem_attr_once((const void *)conv_direct_kernel<KK, SS>, 64 * 1024))            \
             return ERR_CUDA;                                                                 \
-        conv_direct_kernel<KK, SS><<<g, 256, smem, st>>>(x, xbs, w, bias, y, ybs, IC, H, W, OC,  \
+        pdl_launch(conv_direct_kernel<KK, SS>, g, 256, smem, st, x, xbs, w, bias, y, ybs, IC, H, W, OC,  \
                                                         OH, OW, P, act, tiles_x, ICB);           \
     } while (0)
     if (K == 2 && S == 1)
@@ -1073,7 +1087,7 @@ Status launch_maxpool2_pad(const float *x, long long xbs, float *y, long long yb
     if (!grid3_ok((long long)H * W, C, B) || W % 4 || ((uintptr_t)x & 15) || xbs % 4 ||
         ((uintptr_t)y & 15) || ybs % 4)
         return ERR_SHAPE;
-    maxpool2_pad_kernel<<<grid3((long long)H * W / 4, C, B), 256, 0, st>>>(x, xbs, y, ybs, C, H, W,
+    pdl_launch(maxpool2_pad_kernel, grid3((long long)H * W / 4, C, B), 256, 0, st, x, xbs, y, ybs, C, H, W,
                                                                            B);
     return cuda_status();
 }
@@ -1085,10 +1099,10 @@ Status launch_interp(const float *x, long long xbs, float *y, long long ybs, con
     const bool vec = OW % 4 == 0 && ((uintptr_t)y & 15) == 0 && ybs % 4 == 0 &&
                      (!base || (((uintptr_t)base & 15) == 0 && bbs % 4 == 0));
     if (vec)
-        interp_kernel<4><<<grid3((long long)OH * OW / 4, C, B), 256, 0, st>>>(
+        pdl_launch(interp_kernel<4>, grid3((long long)OH * OW / 4, C, B), 256, 0, st, 
             x, xbs, y, ybs, base, bbs, C, H, W, OH, OW, bilinear ? 1 : 0, B);
     else
-        interp_kernel<1><<<grid3((long long)OH * OW, C, B), 256, 0, st>>>(
+        pdl_launch(interp_kernel<1>, grid3((long long)OH * OW, C, B), 256, 0, st, 
             x, xbs, y, ybs, base, bbs, C, H, W, OH, OW, bilinear ? 1 : 0, B);
     return cuda_status();
 }
@@ -1096,7 +1110,7 @@ Status launch_interp(const float *x, long long xbs, float *y, long long ybs, con
 Status launch_transpose(const float *x, long long xbs, float *y, long long ybs, int R, int Cc,
                         long long ldx, long long ldy, int B, cudaStream_t st) {
     dim3 grid((unsigned)cdiv(Cc, 32), (unsigned)cdiv(R, 32), (unsigned)B);
-    transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(x, xbs, y, ybs, R, Cc, ldx, ldy);
+    pdl_launch(transpose_kernel, grid, dim3(32, 8), 0, st, x, xbs, y, ybs, R, Cc, ldx, ldy);
     (void)sm_count;
     return cuda_status();
 }

@@ -34,6 +34,7 @@ __global__ void layernorm256_kernel(const float *__restrict__ x, const float *__
                                     const float *__restrict__ g, const float *__restrict__ bta,
                                     float *__restrict__ y, const float *__restrict__ q,
                                     float *__restrict__ y2, long long rows) {
+    pdl_begin();
     const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
     const int lane = threadIdx.x & 31;
@@ -83,6 +84,7 @@ __global__ void layernorm256_kernel(const float *__restrict__ x, const float *__
 
 // one warp per row of length L, in place
 __global__ void softmax_rows_kernel(float *__restrict__ x, long long rows, int L) {
+    pdl_begin();
     const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
     const int lane = threadIdx.x & 31;
@@ -103,6 +105,7 @@ __global__ void softmax_rows_kernel(float *__restrict__ x, long long rows, int L
 
 __global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b,
                            float *__restrict__ y, long long n) {
+    pdl_begin();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = __fadd_rn(a[i], b[i]);
 }
@@ -110,11 +113,13 @@ __global__ void add_kernel(const float *__restrict__ a, const float *__restrict_
 // y[i] = a[i] + b[i % nb]: b shared by every page (nb elements per page)
 __global__ void add_bcast_kernel(const float *__restrict__ a, const float *__restrict__ b,
                                  float *__restrict__ y, long long n, long long nb) {
+    pdl_begin();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = __fadd_rn(a[i], b[i % nb]);
 }
 
 __global__ void sigmoid_kernel(const float *__restrict__ x, float *__restrict__ y, long long n) {
+    pdl_begin();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x[i])));
 }
@@ -133,6 +138,7 @@ __global__ void box_refine_kernel(const float *__restrict__ h, const float *__re
                                   const float *__restrict__ b, float *__restrict__ ref,
                                   const float *__restrict__ wq, const float *__restrict__ bq,
                                   float *__restrict__ qp, int rows, int nqp) {
+    pdl_begin();
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
     const int lane = threadIdx.x & 31;
@@ -184,6 +190,7 @@ __global__ void box_refine_kernel(const float *__restrict__ h, const float *__re
 __global__ void row_scale_kernel(const float4 *__restrict__ x, const float *__restrict__ v,
                                  float4 *__restrict__ y, unsigned rows_per_page, unsigned d4,
                                  unsigned n4) {
+    pdl_begin();
     const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n4) return;
     const float s = v[(i / d4) % rows_per_page];
@@ -194,6 +201,7 @@ __global__ void row_scale_kernel(const float4 *__restrict__ x, const float *__re
 // y[b][i][:] = x[b][idx[b][i]][:]
 __global__ void gather_rows_kernel(const float *__restrict__ x, const int32_t *__restrict__ idx,
                                    float *__restrict__ y, int rows_in, int rows_out, int D, int B) {
+    pdl_begin();
     const long long n = (long long)B * rows_out * D;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
@@ -215,6 +223,7 @@ __global__ void gather_rows_kernel(const float *__restrict__ x, const int32_t *_
 constexpr int kVoteJ = 16;
 __global__ void __launch_bounds__(256)
 pp_votes_kernel(const float *__restrict__ order, float *__restrict__ votes) {
+    pdl_begin();
     __shared__ float s_row[kVoteJ][kNQ + 1];  // order[j0 + jj][i]
     __shared__ float s_col[kNQ][kVoteJ + 1];  // order[i][j0 + jj], then the terms
     const int b = blockIdx.y, j0 = blockIdx.x * kVoteJ;
@@ -251,6 +260,7 @@ __global__ void __launch_bounds__(1024)
 pp_select_kernel(const float *__restrict__ logits, const float *__restrict__ boxes,
                  const float *__restrict__ votes, const int32_t *__restrict__ ori_hw,
                  float *__restrict__ dets, int32_t *__restrict__ sel) {
+    pdl_begin();
     constexpr int N = kNQ * kNC;
     extern __shared__ unsigned long long s_key[];  // N keys (dynamic)
     __shared__ unsigned long long s_top[kSelectMax];
@@ -297,6 +307,7 @@ pp_select_kernel(const float *__restrict__ logits, const float *__restrict__ box
 // masks[b][r][p] = mask_logits[b][sel/25][p] > 0
 __global__ void pp_masks_kernel(const float *__restrict__ ml, const int32_t *__restrict__ sel,
                                 int32_t *__restrict__ out) {
+    pdl_begin();
     const int r = blockIdx.y, b = blockIdx.z;
     const int q = sel[b * kNQ + r] / kNC;
     const float4 *src = reinterpret_cast<const float4 *>(ml + ((long long)b * kNQ + q) * kMaskPix);
@@ -316,6 +327,7 @@ __global__ void pp_masks_kernel(const float *__restrict__ ml, const int32_t *__r
 constexpr int kBitsWordsPerWarp = 8;
 __global__ void pp_mask_bits_kernel(const float *__restrict__ ml, const int32_t *__restrict__ sel,
                                     uint32_t *__restrict__ bits) {
+    pdl_begin();
     const int r = blockIdx.y, b = blockIdx.z;
     const int q = sel ? sel[b * kNQ + r] / kNC : r;  // no sel: row r is query r
     const float *src = ml + ((long long)b * kNQ + q) * kMaskPix;
@@ -340,6 +352,7 @@ __global__ void pp_mask_bits_kernel(const float *__restrict__ ml, const int32_t 
 __global__ void pp_gather_bits_kernel(const uint32_t *__restrict__ qbits,
                                       const int32_t *__restrict__ sel,
                                       uint32_t *__restrict__ bits) {
+    pdl_begin();
     const int r = blockIdx.y, b = blockIdx.z;
     const int q = sel[b * kNQ + r] / kNC;
     const uint32_t *src = qbits + ((long long)b * kNQ + q) * kMaskWords;
@@ -354,6 +367,7 @@ __global__ void pp_gather_bits_kernel(const uint32_t *__restrict__ qbits,
 // thread expands one word into 32 ints (eight 16-byte stores).
 __global__ void unpack_mask_bits_kernel(const uint32_t *__restrict__ bits,
                                         int32_t *__restrict__ masks, long long words) {
+    pdl_begin();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= words) return;
     const uint32_t w = __ldg(bits + i);
@@ -369,7 +383,7 @@ __global__ void unpack_mask_bits_kernel(const uint32_t *__restrict__ bits,
 Status launch_pack_mask_bits(const float *ml, uint32_t *bits, int B, cudaStream_t st) {
     if (B <= 0 || B > 65535) return ERR_SHAPE;
     dim3 grid((unsigned)cdiv(kMaskWords, 8 * kBitsWordsPerWarp), kNQ, (unsigned)B);
-    pp_mask_bits_kernel<<<grid, 256, 0, st>>>(ml, nullptr, bits);
+    pdl_launch(pp_mask_bits_kernel, grid, 256, 0, st, ml, nullptr, bits);
     return cuda_status();
 }
 
@@ -377,7 +391,7 @@ Status launch_unpack_mask_bits(const uint32_t *bits, int32_t *masks, long long r
                                cudaStream_t st) {
     if (rows <= 0) return rows == 0 ? OK : ERR_SHAPE;
     const long long words = rows * kMaskWords;
-    unpack_mask_bits_kernel<<<blocks(words), 256, 0, st>>>(bits, masks, words);
+    pdl_launch(unpack_mask_bits_kernel, blocks(words), 256, 0, st, bits, masks, words);
     return cuda_status();
 }
 
@@ -391,17 +405,17 @@ Status launch_layernorm256_add(const float *x, const float *r, const float *g, c
                                cudaStream_t st) {
     if (rows <= 0) return rows == 0 ? OK : ERR_SHAPE;
     if (q && !y2) return ERR_SHAPE;
-    layernorm256_kernel<<<blocks(rows * 32), 256, 0, st>>>(x, r, g, b, y, q, y2, rows);
+    pdl_launch(layernorm256_kernel, blocks(rows * 32), 256, 0, st, x, r, g, b, y, q, y2, rows);
     return cuda_status();
 }
 
 Status launch_softmax_rows(float *x, long long rows, int L, cudaStream_t st) {
-    softmax_rows_kernel<<<blocks(rows * 32), 256, 0, st>>>(x, rows, L);
+    pdl_launch(softmax_rows_kernel, blocks(rows * 32), 256, 0, st, x, rows, L);
     return cuda_status();
 }
 
 Status launch_add(const float *a, const float *b, float *y, long long n, cudaStream_t st) {
-    add_kernel<<<blocks(n), 256, 0, st>>>(a, b, y, n);
+    pdl_launch(add_kernel, blocks(n), 256, 0, st, a, b, y, n);
     return cuda_status();
 }
 
@@ -409,12 +423,12 @@ Status launch_add_bcast(const float *a, const float *b, float *y, long long n_pe
                         int pages, cudaStream_t st) {
     if (n_per_page <= 0 || pages <= 0) return ERR_SHAPE;
     const long long n = n_per_page * pages;
-    add_bcast_kernel<<<blocks(n), 256, 0, st>>>(a, b, y, n, n_per_page);
+    pdl_launch(add_bcast_kernel, blocks(n), 256, 0, st, a, b, y, n, n_per_page);
     return cuda_status();
 }
 
 Status launch_sigmoid(const float *x, float *y, long long n, cudaStream_t st) {
-    sigmoid_kernel<<<blocks(n), 256, 0, st>>>(x, y, n);
+    pdl_launch(sigmoid_kernel, blocks(n), 256, 0, st, x, y, n);
     return cuda_status();
 }
 
@@ -424,7 +438,7 @@ Status launch_box_refine(const float *h, const float *w, const float *b, float *
     if (rows <= 0 || (qp && nqp <= 0) ||
         (((uintptr_t)h | (uintptr_t)w | (uintptr_t)ref | (uintptr_t)wq) & 15))
         return ERR_SHAPE;
-    box_refine_kernel<<<cdiv(rows, 8), 256, 0, st>>>(h, w, b, ref, wq, bq, qp, rows, nqp);
+    pdl_launch(box_refine_kernel, cdiv(rows, 8), 256, 0, st, h, w, b, ref, wq, bq, qp, rows, nqp);
     return cuda_status();
 }
 
@@ -433,7 +447,7 @@ Status launch_row_scale(const float *x, const float *v, float *y, long long rows
     const long long n = (long long)B * rows_per_page * D;
     if (D % 4 || n / 4 >= (1LL << 31) || ((uintptr_t)x & 15) || ((uintptr_t)y & 15))
         return ERR_SHAPE;
-    row_scale_kernel<<<blocks(n / 4), 256, 0, st>>>(
+    pdl_launch(row_scale_kernel, blocks(n / 4), 256, 0, st, 
         reinterpret_cast<const float4 *>(x), v, reinterpret_cast<float4 *>(y),
         (unsigned)rows_per_page, (unsigned)(D / 4), (unsigned)(n / 4));
     return cuda_status();
@@ -442,7 +456,7 @@ Status launch_row_scale(const float *x, const float *v, float *y, long long rows
 Status launch_gather_rows(const float *x, const int32_t *idx, float *y, int rows_in, int rows_out,
                           int D, int B, cudaStream_t st) {
     const long long n = (long long)B * rows_out * D;
-    gather_rows_kernel<<<blocks(n), 256, 0, st>>>(x, idx, y, rows_in, rows_out, D, B);
+    pdl_launch(gather_rows_kernel, blocks(n), 256, 0, st, x, idx, y, rows_in, rows_out, D, B);
     return cuda_status();
 }
 
@@ -453,19 +467,19 @@ Status launch_postprocess(const float *logits, const float *boxes, const float *
     const int smem = kNQ * kNC * (int)sizeof(unsigned long long);
     if (!smem_attr_once((const void *)pp_select_kernel, smem)) return ERR_CUDA;
     float *votes = reinterpret_cast<float *>(rank);  // the 300 votes of each page
-    pp_votes_kernel<<<dim3(cdiv(kNQ, kVoteJ), B), 256, 0, st>>>(order, votes);
-    pp_select_kernel<<<B, 1024, smem, st>>>(logits, boxes, votes, ori_hw, dets, sel);
+    pdl_launch(pp_votes_kernel, dim3(cdiv(kNQ, kVoteJ), B), 256, 0, st, order, votes);
+    pdl_launch(pp_select_kernel, B, 1024, smem, st, logits, boxes, votes, ori_hw, dets, sel);
     if (masks) {
         dim3 grid((unsigned)cdiv(kMaskPix / 4, 256), kNQ, (unsigned)B);
-        pp_masks_kernel<<<grid, 256, 0, st>>>(mask_logits, sel, masks);
+        pdl_launch(pp_masks_kernel, grid, 256, 0, st, mask_logits, sel, masks);
     }
     if (mask_bits && mask_bits_q) {
-        pp_gather_bits_kernel<<<dim3(1, kNQ, (unsigned)B), 128, 0, st>>>(mask_bits_q, sel,
+        pdl_launch(pp_gather_bits_kernel, dim3(1, kNQ, (unsigned)B), 128, 0, st, mask_bits_q, sel,
                                                                           mask_bits);
     } else if (mask_bits && mask_logits) {
         // 1250 words per row: blocks of 8 warps x 8 words
         dim3 grid((unsigned)cdiv(kMaskWords, 8 * kBitsWordsPerWarp), kNQ, (unsigned)B);
-        pp_mask_bits_kernel<<<grid, 256, 0, st>>>(mask_logits, sel, mask_bits);
+        pdl_launch(pp_mask_bits_kernel, grid, 256, 0, st, mask_logits, sel, mask_bits);
     }
     return cuda_status();
 }

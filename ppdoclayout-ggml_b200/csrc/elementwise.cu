@@ -13,6 +13,7 @@ namespace {
 __global__ void bias_act_kernel(const float *__restrict__ x, const float *__restrict__ bias,
                                 float *__restrict__ y, long long n, long long plane, int C,
                                 int act) {
+    pdl_begin();
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
         float v = x[i];
@@ -24,6 +25,7 @@ __global__ void bias_act_kernel(const float *__restrict__ x, const float *__rest
 __global__ void bias_act_kernel_v4(const float4 *__restrict__ x, const float *__restrict__ bias,
                                    float4 *__restrict__ y, long long n4, long long plane4, int C,
                                    int act) {
+    pdl_begin();
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
         float4 v = x[i];
@@ -39,6 +41,7 @@ __global__ void bias_act_kernel_v4(const float4 *__restrict__ x, const float *__
 }
 
 __global__ void copy_kernel(const float4 *__restrict__ x, float4 *__restrict__ y, long long n4) {
+    pdl_begin();
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride)
         y[i] = x[i];
@@ -46,6 +49,7 @@ __global__ void copy_kernel(const float4 *__restrict__ x, float4 *__restrict__ y
 
 __global__ void copy_kernel_tail(const float *__restrict__ x, float *__restrict__ y,
                                  long long from, long long n) {
+    pdl_begin();
     const long long i = from + (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = x[i];
 }
@@ -71,11 +75,11 @@ Status launch_bias_act(const float *x, const float *bias, float *y, long long n,
     if (((uintptr_t)x | (uintptr_t)y) % 16 == 0 && plane % 4 == 0) {
         const long long n4 = n / 4;
         const int grid = (int)(cdiv(n4, 256) < grid_cap ? cdiv(n4, 256) : grid_cap);
-        bias_act_kernel_v4<<<grid, 256, 0, stream>>>((const float4 *)x, bias, (float4 *)y, n4,
+        pdl_launch(bias_act_kernel_v4, grid, 256, 0, stream, (const float4 *)x, bias, (float4 *)y, n4,
                                                      plane / 4, C, act);
     } else {
         const int grid = (int)(cdiv(n, 256) < grid_cap ? cdiv(n, 256) : grid_cap);
-        bias_act_kernel<<<grid, 256, 0, stream>>>(x, bias, y, n, plane, C, act);
+        pdl_launch(bias_act_kernel, grid, 256, 0, stream, x, bias, y, n, plane, C, act);
     }
     return cuda_status();
 }
@@ -89,11 +93,11 @@ Status launch_copy(const float *x, float *y, long long n, cudaStream_t stream) {
         if (n4) {
             const int grid_cap = sm_count() * 8;
             const int grid = (int)(cdiv(n4, 256) < grid_cap ? cdiv(n4, 256) : grid_cap);
-            copy_kernel<<<grid, 256, 0, stream>>>((const float4 *)x, (float4 *)y, n4);
+            pdl_launch(copy_kernel, grid, 256, 0, stream, (const float4 *)x, (float4 *)y, n4);
         }
         done = n4 * 4;
     }
-    if (done < n) copy_kernel_tail<<<cdiv(n - done, 256), 256, 0, stream>>>(x, y, done, n);
+    if (done < n) pdl_launch(copy_kernel_tail, cdiv(n - done, 256), 256, 0, stream, x, y, done, n);
     return cuda_status();
 }
 

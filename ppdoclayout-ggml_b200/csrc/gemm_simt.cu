@@ -23,6 +23,7 @@ constexpr int kThreads = 256;
 template <int BM, int BN, int BK, bool kAK, bool kBN, bool kConv>
 __global__ void __launch_bounds__(kThreads)
 gemm_simt_kernel(const GemmArgs g) {
+    pdl_begin();
     constexpr int TM = BM / 16, TN = BN / 16;
     constexpr int LA = BM * BK / kThreads, LB = BK * BN / kThreads;
     __shared__ __align__(16) float As[2][BK][BM + 4];
@@ -172,16 +173,16 @@ Status dispatch(const GemmArgs &g, cudaStream_t stream) {
     const bool bn = g.B.s1 == 1;  // n contiguous
     dim3 grid((unsigned)cdiv(g.N, BN), (unsigned)cdiv(g.M, BM), (unsigned)g.batch);
     if (g.conv.K > 0) {
-        if (ak) gemm_simt_kernel<BM, BN, BK, true, true, true><<<grid, kThreads, 0, stream>>>(g);
-        else gemm_simt_kernel<BM, BN, BK, false, true, true><<<grid, kThreads, 0, stream>>>(g);
+        if (ak) pdl_launch(gemm_simt_kernel<BM, BN, BK, true, true, true>, grid, kThreads, 0, stream, g);
+        else pdl_launch(gemm_simt_kernel<BM, BN, BK, false, true, true>, grid, kThreads, 0, stream, g);
     } else if (ak && bn) {
-        gemm_simt_kernel<BM, BN, BK, true, true, false><<<grid, kThreads, 0, stream>>>(g);
+        pdl_launch(gemm_simt_kernel<BM, BN, BK, true, true, false>, grid, kThreads, 0, stream, g);
     } else if (ak) {
-        gemm_simt_kernel<BM, BN, BK, true, false, false><<<grid, kThreads, 0, stream>>>(g);
+        pdl_launch(gemm_simt_kernel<BM, BN, BK, true, false, false>, grid, kThreads, 0, stream, g);
     } else if (bn) {
-        gemm_simt_kernel<BM, BN, BK, false, true, false><<<grid, kThreads, 0, stream>>>(g);
+        pdl_launch(gemm_simt_kernel<BM, BN, BK, false, true, false>, grid, kThreads, 0, stream, g);
     } else {
-        gemm_simt_kernel<BM, BN, BK, false, false, false><<<grid, kThreads, 0, stream>>>(g);
+        pdl_launch(gemm_simt_kernel<BM, BN, BK, false, false, false>, grid, kThreads, 0, stream, g);
     }
     return cuda_status();
 }

@@ -614,6 +614,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // barriers and TMEM are set up before the wait for the previous grid:
+    // every global access of every role follows it
+    pdl_begin();
     const int kblocks = (a.K + kBK - 1) / kBK;
     // k-blocks of the tiles of batch entry z: all of them, or with split K
     // (a.kps > 0) the range [z kps, z kps + kps) of the entry's split z
@@ -1351,6 +1354,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
 __global__ void tf32_split_kernel(const float *__restrict__ w, float *__restrict__ hi,
                                   float *__restrict__ lo, long long n) {
+    pdl_begin();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const float v = w[i];
@@ -1361,6 +1365,7 @@ __global__ void tf32_split_kernel(const float *__restrict__ w, float *__restrict
 
 __global__ void tf32_split_pad_kernel(const float *__restrict__ w, float *__restrict__ hi,
                                       float *__restrict__ lo, int rows, int K, int Kp) {
+    pdl_begin();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)rows * Kp) return;
     const int n = (int)(i / Kp), k = (int)(i - (long long)n * Kp);
@@ -1376,6 +1381,7 @@ __global__ void tf32_split_pad_kernel(const float *__restrict__ w, float *__rest
 __global__ void tf32_split_box_kernel(const float *__restrict__ w, float *__restrict__ hi,
                                       float *__restrict__ lo, int OC, int IC, int KS, int CB,
                                       int kbpb, int Kb) {
+    pdl_begin();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)OC * Kb) return;
     const int n = (int)(i / Kb), k = (int)(i - (long long)n * Kb);
@@ -1438,7 +1444,7 @@ int sm_count() {
 
 Status launch_tf32_split(const float *w, float *hi, float *lo, long long n, cudaStream_t st) {
     if (n <= 0) return n == 0 ? OK : ERR_SHAPE;
-    tf32_split_kernel<<<(int)((n + 255) / 256), 256, 0, st>>>(w, hi, lo, n);
+    pdl_launch(tf32_split_kernel, (int)((n + 255) / 256), 256, 0, st, w, hi, lo, n);
     return cuda_status();
 }
 
@@ -1446,7 +1452,7 @@ Status launch_tf32_split_pad(const float *w, float *hi, float *lo, int rows, int
                              cudaStream_t st) {
     if (rows <= 0 || K <= 0 || Kp < K) return ERR_SHAPE;
     const long long n = (long long)rows * Kp;
-    tf32_split_pad_kernel<<<(int)((n + 255) / 256), 256, 0, st>>>(w, hi, lo, rows, K, Kp);
+    pdl_launch(tf32_split_pad_kernel, (int)((n + 255) / 256), 256, 0, st, w, hi, lo, rows, K, Kp);
     return cuda_status();
 }
 
@@ -1457,7 +1463,7 @@ Status launch_tf32_split_box(const float *w, float *hi, float *lo, int OC, int I
     tc_conv_box_blocks(IC, KS, &CB, &kbpb, &nbx);
     const int Kb = nbx * kbpb * 32;
     const long long n = (long long)OC * Kb;
-    tf32_split_box_kernel<<<(int)((n + 255) / 256), 256, 0, st>>>(w, hi, lo, OC, IC, KS, CB, kbpb,
+    pdl_launch(tf32_split_box_kernel, (int)((n + 255) / 256), 256, 0, st, w, hi, lo, OC, IC, KS, CB, kbpb,
                                                                   Kb);
     return cuda_status();
 }
@@ -1794,6 +1800,7 @@ namespace {
 // + bias, + residual mode 1, activation, + residual mode 2).
 __global__ void splitk_reduce_kernel(const float *__restrict__ ws, long long ws_bs, int splits,
                                      int M, int N, TcEpilogue e) {
+    pdl_begin();
     const long long n_all = (long long)M * N;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n_all;
          i += (long long)gridDim.x * blockDim.x) {
@@ -1894,19 +1901,19 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     if (grid > a.tiles) grid = a.tiles;
     if (g.kps) {
         if (g.gather || g.box || g.rows || g.bits || g.batch < 1) return ERR_SHAPE;
-        tc_gemm_kernel<ACT_NONE, kModeTile><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi,
+        pdl_launch(tc_gemm_kernel<ACT_NONE, kModeTile>, grid, kThreads, g.smem, st, g.tmA, g.tmBhi,
                                                                            g.tmBlo, g.tmC, a);
         const Status s0 = cuda_status();
         if (s0 != OK) return s0;
         const long long n_all = (long long)g.M * g.N;
         int rb = (int)((n_all + 255) / 256);
         if (rb > 8 * sm_count()) rb = 8 * sm_count();
-        splitk_reduce_kernel<<<rb, 256, 0, st>>>(g.ws, g.ws_bs, splits, g.M, g.N, g.epi);
+        pdl_launch(splitk_reduce_kernel, rb, 256, 0, st, g.ws, g.ws_bs, splits, g.M, g.N, g.epi);
         return cuda_status();
     }
     if (g.bits) {
         // packed output: tile A, no epilogue ops (checked by the planner)
-        tc_gemm_kernel<ACT_NONE, kModeBits><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi,
+        pdl_launch(tc_gemm_kernel<ACT_NONE, kModeBits>, grid, kThreads, g.smem, st, g.tmA, g.tmBhi,
                                                                            g.tmBlo, g.tmC, a);
         return cuda_status();
     }
@@ -1914,7 +1921,7 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     switch (mode * 4 + g.epi.act) {
 #define PPDL_TC_CASE(M_, A_)                                                                  \
     case M_ * 4 + A_:                                                                      \
-        tc_gemm_kernel<A_, M_><<<grid, kThreads, g.smem, st>>>(g.tmA, g.tmBhi, g.tmBlo, g.tmC, \
+        pdl_launch(tc_gemm_kernel<A_, M_>, grid, kThreads, g.smem, st, g.tmA, g.tmBhi, g.tmBlo, g.tmC, \
                                                                a);                          \
         break;
         PPDL_TC_CASE(kModeTile, ACT_NONE)

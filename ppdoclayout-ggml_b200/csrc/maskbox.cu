@@ -54,6 +54,7 @@ __device__ __forceinline__ void write_box(int xmin, int ymin, int xmax, int ymax
 
 __global__ void __launch_bounds__(kThreads)
 mask_box_kernel(const float *__restrict__ ml, float *__restrict__ out) {
+    pdl_begin();
     const int q = blockIdx.x;
     const float4 *m = reinterpret_cast<const float4 *>(ml + (size_t)q * kMaskPix);
     constexpr int kRowVec = kMaskHW / 4;  // 50 float4 per mask row
@@ -97,6 +98,7 @@ mask_box_kernel(const float *__restrict__ ml, float *__restrict__ out) {
 // lowest and highest set bit.  Same pixels, same extents, same result.
 __global__ void __launch_bounds__(kThreads)
 mask_box_bits_kernel(const uint32_t *__restrict__ bits, float *__restrict__ out) {
+    pdl_begin();
     const int q = blockIdx.x;
     const uint32_t *m = bits + (size_t)q * kMaskWords;
     int xmin = INT_MAX, ymin = INT_MAX, xmax = -1, ymax = -1;
@@ -146,14 +148,14 @@ mask_box_bits_kernel(const uint32_t *__restrict__ bits, float *__restrict__ out)
 Status launch_mask_box_bits(const uint32_t *bits, float *out, int rows, cudaStream_t stream) {
     if (rows <= 0) return rows == 0 ? OK : ERR_SHAPE;
     if ((uintptr_t)out & 15) return ERR_SHAPE;
-    mask_box_bits_kernel<<<rows, kThreads, 0, stream>>>(bits, out);
+    pdl_launch(mask_box_bits_kernel, rows, kThreads, 0, stream, bits, out);
     return cuda_status();
 }
 
 Status launch_mask_box(const float *ml, float *out, int rows, cudaStream_t stream) {
     if (rows <= 0) return rows == 0 ? OK : ERR_SHAPE;
     if (((uintptr_t)ml | (uintptr_t)out) & 15) return ERR_SHAPE;
-    mask_box_kernel<<<rows, kThreads, 0, stream>>>(ml, out);
+    pdl_launch(mask_box_kernel, rows, kThreads, 0, stream, ml, out);
     return cuda_status();
 }
 

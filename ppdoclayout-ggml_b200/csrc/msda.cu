@@ -55,6 +55,7 @@ msda_kernel(const float *__restrict__ val,  // [B][13125][ldv], 256 used
             const float *__restrict__ ref,  // [B*nq][4] (in-model only)
             float *__restrict__ out,        // [B*nq][256]
             int nq, int npairs, int ld1, int ld2, int ldv) {
+    pdl_begin();
     __shared__ float s_w[kPairs][12];
     __shared__ int s_idx[kPairs][kTapStride];
     __shared__ float s_tw[kPairs][kTapStride];
@@ -171,10 +172,10 @@ Status launch_msda(const float *val, const float *p1, const float *p2, const flo
     const int npairs = batch * nq * kNH;
     const int grid = cdiv(npairs, kPairs);
     if (canon)
-        msda_kernel<true><<<grid, kThreads, 0, stream>>>(val, p1, p2, ref, out, nq, npairs, ld1,
+        pdl_launch(msda_kernel<true>, grid, kThreads, 0, stream, val, p1, p2, ref, out, nq, npairs, ld1,
                                                          ld2, ldv);
     else
-        msda_kernel<false><<<grid, kThreads, 0, stream>>>(val, p1, p2, ref, out, nq, npairs, ld1,
+        pdl_launch(msda_kernel<false>, grid, kThreads, 0, stream, val, p1, p2, ref, out, nq, npairs, ld1,
                                                           ld2, ldv);
     return cuda_status();
 }

@@ -26,6 +26,7 @@ constexpr int kMaxKeys = 16384;
 __global__ void __launch_bounds__(kThreads)
 topk_kernel(const float *__restrict__ lg, int32_t *__restrict__ out, int ntok, int nc, int nq,
             int n2) {
+    pdl_begin();
     extern __shared__ unsigned long long s_key[];
     const float *lb = lg + (size_t)blockIdx.x * ntok * nc;
     for (int q = threadIdx.x; q < n2; q += kThreads) {
@@ -79,6 +80,7 @@ constexpr int kChunk = 512;  // tokens whose logits are staged in shared memory 
 __global__ void __launch_bounds__(kThreads)
 topk_select_kernel(const float *__restrict__ lg, int32_t *__restrict__ out, int ntok, int nc,
                    int nq) {
+    pdl_begin();
     extern __shared__ unsigned long long s_key[];  // ntok keys, then kChunk x nc logits
     float *s_lg = reinterpret_cast<float *>(s_key + ntok);
     __shared__ unsigned long long s_sel[kSelectMax];
@@ -120,9 +122,9 @@ Status launch_topk(const float *lg, int32_t *out, int ntok, int nc, int nq, int 
         return ERR_CUDA;
     const size_t sel_smem = (size_t)ntok * sizeof(unsigned long long) + (size_t)kChunk * nc * 4;
     if (nq <= kSelectMax && sel_smem <= kSelSmemMax)
-        topk_select_kernel<<<batch, kThreads, sel_smem, stream>>>(lg, out, ntok, nc, nq);
+        pdl_launch(topk_select_kernel, batch, kThreads, sel_smem, stream, lg, out, ntok, nc, nq);
     else
-        topk_kernel<<<batch, kThreads, smem, stream>>>(lg, out, ntok, nc, nq, n2);
+        pdl_launch(topk_kernel, batch, kThreads, smem, stream, lg, out, ntok, nc, nq, n2);
     return cuda_status();
 }
 
