@@ -396,12 +396,13 @@ public:
     // y = act(conv(x) + bias (+ res if res_mode == 1)) (+ res if res_mode == 2)
     // p_hi < 0: symmetric padding p; otherwise bottom/right padding p_hi
     // (the stem's ggml_pad, :621-624).
-    // w_fold / b_fold: weights to use instead of the named ones (same shapes)
+    // w_ov / b_ov: weight and bias tensors to use instead of the named ones
+    // (folded or stacked weights; name then only names the step)
     void conv(const V &x, const V &y, const std::string &name, int s, int p, int act,
-              const V &res = V(), int res_mode = 0, int p_hi = -1,
-              const float *w_fold = nullptr, const float *b_fold = nullptr) {
-        const WT &wt = W(name + ".weight");
-        const WT &bt = W(name + ".bias");
+              const V &res = V(), int res_mode = 0, int p_hi = -1, const WT *w_ov = nullptr,
+              const WT *b_ov = nullptr) {
+        const WT &wt = w_ov ? *w_ov : W(name + ".weight");
+        const WT &bt = b_ov ? *b_ov : W(name + ".bias");
         if (!ok) return;
         const int K = (int)wt.ne[0], IC = (int)wt.ne[2], OC = (int)wt.ne[3];
         const int ph = p_hi < 0 ? p : p_hi;
@@ -412,7 +413,7 @@ public:
             fail("conv " + name + ": shape mismatch");
             return;
         }
-        const float *wp = w_fold ? w_fold : wt.p, *bp = b_fold ? b_fold : bt.p;
+        const float *wp = wt.p, *bp = bt.p;
         if (dw) {
             if (res_mode || p_hi >= 0) {
                 fail("conv " + name + ": depthwise form not supported");
@@ -804,8 +805,8 @@ public:
 
     // RepVGG block (src/ppdoclayout.cpp:656-661): silu(c1(x) + c2(x)), c1 3x3
     // and c2 1x1, run as one 3x3 conv with c2 folded into c1's centre tap
-    // (launch_rep_fold, at load)
-    void repvgg(const V &x, const V &y, const std::string &pfx) {
+    // (launch_rep_fold, at load); res: added after the SiLU
+    void repvgg(const V &x, const V &y, const std::string &pfx, const V &res = V()) {
         const WT &w3 = W(pfx + ".c1.weight"), &b3 = W(pfx + ".c1.bias");
         const WT &w1 = W(pfx + ".c2.weight"), &b1 = W(pfx + ".c2.bias");
         if (!ok) return;
@@ -821,17 +822,67 @@ public:
             fail("repvgg " + pfx + ": fold launch failed");
             return;
         }
-        conv(x, y, pfx + ".c1", 1, 1, ACT_SILU, V(), 0, -1, wm, bm);
+        WT wmt, bmt;
+        wmt.p = wm;
+        for (int i = 0; i < 4; i++) wmt.ne[i] = w3.ne[i];
+        bmt.p = bm;
+        bmt.ne[0] = OC;
+        conv(x, y, pfx + ".c1", 1, 1, ACT_SILU, res, res.p ? 2 : 0, -1, &wmt, &bmt);
     }
 
-    void csp(const V &x, const V &out, const std::string &pfx) {
-        V a = tensor(256, x.H, x.W), b = tensor(256, x.H, x.W);
-        conv(x, a, pfx + ".c1", 1, 0, ACT_SILU);
-        for (int i = 0; i < 3; i++) {
-            repvgg(a, b, pfx + ".bn" + std::to_string(i));
-            std::swap(a, b);
+    // 1x1 convs of the same input stacked along the output channels: one GEMM
+    // writing their outputs as consecutive channel slices of y
+    void conv_cat(const V &x, const V &y, const std::vector<std::string> &names,
+                  const std::string &name, int act) {
+        std::vector<const WT *> ws, bs;
+        for (const auto &n : names) {
+            ws.push_back(&W(n + ".weight"));
+            bs.push_back(&W(n + ".bias"));
         }
-        conv(x, out, pfx + ".c2", 1, 0, ACT_SILU, a, 2);  // a + c2(x)
+        if (!ok) return;
+        const int64_t IC = ws[0]->ne[2];
+        int64_t OC = 0;
+        for (size_t i = 0; i < ws.size(); i++) {
+            if (ws[i]->ne[0] != 1 || ws[i]->ne[1] != 1 || ws[i]->ne[2] != IC ||
+                bs[i]->ne[0] != ws[i]->ne[3]) {
+                fail("conv " + name + ": stacked weights disagree");
+                return;
+            }
+            OC += ws[i]->ne[3];
+        }
+        float *wc = dalloc(OC * IC), *bc = dalloc(OC);
+        if (!ok) return;
+        long long r = 0;
+        for (size_t i = 0; i < ws.size(); i++) {
+            const long long o = ws[i]->ne[3];
+            if (cudaMemcpy(wc + r * IC, ws[i]->p, sizeof(float) * o * IC,
+                           cudaMemcpyDeviceToDevice) != cudaSuccess ||
+                cudaMemcpy(bc + r, bs[i]->p, sizeof(float) * o, cudaMemcpyDeviceToDevice) !=
+                    cudaSuccess) {
+                fail("conv " + name + ": weight stacking failed");
+                return;
+            }
+            r += o;
+        }
+        WT wt, bt;
+        wt.p = wc;
+        wt.ne[2] = IC;
+        wt.ne[3] = OC;
+        bt.p = bc;
+        bt.ne[0] = OC;
+        conv(x, y, name, 1, 0, act, V(), 0, -1, &wt, &bt);
+    }
+
+    // CSP block (src/ppdoclayout.cpp:663-668): c1 and c2 (1x1 + SiLU of x)
+    // as one GEMM into [a | c2(x)], three RepVGG blocks on a, the last one
+    // adding c2(x) after its SiLU (the reference's final add)
+    void csp(const V &x, const V &out, const std::string &pfx) {
+        V ab = tensor(512, x.H, x.W), t1 = tensor(256, x.H, x.W), t2 = tensor(256, x.H, x.W);
+        const V a = ab.slice(0, 256), c2o = ab.slice(256, 256);
+        conv_cat(x, ab, {pfx + ".c1", pfx + ".c2"}, pfx + ".c1c2", ACT_SILU);
+        repvgg(a, t1, pfx + ".bn0");
+        repvgg(t1, t2, pfx + ".bn1");
+        repvgg(t2, out, pfx + ".bn2", c2o);
     }
 
     void interp(const V &x, const V &y, bool bilinear, const V &base = V()) {
