@@ -1160,7 +1160,9 @@ public:
             S v = seq(kNQ, kDM);
             on_lane(2);
             after(e_x);
-            lin(x, v, dp + ".sa.v");
+            // at most 34 CTAs: the chain's 2400-row GEMMs beside it take 114
+            // (19 row tiles x 6 column tiles), so neither waits for SMs
+            lin(x, v, dp + ".sa.v", ACT_NONE, S(), 34);
             on_lane(0);
             S qpos = seq(kNQ, kDM);
             lin(qp1, qpos, "qpos.1");
