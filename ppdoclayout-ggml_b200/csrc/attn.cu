@@ -220,11 +220,11 @@ Status launch_attention(const float *q, const float *k, const float *v, float *o
     const int ldS = attention_lds(T);
     const dim3 grid((T + kBQ - 1) / kBQ, heads, B);
     if (T <= kKTAll)
-        pdl_launch(attn_kernel<kKTAll, 1>, grid, kThreads, smem, st, q, k, v, o, T, ldqk, bsqk, ldvo, bsvo,
-                                                             scale, ldS);
+        pdl_launch(attn_kernel<kKTAll, 1>, grid, kThreads, smem, st, q, k, v, o, T, ldqk, bsqk,
+                   ldvo, bsvo, scale, ldS);
     else
-        pdl_launch(attn_kernel<64, 2>, grid, kThreads, smem, st, q, k, v, o, T, ldqk, bsqk, ldvo, bsvo,
-                                                         scale, ldS);
+        pdl_launch(attn_kernel<64, 2>, grid, kThreads, smem, st, q, k, v, o, T, ldqk, bsqk, ldvo,
+                   bsvo, scale, ldS);
     return cuda_status();
 }
 

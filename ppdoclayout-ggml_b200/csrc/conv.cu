@@ -15,6 +15,8 @@
 //     RepVGG sum and the HG-block concat cost no extra pass.
 // The transform matrices are the reference's (a data format shared with its
 // op 10/11/12 planes and ".wg4" weights).
+#include <cmath>
+
 #include "common.cuh"
 #include "conv.h"
 
@@ -734,15 +736,21 @@ __global__ void maxpool2_pad_kernel(const float *__restrict__ x, long long xbs, 
 // NEAREST: src = (int)(dst / sf).  BILINEAR (no align-corners): src =
 // (dst + 0.5) / sf - 0.5, floor, both taps clamped to the edge, fractional
 // weight clamped to [0, 1].  Optionally adds into y (y = base + interp).
+// rx / ry: 1 / sf when sf is a power of two (the quotient is then exact, so
+// the product is the same number as the division), else 0: divide.
+__device__ __forceinline__ float interp_div(float a, float sf, float r) {
+    return r != 0.0f ? __fmul_rn(a, r) : __fdiv_rn(a, sf);
+}
 __device__ __forceinline__ float interp_one(const float *__restrict__ xp, int ox, int oy, int H,
-                                            int W, float sfx, float sfy, int bilinear) {
+                                            int W, float sfx, float sfy, float rx, float ry,
+                                            int bilinear) {
     if (!bilinear) {
-        const int sx = min((int)((float)ox / sfx), W - 1);
-        const int sy = min((int)((float)oy / sfy), H - 1);
+        const int sx = min((int)interp_div((float)ox, sfx, rx), W - 1);
+        const int sy = min((int)interp_div((float)oy, sfy, ry), H - 1);
         return xp[(long long)sy * W + sx];
     }
-    const float fx = __fsub_rn(__fdiv_rn(__fadd_rn((float)ox, 0.5f), sfx), 0.5f);
-    const float fy = __fsub_rn(__fdiv_rn(__fadd_rn((float)oy, 0.5f), sfy), 0.5f);
+    const float fx = __fsub_rn(interp_div(__fadd_rn((float)ox, 0.5f), sfx, rx), 0.5f);
+    const float fy = __fsub_rn(interp_div(__fadd_rn((float)oy, 0.5f), sfy, ry), 0.5f);
     const float flx = floorf(fx), fly = floorf(fy);
     int x0 = (int)flx, y0 = (int)fly;
     int x1 = x0 + 1, y1 = y0 + 1;
@@ -761,7 +769,8 @@ __device__ __forceinline__ float interp_one(const float *__restrict__ xp, int ox
 template <int V>
 __global__ void interp_kernel(const float *__restrict__ x, long long xbs, float *__restrict__ y,
                               long long ybs, const float *__restrict__ base, long long bbs, int C,
-                              int H, int W, int OH, int OW, int bilinear, int B) {
+                              int H, int W, int OH, int OW, int bilinear, int B, float rx,
+                              float ry) {
     pdl_begin();
     // grid (C*OH*OW / (256 V), B)
     const int ow = OW / V;
@@ -774,7 +783,8 @@ __global__ void interp_kernel(const float *__restrict__ x, long long xbs, float 
     const long long off = (long long)c * OH * OW + (long long)oy * OW + ox0;
     float v[V];
 #pragma unroll
-    for (int e = 0; e < V; e++) v[e] = interp_one(xp, ox0 + e, oy, H, W, sfx, sfy, bilinear);
+    for (int e = 0; e < V; e++)
+        v[e] = interp_one(xp, ox0 + e, oy, H, W, sfx, sfy, rx, ry, bilinear);
     if (V == 4) {
         if (base) {
             const float4 b4 = *reinterpret_cast<const float4 *>(base + (long long)b * bbs + off);
@@ -867,11 +877,11 @@ Status launch_wg4_input(const float *x, long long xbs, float *dt, int IC, int H,
     if (pstride <= 0) pstride = IC * ldt;
     if (bstride <= 0) bstride = 36 * pstride;
     if (pad == 1 && W == 4 * TW && ((uintptr_t)x & 15) == 0 && xbs % 4 == 0)
-        pdl_launch(wg4_input_vec_kernel, grid3((long long)TW * TH, IC, B), 256, 0, st, 
-            x, xbs, dt, IC, H, W, TW, TH, B, ldt, pstride, bstride);
+        pdl_launch(wg4_input_vec_kernel, grid3((long long)TW * TH, IC, B), 256, 0, st, x, xbs, dt,
+                   IC, H, W, TW, TH, B, ldt, pstride, bstride);
     else
-        pdl_launch(wg4_input_kernel, grid3((long long)TW * TH, IC, B), 256, 0, st, 
-            x, xbs, dt, IC, H, W, TW, TH, pad, B, ldt, pstride, bstride);
+        pdl_launch(wg4_input_kernel, grid3((long long)TW * TH, IC, B), 256, 0, st, x, xbs, dt, IC,
+                   H, W, TW, TH, pad, B, ldt, pstride, bstride);
     return cuda_status();
 }
 
@@ -885,8 +895,8 @@ Status launch_wg4_output(const float *yt, const float *bias, float *y, long long
     if (ldt < TW * TH) return ERR_SHAPE;
     if (pstride <= 0) pstride = OC * ldt;
     if (bstride <= 0) bstride = 36 * pstride;
-    pdl_launch(wg4_output_kernel, grid3((long long)TW * TH, OC, B), 256, 0, st, 
-        yt, bias, y, ybs, res, rbs, res_mode, OC, OH, OW, TW, TH, act, B, ldt, pstride, bstride);
+    pdl_launch(wg4_output_kernel, grid3((long long)TW * TH, OC, B), 256, 0, st, yt, bias, y, ybs,
+               res, rbs, res_mode, OC, OH, OW, TW, TH, act, B, ldt, pstride, bstride);
     return cuda_status();
 }
 
@@ -908,7 +918,8 @@ Status launch_kmajor_split(const float *src, float *hi, float *lo, int planes, i
                            long long pstride, int nc, cudaStream_t st) {
     if (planes <= 0 || IC <= 0 || nc <= 0 || ld < nc) return ERR_SHAPE;
     const long long n = (long long)planes * IC * nc;
-    pdl_launch(kmajor_split_kernel, blocks(n), 256, 0, st, src, hi, lo, planes, IC, ld, pstride, nc);
+    pdl_launch(kmajor_split_kernel, blocks(n), 256, 0, st, src, hi, lo, planes, IC, ld, pstride,
+               nc);
     return cuda_status();
 }
 
@@ -957,8 +968,8 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
         if (!smem_attr_once((const void *)dwconv_plane_kernel<KK, SS, AA>,                    \
                             (int)kDwPlaneSmemMax))                                       \
             return ERR_CUDA;                                                                 \
-        pdl_launch(dwconv_plane_kernel<KK, SS, AA>, g, nthr, sm, st,                                     \
-            x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, ld, HPp, GX, GY, pairs, even);        \
+        pdl_launch(dwconv_plane_kernel<KK, SS, AA>, g, nthr, sm, st, x, xbs, w, bias, y, ybs,\
+                   H, W, OH, OW, P, act, ld, HPp, GX, GY, pairs, even);                      \
     } while (0)
 #define PPDL_DW_PLANE_ACT(KK, SS)                                                                 \
     do {                                                                                         \
@@ -1008,8 +1019,8 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
     do {                                                                                         \
         if (!smem_attr_once((const void *)dwconv_band_kernel<KK, SS>, (int)kDwBandSmem))     \
             return ERR_CUDA;                                                                 \
-        pdl_launch(dwconv_band_kernel<KK, SS>, (unsigned)nblk, nthr, smem, st,                           \
-            x, xbs, w, bias, y, ybs, C, H, W, OH, OW, P, act, bld, bcols, BR, nbands);             \
+        pdl_launch(dwconv_band_kernel<KK, SS>, (unsigned)nblk, nthr, smem, st, x, xbs, w,    \
+                   bias, y, ybs, C, H, W, OH, OW, P, act, bld, bcols, BR, nbands);           \
     } while (0)
         if (K == 3 && S == 1)
             PPDL_DW_BAND(3, 1);
@@ -1027,13 +1038,17 @@ Status launch_dwconv(const float *x, long long xbs, const float *w, const float 
     const int tiles_x = (OW + kDwTW - 1) / kDwTW, tiles_y = (OH + kDwTH - 1) / kDwTH;
     const dim3 g(tiles_x * tiles_y, C, B);
     if (K == 3 && S == 1)
-        pdl_launch(dwconv_kernel<3, 1>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
+        pdl_launch(dwconv_kernel<3, 1>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P,
+                   act, tiles_x);
     else if (K == 3 && S == 2)
-        pdl_launch(dwconv_kernel<3, 2>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
+        pdl_launch(dwconv_kernel<3, 2>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P,
+                   act, tiles_x);
     else if (K == 5 && S == 1)
-        pdl_launch(dwconv_kernel<5, 1>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
+        pdl_launch(dwconv_kernel<5, 1>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P,
+                   act, tiles_x);
     else if (K == 5 && S == 2)
-        pdl_launch(dwconv_kernel<5, 2>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P, act, tiles_x);
+        pdl_launch(dwconv_kernel<5, 2>, g, 256, 0, st, x, xbs, w, bias, y, ybs, H, W, OH, OW, P,
+                   act, tiles_x);
     else
         return ERR_UNSUPPORTED;
     return cuda_status();
@@ -1067,8 +1082,8 @@ Status launch_conv_direct(const float *x, long long xbs, const float *w, const f
     do {                                                                                         \
         if (!smem_attr_once((const void *)conv_direct_kernel<KK, SS>, 64 * 1024))            \
             return ERR_CUDA;                                                                 \
-        pdl_launch(conv_direct_kernel<KK, SS>, g, 256, smem, st, x, xbs, w, bias, y, ybs, IC, H, W, OC,  \
-                                                        OH, OW, P, act, tiles_x, ICB);           \
+        pdl_launch(conv_direct_kernel<KK, SS>, g, 256, smem, st, x, xbs, w, bias, y, ybs,    \
+                   IC, H, W, OC, OH, OW, P, act, tiles_x, ICB);                              \
     } while (0)
     if (K == 2 && S == 1)
         PPDL_DIRECT(2, 1);
@@ -1087,8 +1102,8 @@ Status launch_maxpool2_pad(const float *x, long long xbs, float *y, long long yb
     if (!grid3_ok((long long)H * W, C, B) || W % 4 || ((uintptr_t)x & 15) || xbs % 4 ||
         ((uintptr_t)y & 15) || ybs % 4)
         return ERR_SHAPE;
-    pdl_launch(maxpool2_pad_kernel, grid3((long long)H * W / 4, C, B), 256, 0, st, x, xbs, y, ybs, C, H, W,
-                                                                           B);
+    pdl_launch(maxpool2_pad_kernel, grid3((long long)H * W / 4, C, B), 256, 0, st, x, xbs, y, ybs,
+               C, H, W, B);
     return cuda_status();
 }
 
@@ -1098,12 +1113,20 @@ Status launch_interp(const float *x, long long xbs, float *y, long long ybs, con
     if (!grid3_ok((long long)OH * OW, C, B)) return ERR_SHAPE;
     const bool vec = OW % 4 == 0 && ((uintptr_t)y & 15) == 0 && ybs % 4 == 0 &&
                      (!base || (((uintptr_t)base & 15) == 0 && bbs % 4 == 0));
+    // 1 / sf when the kernel's sf = out / in is a power of two (the forward's
+    // 2x upsamples), so that it multiplies instead of dividing
+    auto exact_recip = [](int out, int in) -> float {
+        const float sf = (float)out / (float)in;
+        int e = 0;
+        return std::frexp(sf, &e) == 0.5f ? 1.0f / sf : 0.0f;
+    };
+    const float rx = exact_recip(OW, W), ry = exact_recip(OH, H);
     if (vec)
-        pdl_launch(interp_kernel<4>, grid3((long long)OH * OW / 4, C, B), 256, 0, st, 
-            x, xbs, y, ybs, base, bbs, C, H, W, OH, OW, bilinear ? 1 : 0, B);
+        pdl_launch(interp_kernel<4>, grid3((long long)OH * OW / 4, C, B), 256, 0, st, x, xbs, y,
+                   ybs, base, bbs, C, H, W, OH, OW, bilinear ? 1 : 0, B, rx, ry);
     else
-        pdl_launch(interp_kernel<1>, grid3((long long)OH * OW, C, B), 256, 0, st, 
-            x, xbs, y, ybs, base, bbs, C, H, W, OH, OW, bilinear ? 1 : 0, B);
+        pdl_launch(interp_kernel<1>, grid3((long long)OH * OW, C, B), 256, 0, st, x, xbs, y, ybs,
+                   base, bbs, C, H, W, OH, OW, bilinear ? 1 : 0, B, rx, ry);
     return cuda_status();
 }
 

@@ -447,9 +447,9 @@ Status launch_row_scale(const float *x, const float *v, float *y, long long rows
     const long long n = (long long)B * rows_per_page * D;
     if (D % 4 || n / 4 >= (1LL << 31) || ((uintptr_t)x & 15) || ((uintptr_t)y & 15))
         return ERR_SHAPE;
-    pdl_launch(row_scale_kernel, blocks(n / 4), 256, 0, st, 
-        reinterpret_cast<const float4 *>(x), v, reinterpret_cast<float4 *>(y),
-        (unsigned)rows_per_page, (unsigned)(D / 4), (unsigned)(n / 4));
+    pdl_launch(row_scale_kernel, blocks(n / 4), 256, 0, st, reinterpret_cast<const float4 *>(x), v,
+               reinterpret_cast<float4 *>(y), (unsigned)rows_per_page, (unsigned)(D / 4),
+               (unsigned)(n / 4));
     return cuda_status();
 }
 
@@ -475,7 +475,7 @@ Status launch_postprocess(const float *logits, const float *boxes, const float *
     }
     if (mask_bits && mask_bits_q) {
         pdl_launch(pp_gather_bits_kernel, dim3(1, kNQ, (unsigned)B), 128, 0, st, mask_bits_q, sel,
-                                                                          mask_bits);
+                   mask_bits);
     } else if (mask_bits && mask_logits) {
         // 1250 words per row: blocks of 8 warps x 8 words
         dim3 grid((unsigned)cdiv(kMaskWords, 8 * kBitsWordsPerWarp), kNQ, (unsigned)B);

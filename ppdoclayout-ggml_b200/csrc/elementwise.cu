@@ -75,8 +75,8 @@ Status launch_bias_act(const float *x, const float *bias, float *y, long long n,
     if (((uintptr_t)x | (uintptr_t)y) % 16 == 0 && plane % 4 == 0) {
         const long long n4 = n / 4;
         const int grid = (int)(cdiv(n4, 256) < grid_cap ? cdiv(n4, 256) : grid_cap);
-        pdl_launch(bias_act_kernel_v4, grid, 256, 0, stream, (const float4 *)x, bias, (float4 *)y, n4,
-                                                     plane / 4, C, act);
+        pdl_launch(bias_act_kernel_v4, grid, 256, 0, stream, (const float4 *)x, bias, (float4 *)y,
+                   n4, plane / 4, C, act);
     } else {
         const int grid = (int)(cdiv(n, 256) < grid_cap ? cdiv(n, 256) : grid_cap);
         pdl_launch(bias_act_kernel, grid, 256, 0, stream, x, bias, y, n, plane, C, act);

@@ -173,8 +173,10 @@ Status dispatch(const GemmArgs &g, cudaStream_t stream) {
     const bool bn = g.B.s1 == 1;  // n contiguous
     dim3 grid((unsigned)cdiv(g.N, BN), (unsigned)cdiv(g.M, BM), (unsigned)g.batch);
     if (g.conv.K > 0) {
-        if (ak) pdl_launch(gemm_simt_kernel<BM, BN, BK, true, true, true>, grid, kThreads, 0, stream, g);
-        else pdl_launch(gemm_simt_kernel<BM, BN, BK, false, true, true>, grid, kThreads, 0, stream, g);
+        if (ak) pdl_launch(gemm_simt_kernel<BM, BN, BK, true, true, true>, grid, kThreads, 0,
+                           stream, g);
+        else pdl_launch(gemm_simt_kernel<BM, BN, BK, false, true, true>, grid, kThreads, 0, stream,
+                        g);
     } else if (ak && bn) {
         pdl_launch(gemm_simt_kernel<BM, BN, BK, true, true, false>, grid, kThreads, 0, stream, g);
     } else if (ak) {

@@ -1463,8 +1463,8 @@ Status launch_tf32_split_box(const float *w, float *hi, float *lo, int OC, int I
     tc_conv_box_blocks(IC, KS, &CB, &kbpb, &nbx);
     const int Kb = nbx * kbpb * 32;
     const long long n = (long long)OC * Kb;
-    pdl_launch(tf32_split_box_kernel, (int)((n + 255) / 256), 256, 0, st, w, hi, lo, OC, IC, KS, CB, kbpb,
-                                                                  Kb);
+    pdl_launch(tf32_split_box_kernel, (int)((n + 255) / 256), 256, 0, st, w, hi, lo, OC, IC, KS, CB,
+               kbpb, Kb);
     return cuda_status();
 }
 
@@ -1902,7 +1902,7 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     if (g.kps) {
         if (g.gather || g.box || g.rows || g.bits || g.batch < 1) return ERR_SHAPE;
         pdl_launch(tc_gemm_kernel<ACT_NONE, kModeTile>, grid, kThreads, g.smem, st, g.tmA, g.tmBhi,
-                                                                           g.tmBlo, g.tmC, a);
+                   g.tmBlo, g.tmC, a);
         const Status s0 = cuda_status();
         if (s0 != OK) return s0;
         const long long n_all = (long long)g.M * g.N;
@@ -1914,7 +1914,7 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     if (g.bits) {
         // packed output: tile A, no epilogue ops (checked by the planner)
         pdl_launch(tc_gemm_kernel<ACT_NONE, kModeBits>, grid, kThreads, g.smem, st, g.tmA, g.tmBhi,
-                                                                           g.tmBlo, g.tmC, a);
+                   g.tmBlo, g.tmC, a);
         return cuda_status();
     }
     const int mode = g.box ? kModeBox : (g.rows ? kModeRows : kModeTile);

@@ -172,11 +172,11 @@ Status launch_msda(const float *val, const float *p1, const float *p2, const flo
     const int npairs = batch * nq * kNH;
     const int grid = cdiv(npairs, kPairs);
     if (canon)
-        pdl_launch(msda_kernel<true>, grid, kThreads, 0, stream, val, p1, p2, ref, out, nq, npairs, ld1,
-                                                         ld2, ldv);
+        pdl_launch(msda_kernel<true>, grid, kThreads, 0, stream, val, p1, p2, ref, out, nq, npairs,
+                   ld1, ld2, ldv);
     else
-        pdl_launch(msda_kernel<false>, grid, kThreads, 0, stream, val, p1, p2, ref, out, nq, npairs, ld1,
-                                                          ld2, ldv);
+        pdl_launch(msda_kernel<false>, grid, kThreads, 0, stream, val, p1, p2, ref, out, nq, npairs,
+                   ld1, ld2, ldv);
     return cuda_status();
 }
 
