@@ -17,8 +17,11 @@ namespace ppdl {
 namespace {
 
 constexpr int kHeadDim = 32;  // head dim
-constexpr int kBQ = 32;       // queries per block
-constexpr int kThreads = 256;
+// queries per block: a warp per 4 queries.  Single-tile sequences take 40
+// (10 warps): the decoder's 300 queries x 8 heads x 8 pages are then 512
+// blocks, two waves of two blocks per SM, where 32 made 640 (a third wave
+// one-sixth full); the streamed form keeps 32 (two blocks per SM fit).
+constexpr int kBQAll = 40, kBQStream = 32;
 constexpr int kLD = 36;       // row stride of the Q and K/V tiles
 // Key tiles: sequences of up to kKTAll keys (the decoder's 300 queries) keep
 // all keys in one tile, so K and then V each arrive with one wait (V's
@@ -58,12 +61,13 @@ __device__ __forceinline__ float warp_sum32(float v) {
 // warp on distinct banks.  K and V tiles arrive by cp.async: with two buffers
 // the next tile lands while the current one is used; with one (all keys in
 // one tile) V lands while the softmax runs.
-template <int kKT, int kBufs>
-__global__ void __launch_bounds__(kThreads, 2)
+template <int kKT, int kBufs, int kBQ>
+__global__ void __launch_bounds__(kBQ / 4 * 32, 2)
 attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
             float *__restrict__ o, int T, int ldqk, long long bsqk, int ldvo, long long bsvo,
             float scale, int ldS) {
     pdl_begin();
+    constexpr int kThreads = kBQ / 4 * 32;
     static_assert(kKT % 64 == 0, "the score loop walks 64-key slices of a tile");
     extern __shared__ float sm[];
     float *Qs = sm;                      // [kBQ][kLD]
@@ -198,7 +202,8 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ k, const floa
 int attention_lds(int T) { return (T + 3) / 4 * 4; }
 size_t attention_smem_bytes(int T) {
     const size_t tiles = T <= kKTAll ? (size_t)kKTAll : 2 * 64;
-    return sizeof(float) * ((size_t)kBQ * kLD + tiles * kLD + (size_t)kBQ * attention_lds(T));
+    const size_t bq = T <= kKTAll ? kBQAll : kBQStream;
+    return sizeof(float) * (bq * kLD + tiles * kLD + bq * attention_lds(T));
 }
 
 }  // namespace
@@ -214,17 +219,17 @@ Status launch_attention(const float *q, const float *k, const float *v, float *o
         return ERR_SHAPE;
     const size_t smem = attention_smem_bytes(T);
     if (smem > 227 * 1024) return ERR_SHAPE;
-    if (!smem_attr_once((const void *)attn_kernel<kKTAll, 1>, 227 * 1024) ||
-        !smem_attr_once((const void *)attn_kernel<64, 2>, 227 * 1024))
+    if (!smem_attr_once((const void *)attn_kernel<kKTAll, 1, kBQAll>, 227 * 1024) ||
+        !smem_attr_once((const void *)attn_kernel<64, 2, kBQStream>, 227 * 1024))
         return ERR_CUDA;
     const int ldS = attention_lds(T);
-    const dim3 grid((T + kBQ - 1) / kBQ, heads, B);
     if (T <= kKTAll)
-        pdl_launch(attn_kernel<kKTAll, 1>, grid, kThreads, smem, st, q, k, v, o, T, ldqk, bsqk,
-                   ldvo, bsvo, scale, ldS);
+        pdl_launch(attn_kernel<kKTAll, 1, kBQAll>, dim3((T + kBQAll - 1) / kBQAll, heads, B),
+                   kBQAll / 4 * 32, smem, st, q, k, v, o, T, ldqk, bsqk, ldvo, bsvo, scale, ldS);
     else
-        pdl_launch(attn_kernel<64, 2>, grid, kThreads, smem, st, q, k, v, o, T, ldqk, bsqk, ldvo,
-                   bsvo, scale, ldS);
+        pdl_launch(attn_kernel<64, 2, kBQStream>,
+                   dim3((T + kBQStream - 1) / kBQStream, heads, B), kBQStream / 4 * 32, smem, st,
+                   q, k, v, o, T, ldqk, bsqk, ldvo, bsvo, scale, ldS);
     return cuda_status();
 }
 
