@@ -98,6 +98,16 @@ constexpr int kStagingBytes = 8 * 2 * kBoxBytes;  // 32 KB
 constexpr int kCtrlBytes = 2048;                 // control block + 1024-alignment slack
 // box mode: input windows in flight (a ring of their own beside the stages)
 constexpr int kMaxBoxes = 4;
+// Alternate-tile epilogue (the ALT instantiations, for narrow tiles of one or
+// two k-blocks, many per CTA): each epilogue warpgroup owns kSlots partial
+// slots of kAltSlotCols columns (warpgroup g's slot s at TMEM column
+// (g kSlots + s) kAltSlotCols, below the A stages) and the barriers that go
+// with them.
+constexpr int kAltSlotCols = 64;
+static_assert(2 * kSlots * kAltSlotCols <= kACol0, "alternate slots overlap the A stages");
+static_assert(16 * kMaxStages + 8 * kAStages + 8 * kSlots + 8 + 16 * kMaxBoxes <= 256 &&
+                  16 * kMaxStages + 8 * kAStages + 32 * kSlots + 8 + 16 * kMaxBoxes <= 384,
+              "mbarriers overlap the control words");
 // rows mode: channel rows c and c + 4 of a CHW tensor lie 4 * plane floats
 // apart, a 16-byte multiple for any plane, so the tensor is viewed as
 // [pages][C / 4][4 * plane] and a k-block (32 channels) is four TMA boxes,
@@ -559,7 +569,7 @@ constexpr int kModeBox = 1;   // implicit conv from TMA windows of the input
 constexpr int kModeRows = 2;  // M-major A as 32 per-channel TMA rows
 constexpr int kModeBits = 3;  // A as kModeTile; output packed 1 bit per (m, n): total > 0
 
-template <int ACT, int AMODE>
+template <int ACT, int AMODE, bool ALT = false>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBhi,
                const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmC,
@@ -576,10 +586,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const uint32_t ctrl = raw;
     const uint32_t bar_full = ctrl, bar_empty = ctrl + 8 * kMaxStages,
                    bar_afull = ctrl + 16 * kMaxStages, bar_pempty = bar_afull + 8 * kAStages,
-                   bar_done = bar_pempty + 8 * kSlots,
-                   bar_bfull = bar_done + 8, bar_bempty = bar_bfull + 8 * kMaxBoxes;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem_raw + 256);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem_raw + 260);
+                   bar_done = bar_pempty + 8 * (ALT ? 2 * kSlots : kSlots),
+                   bar_bfull = bar_done + 8, bar_bempty = bar_bfull + 8 * kMaxBoxes,
+                   bar_pfull = bar_bempty + 8 * kMaxBoxes;  // ALT only
+    constexpr int kCtrlWord = ALT ? 384 : 256;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem_raw + kCtrlWord);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem_raw + kCtrlWord + 4);
     const uint32_t stage0 = (raw + 512 + 1023) & ~1023u;
     uint8_t *stage0_ptr = smem_raw + (stage0 - raw);
 
@@ -592,7 +604,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_init(bar_empty + 8 * s, 1);
         }
         for (int j = 0; j < kAStages; j++) mbar_init(bar_afull + 8 * j, kConvThreads);
-        for (int i = 0; i < kSlots; i++) mbar_init(bar_pempty + 8 * i, kEpiThreads);
+        if constexpr (ALT) {
+            // pempty[p]: slot p folded by its warpgroup (slots 0..2 by
+            // warpgroup 0, 3..5 by warpgroup 1); pfull[p]: its partial is
+            // complete
+            for (int i = 0; i < 2 * kSlots; i++) {
+                mbar_init(bar_pempty + 8 * i, kEpiThreads / 2);
+                mbar_init(bar_pfull + 8 * i, 1);
+            }
+        } else {
+            for (int i = 0; i < kSlots; i++) mbar_init(bar_pempty + 8 * i, kEpiThreads);
+        }
         mbar_init(bar_done, kMmaWarps);
         // box mode: bfull[b] window b landed (producer arrive + tx),
         // bempty[b] window b read by all 128 converter threads
@@ -792,22 +814,28 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 // this thread issues the k-blocks it with it % kMmaWarps == q
                 const int q = warp - kWarpMma;
                 int it = 0;
-                Ring rs(S), rp(kSlots), ra(kAStages);
+                // rp: slot ring (ALT: of warpgroup 0's tiles; rq of
+                // warpgroup 1's, which owns the CTA's odd tiles)
+                Ring rs(S), rp(kSlots), rq(kSlots), ra(kAStages);
                 bool ok = true;
                 for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
                     const int nkb = pkps ? kb_count(t / (pmt * pnt)) : kblocks;
+                    const bool own1 = ALT && (((t - (int)blockIdx.x) / (int)gridDim.x) & 1);
                     for (int kb = 0; kb < nkb;
-                         kb++, it++, rs.next(), rp.next(), ra.next()) {
+                         kb++, it++, rs.next(), (own1 ? rq : rp).next(), ra.next()) {
                         if (it % kMmaWarps != q) continue;
+                        const Ring &sr = own1 ? rq : rp;
+                        const int sp = own1 ? kSlots + sr.i : sr.i;
                         // the A stage is written only after the stage's TMA landed,
                         // so afull also covers the B operand
-                        if (!mbar_wait(bar_pempty + 8 * rp.i, rp.ph ^ 1, abort_flag) ||
+                        if (!mbar_wait(bar_pempty + 8 * sp, sr.ph ^ 1, abort_flag) ||
                             !mbar_wait(bar_afull + 8 * ra.i, ra.ph, abort_flag)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t d = tmem_base + (uint32_t)(rp.i * kSlotCols);
+                        const uint32_t d =
+                            tmem_base + (uint32_t)(sp * (ALT ? kAltSlotCols : kSlotCols));
                         const uint32_t ahi = tmem_base + (uint32_t)(kACol0 + ra.i * kACols);
                         const uint32_t alo = ahi + kBK;
                         const uint32_t bhi = stage0 + rs.i * pstage + pstage - 2u * 128u * pbn;
@@ -825,6 +853,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         for (int kk = 0; kk < kBK / 8; kk++)
                             umma_tf32_ts(d, ahi + 8 * kk, dbh + 2 * kk, pidesc, 1u);
                         umma_commit(bar_empty + 8 * rs.i);
+                        if constexpr (ALT) umma_commit(bar_pfull + 8 * sp);
                     }
                 }
                 // all issued MMAs must finish before TMEM is released (both
@@ -988,10 +1017,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                   pnt = a.n_tiles, ptma = a.tma_c;
         const int quad = warp & 3;
         // the two warpgroups split the N tile in 16-column units: [0, half)
-        // and [half, bn), half <= kHalfCols (a narrow tile keeps both busy)
+        // and [half, bn), half <= kHalfCols (a narrow tile keeps both busy).
+        // ALT (N tiles of at most kHalfCols columns, one or two k-blocks,
+        // several tiles per CTA, where the epilogue's per-tile instructions
+        // bound the pipeline): each warpgroup instead takes every other tile
+        // whole, so that a tile's folds and stores have two tile periods;
+        // its slots and barriers are its own, so every waiter sees every
+        // phase of its barriers in order, as in the shared form.
+        const bool wg = warp >= kWarpEpi2;
         const int half = ((pbn + 31) / 32) * 16;
-        const int c_lo = warp >= kWarpEpi2 ? half : 0;
-        const int c_hi = warp >= kWarpEpi2 ? pbn : half;
+        const int c_lo = (wg && !ALT) ? half : 0;
+        const int c_hi = (wg || ALT) ? pbn : half;
         const int ew = warp < 4 ? warp : warp - 4;  // epilogue warp 0..7
         // ReLU / SiLU / identity outputs apply alpha, bias and a mode-1
         // residual in registers before the box (measured faster); the GELU
@@ -1010,6 +1046,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         bool ok = true;
         for (int t = blockIdx.x; t < ptiles && ok; t += gridDim.x) {
             const int z = t / (pmt * pnt);
+            if constexpr (ALT) {
+                if ((((t - (int)blockIdx.x) / (int)gridDim.x) & 1) != (int)wg)
+                    continue;  // the other warpgroup's tile
+            }
             const int r = t - z * pmt * pnt;
             const int mt = r / pnt;
             const int m0 = mt * kBM, n0 = (r - mt * pnt) * pbn;
@@ -1032,13 +1072,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             };
             const int nkb = kb_count(z);
             for (int c = 0; c < nkb; c++, ctr++, rp.next(), re.next()) {
-                const int p = rp.i;
-                if (!mbar_wait(bar_empty + 8 * re.i, re.ph, abort_flag)) {
+                const int p = (ALT && wg) ? kSlots + rp.i : rp.i;
+                if (!(ALT ? mbar_wait(bar_pfull + 8 * p, rp.ph, abort_flag)
+                          : mbar_wait(bar_empty + 8 * re.i, re.ph, abort_flag))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t part = tmem_base + lane_base + (uint32_t)(p * kSlotCols + c_lo);
+                const uint32_t part = tmem_base + lane_base +
+                                      (uint32_t)(p * (ALT ? kAltSlotCols : kSlotCols) + c_lo);
 #pragma unroll
                 for (int q = 0; q < kHalfCols / 32; q++) {
                     if (c_lo + q * 32 < c_hi) {
@@ -1831,7 +1873,8 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     {
         std::lock_guard<std::mutex> lk(mu);
         if (!attr[dev]) {
-            const void *fns[13] = {
+            const void *fns[14] = {
+                (const void *)tc_gemm_kernel<0, kModeTile, true>,
                 (const void *)tc_gemm_kernel<0, kModeBits>,
                 (const void *)tc_gemm_kernel<0, kModeTile>, (const void *)tc_gemm_kernel<1, kModeTile>,
                 (const void *)tc_gemm_kernel<2, kModeTile>, (const void *)tc_gemm_kernel<3, kModeTile>,
@@ -1918,6 +1961,15 @@ Status launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
         return cuda_status();
     }
     const int mode = g.box ? kModeBox : (g.rows ? kModeRows : kModeTile);
+    // alternate-tile epilogue: tile-mode identity outputs in N tiles of at
+    // most kHalfCols columns and at most two k-blocks, at least four tiles per
+    // CTA (the forward's stage-0 Winograd GEMMs, 48 -> 48 channels)
+    if (mode == kModeTile && g.epi.act == ACT_NONE && g.bn <= kHalfCols &&
+        (g.K + kBK - 1) / kBK <= 2 && a.tiles >= 4 * grid) {
+        pdl_launch(tc_gemm_kernel<ACT_NONE, kModeTile, true>, grid, kThreads, g.smem, st, g.tmA,
+                   g.tmBhi, g.tmBlo, g.tmC, a);
+        return cuda_status();
+    }
     switch (mode * 4 + g.epi.act) {
 #define PPDL_TC_CASE(M_, A_)                                                                  \
     case M_ * 4 + A_:                                                                      \

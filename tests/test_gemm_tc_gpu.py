@@ -101,6 +101,23 @@ def test_tc_gemm_large(cuda, M, N, K, batch, a_m_major):
     assert err < RTOL, err
 
 
+# Narrow identity GEMMs of one or two k-blocks with at least four tiles per
+# CTA run the alternate-tile epilogue (each epilogue warpgroup takes every
+# other tile whole, with TMEM slots and barriers of its own): odd tile counts
+# per CTA, M, N and K tails, both A layouts.
+@pytest.mark.parametrize("M,N,K,batch,a_m_major", [
+    (20000, 48, 48, 6, 1),     # the stage-0 Winograd plane GEMM shape, 942 tiles
+    (19999, 40, 20, 5, 1),     # one k-block, N tail (40 of a 48-column tile), M tail
+    (80000, 64, 64, 1, 0),     # K-major A, 64-column tiles, 625 tiles
+    (30001, 32, 36, 3, 1),     # K tail: 36 = 32 + 4
+])
+def test_tc_gemm_alternate_tiles(cuda, M, N, K, batch, a_m_major):
+    got, ref = _gemm(cuda, M, N, K, batch, a_m_major, seed=M + 5 * N + K)
+    assert np.isfinite(got).all()
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err < RTOL, err
+
+
 def test_tc_gemm_rejects_unaligned_strides(cuda):
     L = _lib()
     A = torch.zeros(625 * 64, device=cuda)
