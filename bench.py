@@ -387,7 +387,7 @@ SIMT_KINDS = ("attention", "conv_direct")
 # DRAM traffic of the tensor-core GEMM per page of one forward (sum over its
 # launches of dram__bytes_read.sum + dram__bytes_write.sum), from an ncu
 # capture of one eager forward at 2 pages; None until measured.
-TC_GEMM_DRAM_BYTES_PER_PAGE = 1.2486e9  # 2.497 GB over the 166 launches of 2 pages
+TC_GEMM_DRAM_BYTES_PER_PAGE = 1.2477e9  # 2.495 GB over the 166 launches of 2 pages
 
 
 def _fwd_pages(rank, B):
