@@ -147,6 +147,31 @@ def test_batch8_bench_pages_graph_replay(cuda, gguf_path, ref_model):
     assert total >= 120, total
 
 
+def test_batch32_stress_pages_match_batch8(cuda, gguf_path):
+    """Config 4's batch size: a context of capacity 32 (as bench.py's stress
+    workload) takes 32 pages through the pipelined API, and every page's dets
+    and packed masks equal those of the same page in a capacity-8 context
+    (the size the oracle gates above hold), so the parity carries over to the
+    stress configuration.  The results match bit for bit: the GEMMs' tiles
+    cut across pages' rows, never through a dot product, and no reduction
+    order depends on the batch."""
+    import torch
+    imgs = np.stack([synth.synth_page(2000 + i) for i in range(32)])
+    hw = np.array([[800, 800] if i % 3 else [1000, 700] for i in range(32)], np.int32)
+    c32 = ppdl.Context(gguf_path, max_batch=32)
+    buf = torch.from_numpy(imgs).pin_memory().numpy()
+    r32 = [(d.copy(), b.copy()) for d, b in c32.wait(c32.submit(buf, hw), 32)]
+    c32.close()
+    c8 = ppdl.Context(gguf_path, max_batch=8)
+    for b0 in range(0, 32, 8):
+        bb = torch.from_numpy(np.ascontiguousarray(imgs[b0:b0 + 8])).pin_memory().numpy()
+        r8 = c8.wait(c8.submit(bb, np.ascontiguousarray(hw[b0:b0 + 8])), 8)
+        for k in range(8):
+            np.testing.assert_array_equal(r32[b0 + k][0], r8[k][0])
+            np.testing.assert_array_equal(r32[b0 + k][1], r8[k][1])
+    c8.close()
+
+
 def test_pipelined_batches_with_packed_masks(cuda, gguf_path, pages, gpu_out):
     """ppdl_submit_batch / ppdl_wait_batch: three batches in a row from
     pinned host memory, two in flight; every result equals ppdl_infer_batch's
